@@ -1,0 +1,409 @@
+"""MoE-layer benchmark (BASELINE.json metric: MoE-layer tokens/s, % of HBM roofline).
+
+Default workload (N=1): BASELINE config 1 -- GLM-4.7-shape MoE layer (H 5120, 160
+routed experts, top-8, I 1536, 1 shared expert of 1536), bf16-valued weights
+~N(0,0.02) (stored as f16, lossless), reference softmax-biased routing with
+routed_scaling_factor 2.5, decode batches of 1, 8 and 64 tokens; the headline
+line is the 64-token batch, T=1 and T=8 are reported under "sub".
+
+One step = one MoE-layer forward over one batch already resident in HBM.
+Timing: W warm-up steps, then exactly K steps between CUDA events on the
+launching stream, barrier + synchronize on both sides, max over ranks.  The
+touched expert weights (>= 425 MB at T=1) are larger than the 126 MB L2, so no
+flush is needed between steps.
+
+e2e: the same metric through MoeLayer.forward_host (the call behind the
+executor's ``_moe_mlp_block``) with host fp32 activations: pinned H2D of x and
+D2H of the output inside the timed region.
+
+--impl reference: the CPU oracle port of the reference executor
+(offload_runtime/executors/glm4_moe.py:176-240; same numpy expressions) on the
+box's host cores, all BLAS threads, same config, metric and unit.
+
+N > 1 (torchrun): expert-parallel sharding is not wired into this bench yet, so
+each rank runs an independent replica of the layer on its own tokens
+("parallelism": "replicas", weak scaling, no collective in the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "disk-mem-off_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+
+GLM = dict(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536)
+
+
+def _peaks() -> tuple[float, str]:
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Polls NVML (read-only) while the timed region runs."""
+
+    def __init__(self, device_index: int) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._nv = None
+
+    def _run(self) -> None:
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self) -> "ClockSampler":
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a: object) -> None:
+        self._stop.set()
+        if self._ok:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        nv = self._nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = set()
+        for _mhz, r in self.samples:
+            for k, bit in names.items():
+                if r & bit:
+                    seen.add(k)
+        mhz = [m for m, _ in self.samples]
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(mhz)}
+
+
+# ------------------------------------------------------------------ distributed
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def _max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_sample(blob, meta, x_np: np.ndarray, budget_s: float = 20.0) -> dict:
+    """Time the oracle port of the reference executor on the host cores."""
+    from moe_sm100.synthetic import LazyHostTensors
+    from oracle.moe_oracle import OracleConfig, moe_block
+    cfg = OracleConfig(hidden=GLM["hidden"], n_experts=GLM["n_experts"], top_k=GLM["top_k"],
+                       inter=GLM["inter"], shared_inter=GLM["shared_inter"],
+                       routed_scaling_factor=2.5, eps=1e-5)
+    lazy = LazyHostTensors(blob, meta)
+    moe_block(x_np, lazy, cfg)  # warm: fetches the touched experts once (fp32)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        moe_block(x_np, lazy, cfg)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or len(times) >= 10:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    med = float(np.median(times))
+    return {"value": x_np.shape[0] / med, "unit": "tokens/s", "cores": threads,
+            "kind": "port", "seconds_per_step": med, "reps": len(times),
+            "sample": f"oracle port of GLM4MoeExecutor._moe_mlp_block (numpy fp32, "
+                      f"weights = the bf16 values as fp32), T={x_np.shape[0]} decode batch, "
+                      f"{len(times)} reps after 1 warm-up, median"}
+
+
+# ------------------------------------------------------------------ helpers
+def _algorithmic_bytes(ids: np.ndarray, T: int) -> dict:
+    H, I, SI, E = GLM["hidden"], GLM["inter"], GLM["shared_inter"], GLM["n_experts"]
+    U = len(np.unique(ids))
+    w_gateup = (U * 2 * I * H + 2 * SI * H) * 2
+    w_down = (U * H * I + H * SI) * 2
+    rows = T * GLM["top_k"]
+    act_gateup = (rows + T) * H * 2 + (rows * I + T * SI) * 2          # read x rows, write act
+    act_down = (rows * I + T * SI) * 2 + (rows + T) * H * 4             # read act, write y
+    layer = w_gateup + w_down + E * H * 4 + T * H * 8
+    return {"unique_experts": int(U), "gateup": w_gateup + act_gateup,
+            "down": w_down + act_down, "layer": layer}
+
+
+def _make_layer(device: int, seed: int, max_tokens: int):
+    import torch
+    from moe_sm100 import MoeLayer, MoeLayerConfig
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer
+    spec = SyntheticSpec(**GLM, family="glm", expert_dtype="bfloat16", seed=seed)
+    blob, meta = build_device_layer(spec, device=f"cuda:{device}")
+    cfg = MoeLayerConfig(**GLM, routed_scaling_factor=2.5, rms_norm_eps=1e-5,
+                         max_tokens=max_tokens, device=device)
+    ml = MoeLayer(cfg)
+    ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    return ml, blob, meta
+
+
+def _time_steps(fn, steps: int, warmup: int, world: int) -> float:
+    import torch
+    for _ in range(warmup):
+        fn()
+    _barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    return _max_over_ranks(s.elapsed_time(e) / steps, world)
+
+
+# ------------------------------------------------------------------ arms
+def run_ours(args) -> None:  # noqa: ANN001
+    import torch
+    world, rank, local = _dist_init()
+    torch.cuda.set_device(local)
+    hbm, peak_kind = _peaks()
+    T_main = args.tokens
+    ml, blob, meta = _make_layer(local, seed=1234, max_tokens=max(64, T_main))
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+
+    results = {}
+    for T in sorted({1, 8, T_main}):
+        x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
+        out = torch.empty_like(x)
+        ws = ml.workspace(T)
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def step() -> None:
+            ml.forward_ptr(x.data_ptr(), out.data_ptr(), T, ws.data_ptr(), ws.numel(), stream)
+
+        if T == T_main:
+            with ClockSampler(local) as clk:
+                ms = _time_steps(step, args.steps, args.warmup, world)
+            clocks = clk.summary()
+        else:
+            ms = _time_steps(step, args.steps, args.warmup, world)
+        ml.status()
+        # per-stage device times (events between the launches of one forward)
+        stage = np.zeros(4)
+        for _ in range(args.steps):
+            stage += np.array(ml.forward_timed(x, out))
+        stage /= args.steps
+        ids = ml.route(x)["topk_ids"].cpu().numpy()
+        ab = _algorithmic_bytes(ids, T)
+        results[T] = dict(ms=ms, stage=stage.tolist(), bytes=ab, x=x)
+
+    main = results[T_main]
+    ms = main["ms"]
+    stage = main["stage"]
+    ab = main["bytes"]
+    gate_gbs = ab["gateup"] / (stage[1] * 1e-3) / 1e9
+    down_gbs = ab["down"] / (stage[2] * 1e-3) / 1e9
+    layer_gbs = ab["layer"] / (ms * 1e-3) / 1e9
+
+    # end-to-end through the host-buffer call
+    x_host = main["x"].cpu().numpy()
+    for _ in range(args.warmup):
+        ml.forward_host(x_host)
+    _barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ml.forward_host(x_host)
+    e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(blob, meta, x_host)
+
+    sub = {}
+    for T, r in results.items():
+        if T == T_main:
+            continue
+        b = r["bytes"]
+        sub[f"T{T}"] = {
+            "tokens_per_s": world * T / (r["ms"] * 1e-3), "ms_per_step": r["ms"],
+            "stage_ms": r["stage"], "unique_experts": b["unique_experts"],
+            "layer_hbm_frac": b["layer"] / (r["ms"] * 1e-3) / 1e9 / hbm,
+            "gateup_hbm_frac": b["gateup"] / (r["stage"][1] * 1e-3) / 1e9 / hbm,
+        }
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer tokens/s (GLM-4.7-shape decode) and % of HBM roofline",
+            "value": world * T_main / (ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 MMA / fp32 accumulate (bf16-valued weights); fp32 routing",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, random-init)",
+            "config": {"workload": "BASELINE config 1: GLM-4.7-shape MoE layer, bf16 decode",
+                       "tokens_per_rank": T_main, "hidden": 5120, "experts": 160, "top_k": 8,
+                       "moe_intermediate": 1536, "shared_intermediate": 1536,
+                       "routing": "reference softmax(logits+bias), scale 2.5",
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (touched weights >= 425 MB)"},
+            "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel gate/up (swap-AB tcgen05)",
+                         "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gate_gbs / hbm, "peak_source": peak_kind,
+                         "traffic": None,
+                         "algorithmic_bytes_per_launch": ab["gateup"],
+                         "launch_ms": stage[1]},
+            "roofline_down": {"achieved": down_gbs, "frac": down_gbs / hbm,
+                              "algorithmic_bytes_per_launch": ab["down"], "launch_ms": stage[2]},
+            "roofline_layer": {"achieved": layer_gbs, "frac": layer_gbs / hbm,
+                               "algorithmic_bytes_per_step": ab["layer"],
+                               "unique_experts": ab["unique_experts"]},
+            "stage_ms": {"route": stage[0], "gemm_gateup": stage[1], "gemm_down": stage[2],
+                         "combine": stage[3]},
+            "e2e": {"value": world * T_main / e2e_s, "unit": "tokens/s",
+                    "h2d_bytes_per_step": T_main * GLM["hidden"] * 4,
+                    "d2h_bytes_per_step": T_main * GLM["hidden"] * 4,
+                    "ms_per_step": e2e_s * 1e3},
+            "cpu_baseline": cpu,
+            "gpu_launches": 9 * args.steps,
+            "clocks": clocks,
+            "sub": sub,
+        }
+        print(json.dumps(line))
+    ml.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:  # noqa: ANN001
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    from moe_sm100.synthetic import LazyHostTensors, SyntheticSpec, build_device_layer
+    from oracle.moe_oracle import OracleConfig, moe_block
+    spec = SyntheticSpec(**GLM, family="glm", expert_dtype="bfloat16", seed=1234)
+    blob, meta = build_device_layer(spec, device=f"cuda:{local}")
+    T = args.tokens
+    x = torch.randn((T, GLM["hidden"]), generator=torch.Generator(device="cuda").manual_seed(1000),
+                    device="cuda").cpu().numpy()
+    cfg = OracleConfig(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536,
+                       routed_scaling_factor=2.5, eps=1e-5)
+    lazy = LazyHostTensors(blob, meta)
+    moe_block(x, lazy, cfg)  # fetch touched experts to host once (not timed)
+    for _ in range(max(0, args.warmup - 1)):
+        moe_block(x, lazy, cfg)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        moe_block(x, lazy, cfg)
+    sec = (time.perf_counter() - t0) / args.steps
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    value = T / sec
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "MoE-layer tokens/s (GLM-4.7-shape decode) and % of HBM roofline",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
+        "data": "synthetic (same seeds as the GPU arm)",
+        "config": {"workload": "BASELINE config 1: GLM-4.7-shape MoE layer, bf16 decode",
+                   "tokens_per_rank": T, "parallelism": "host cores, rank 0 only"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"oracle port of GLM4MoeExecutor._moe_mlp_block, T={T}, "
+                                   f"{args.steps} steps after {args.warmup} warm-up"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

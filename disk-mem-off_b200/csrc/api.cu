@@ -1,0 +1,704 @@
+// C ABI of libmoe_sm100 (declarations and reference citations: include/moe_sm100.h).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+static int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+static int cuda_fail(cudaError_t st, const char* what) {
+  return fail(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(st));
+}
+
+#define MOE_CUDA(call)                                  \
+  do {                                                  \
+    cudaError_t st_ = (call);                           \
+    if (st_ != cudaSuccess) return cuda_fail(st_, #call); \
+  } while (0)
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// ------------------------------------------------------------ tensor maps
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool int8, uint64_t inner, uint64_t rows,
+                  uint32_t box_inner, uint32_t box_rows, bool swizzle128, std::string* err) {
+  auto fn = get_encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled unavailable from the driver";
+    return false;
+  }
+  if (rows == 0) rows = 1;  // empty operand: never read, but the map must encode
+  const uint64_t esize = int8 ? 1 : 2;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * esize};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d): inner=%llu rows=%llu", (int)r,
+             (unsigned long long)inner, (unsigned long long)rows);
+    *err = buf;
+    return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------ workspace
+static int pick_bn(int T) {
+  if (T <= 16) return 16;
+  if (T <= 32) return 32;
+  if (T <= 64) return 64;
+  if (T <= 128) return 128;
+  return 256;
+}
+
+WsLayout ws_layout(const Plan& p, int T) {
+  WsLayout L{};
+  const size_t R = static_cast<size_t>(T) * p.K;
+  const int E = p.E;
+  L.bn = pick_bn(T);
+  L.nchunks = (T + kPermChunk - 1) / kPermChunk;
+  const int mt1 = (2 * p.I + kBM - 1) / kBM;
+  const int mt2 = (p.H + kBM - 1) / kBM;
+  const int mt1s = p.SI > 0 ? (2 * p.SI + kBM - 1) / kBM : 0;
+  const int ntr = static_cast<int>((R + L.bn - 1) / L.bn) + static_cast<int>(R < (size_t)E ? R : E);
+  const int nts = p.SI > 0 ? (T + L.bn - 1) / L.bn : 0;
+  L.max_tiles1 = ntr * mt1 + nts * mt1s;
+  L.max_tiles2 = ntr * mt2 + nts * mt2;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.h32 = take(static_cast<size_t>(T) * p.H * 4);
+  L.h16 = take(static_cast<size_t>(T) * p.H * 2);
+  L.xg = take(R * p.H * 2);
+  L.act = take(R * p.I * 2);
+  L.act_s = take(static_cast<size_t>(T) * p.SI * 2);
+  L.y = take(R * p.H * 4);
+  L.y_s = take(p.SI > 0 ? static_cast<size_t>(T) * p.H * 4 : 0);
+  L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
+  L.ids = take(R * 4);
+  L.wts = take(R * 4);
+  L.sgate = take(static_cast<size_t>(T) * 4);
+  L.bm = take(static_cast<size_t>(L.nchunks) * E * 32 * 4);
+  L.hist = take(static_cast<size_t>(L.nchunks) * E * 4);
+  L.base = take(static_cast<size_t>(L.nchunks) * E * 4);
+  L.offsets = take(static_cast<size_t>(E + 1) * 4);
+  L.perm = take(R * 4);
+  L.slot_row = take(R * 4);
+  L.tiles1 = take(static_cast<size_t>(L.max_tiles1) * sizeof(Tile));
+  L.tiles2 = take(static_cast<size_t>(L.max_tiles2) * sizeof(Tile));
+  L.tile_count = take(16);
+  L.total = o;
+  return L;
+}
+
+// ------------------------------------------------------------ name parsing
+enum Kind { K_NONE, K_NORM, K_ROUTER, K_BIAS, K_SHARED_GATE, K_EXPERT, K_SHARED };
+enum Proj { P_GATE = 0, P_UP = 1, P_DOWN = 2 };
+
+struct Parsed {
+  Kind kind = K_NONE;
+  int expert = -1;
+  int proj = -1;
+  bool scale = false;
+};
+
+static bool starts_with(const std::string& s, const char* pre) {
+  return s.compare(0, strlen(pre), pre) == 0;
+}
+
+static bool parse_proj(const std::string& rest, Parsed* out) {
+  static const char* names[3] = {"gate_proj.weight", "up_proj.weight", "down_proj.weight"};
+  for (int i = 0; i < 3; ++i) {
+    const std::string n = names[i];
+    if (rest == n) {
+      out->proj = i;
+      return true;
+    }
+    if (rest == n + "_scale") {
+      out->proj = i;
+      out->scale = true;
+      return true;
+    }
+  }
+  return false;
+}
+
+static Parsed parse_name(const char* cname) {
+  Parsed p;
+  std::string n(cname ? cname : "");
+  const size_t pos_norm = n.find("post_attention_layernorm.weight");
+  if (pos_norm != std::string::npos && pos_norm + strlen("post_attention_layernorm.weight") == n.size()) {
+    p.kind = K_NORM;
+    return p;
+  }
+  const size_t pos = n.find("mlp.");
+  if (pos == std::string::npos) return p;
+  std::string s = n.substr(pos);
+  if (s == "mlp.gate.weight") p.kind = K_ROUTER;
+  else if (s == "mlp.gate.e_score_correction_bias") p.kind = K_BIAS;
+  else if (s == "mlp.shared_expert_gate.weight") p.kind = K_SHARED_GATE;
+  else if (starts_with(s, "mlp.shared_experts.") || starts_with(s, "mlp.shared_expert.")) {
+    const std::string rest = s.substr(s.find('.', 4) + 1);
+    if (parse_proj(rest, &p)) p.kind = K_SHARED;
+  } else if (starts_with(s, "mlp.experts.")) {
+    const std::string r = s.substr(strlen("mlp.experts."));
+    const size_t dot = r.find('.');
+    if (dot != std::string::npos && dot > 0) {
+      int e = 0;
+      bool ok = true;
+      for (size_t i = 0; i < dot; ++i) {
+        if (r[i] < '0' || r[i] > '9') ok = false;
+        else e = e * 10 + (r[i] - '0');
+      }
+      if (ok && parse_proj(r.substr(dot + 1), &p)) {
+        p.kind = K_EXPERT;
+        p.expert = e;
+      }
+    }
+  }
+  return p;
+}
+
+static int parse_dtype(const char* d) {
+  std::string s(d ? d : "");
+  if (s == "float32" || s == "<f4" || s == "f4") return SRC_F32;
+  if (s == "float16" || s == "<f2" || s == "f2") return SRC_F16;
+  if (s == "bfloat16" || s == "bf16") return SRC_BF16;
+  if (s == "int8" || s == "|i1" || s == "i1") return SRC_I8;
+  return -1;
+}
+
+static size_t dtype_size(int d) { return d == SRC_F32 ? 4 : (d == SRC_I8 ? 1 : 2); }
+
+}  // namespace moe
+
+// ====================================================================== C ABI
+using namespace moe;
+
+struct MoePlan {
+  Plan p;
+};
+
+extern "C" {
+
+const char* moe_last_error(void) { return g_last_error.c_str(); }
+const char* moe_version(void) { return "moe_sm100 0.1 (sm_100a, tcgen05)"; }
+
+int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan) {
+  if (!cfg || !out_plan) return fail(MOE_ERR_INVALID, "null argument");
+  const MoeConfig& c = *cfg;
+  if (c.hidden <= 0 || c.hidden % 16 != 0)
+    return fail(MOE_ERR_UNSUPPORTED, "hidden must be a positive multiple of 16");
+  if (c.inter <= 0 || c.inter % 16 != 0)
+    return fail(MOE_ERR_UNSUPPORTED, "moe_intermediate_size must be a positive multiple of 16");
+  if (c.shared_inter < 0 || c.shared_inter % 16 != 0)
+    return fail(MOE_ERR_UNSUPPORTED, "shared intermediate size must be a multiple of 16");
+  if (c.n_experts <= 0 || c.n_experts > 1024)
+    return fail(MOE_ERR_UNSUPPORTED, "n_experts must be in [1, 1024]");
+  if (c.top_k <= 0 || c.top_k > kMaxTopK || c.top_k > c.n_experts)
+    return fail(MOE_ERR_INVALID, "top_k must be in [1, min(32, n_experts)]");
+  if (c.score_func != MOE_SCORE_SOFTMAX && c.score_func != MOE_SCORE_SIGMOID)
+    return fail(MOE_ERR_INVALID, "unknown score_func");
+  if (c.weight_format != MOE_WEIGHTS_F16 && c.weight_format != MOE_WEIGHTS_INT8_PC)
+    return fail(MOE_ERR_INVALID, "unknown weight_format");
+  if (c.max_tokens <= 0) return fail(MOE_ERR_INVALID, "max_tokens must be positive");
+  if (c.has_shared_gate && c.shared_inter == 0)
+    return fail(MOE_ERR_INVALID, "shared gate requires a shared expert");
+  int eb = c.expert_begin, ee = c.expert_end;
+  if (eb == 0 && ee == 0) ee = c.n_experts;
+  if (eb < 0 || ee > c.n_experts || eb >= ee) return fail(MOE_ERR_INVALID, "bad expert range");
+  if (eb != 0 || ee != c.n_experts)
+    return fail(MOE_ERR_UNSUPPORTED, "expert ranges are served by the expert-parallel entry points");
+
+  MOE_CUDA(cudaSetDevice(c.device));
+  MoePlan* plan = new MoePlan();
+  Plan& p = plan->p;
+  p.cfg = c;
+  p.device = c.device;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device);
+  p.num_sms = sms > 0 ? sms : 148;
+  p.E = c.n_experts;
+  p.K = c.top_k;
+  p.H = c.hidden;
+  p.I = c.inter;
+  p.SI = c.shared_inter;
+  p.e_begin = eb;
+  p.e_end = ee;
+  p.n_local = ee - eb;
+  p.router_rows = p.E + (c.has_shared_gate ? 1 : 0);
+  p.int8 = c.weight_format == MOE_WEIGHTS_INT8_PC;
+  cudaError_t st = cudaMalloc(&p.d_err, sizeof(int));
+  if (st == cudaSuccess) st = cudaMemset(p.d_err, 0, sizeof(int));
+  if (st != cudaSuccess) {
+    delete plan;
+    return cuda_fail(st, "cudaMalloc(error word)");
+  }
+  *out_plan = plan;
+  return MOE_OK;
+}
+
+int moe_plan_destroy(MoePlan* plan) {
+  if (!plan) return MOE_OK;
+  cudaSetDevice(plan->p.device);
+  if (plan->p.weights_alloc) cudaFree(plan->p.weights_alloc);
+  if (plan->p.d_err) cudaFree(plan->p.d_err);
+  delete plan;
+  return MOE_OK;
+}
+
+uint64_t moe_plan_weight_bytes(const MoePlan* plan) { return plan ? plan->p.weights_bytes : 0; }
+
+int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
+                   const MoeTensorDesc* descs, int32_t n_descs, void* stream) {
+  if (!plan || !blob_dev || !descs || n_descs <= 0) return fail(MOE_ERR_INVALID, "null argument");
+  Plan& p = plan->p;
+  MOE_CUDA(cudaSetDevice(p.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int E = p.E, H = p.H, I = p.I, SI = p.SI, NL = p.n_local;
+
+  struct Src {
+    const char* ptr = nullptr;
+    int dtype = -1;
+  };
+  Src norm, router, bias, sgate;
+  std::vector<Src> ex(static_cast<size_t>(NL) * 3), exs(static_cast<size_t>(NL) * 3);
+  Src sh[3], shs[3];
+  const char* base = static_cast<const char*>(blob_dev);
+
+  for (int i = 0; i < n_descs; ++i) {
+    const MoeTensorDesc& d = descs[i];
+    const Parsed pn = parse_name(d.name);
+    if (pn.kind == K_NONE) continue;
+    const int dt = parse_dtype(d.dtype);
+    if (dt < 0) return fail(MOE_ERR_UNSUPPORTED, std::string("unsupported dtype for ") + d.name);
+    if (d.offset < 0 || d.nbytes < 0 || static_cast<uint64_t>(d.offset + d.nbytes) > blob_bytes)
+      return fail(MOE_ERR_INVALID, std::string("tensor outside the blob: ") + d.name);
+    int64_t numel = 1;
+    for (int k = 0; k < d.ndim && k < 2; ++k) numel *= d.shape[k];
+    if (d.ndim < 1 || d.ndim > 2 || numel * static_cast<int64_t>(dtype_size(dt)) != d.nbytes)
+      return fail(MOE_ERR_INVALID, std::string("shape / nbytes mismatch for ") + d.name);
+    const int64_t r0 = d.shape[0], c0 = d.ndim == 2 ? d.shape[1] : 1;
+    auto need = [&](int64_t rows, int64_t cols) {
+      return (d.ndim == 2 && r0 == rows && c0 == cols) || (d.ndim == 1 && cols == 1 && r0 == rows);
+    };
+    Src src{base + d.offset, dt};
+    switch (pn.kind) {
+      case K_NORM:
+        if (!need(H, 1)) return fail(MOE_ERR_INVALID, "post_attention_layernorm.weight shape");
+        norm = src;
+        break;
+      case K_ROUTER:
+        if (!need(E, H)) return fail(MOE_ERR_INVALID, "mlp.gate.weight must be [n_experts, hidden]");
+        router = src;
+        break;
+      case K_BIAS:
+        if (!need(E, 1)) return fail(MOE_ERR_INVALID, "e_score_correction_bias must be [n_experts]");
+        bias = src;
+        break;
+      case K_SHARED_GATE:
+        if (!(d.ndim == 2 && r0 == 1 && c0 == H) && !(d.ndim == 1 && r0 == H))
+          return fail(MOE_ERR_INVALID, "mlp.shared_expert_gate.weight must be [1, hidden]");
+        sgate = src;
+        break;
+      case K_EXPERT: {
+        if (pn.expert < 0 || pn.expert >= E)
+          return fail(MOE_ERR_INVALID, std::string("expert id out of range: ") + d.name);
+        const int le = pn.expert - p.e_begin;
+        if (le < 0 || le >= NL) break;  // not resident on this plan
+        const int64_t rows = pn.proj == P_DOWN ? H : I, cols = pn.proj == P_DOWN ? I : H;
+        if (pn.scale) {
+          if (dt != SRC_F16 || !need(rows, 1))
+            return fail(MOE_ERR_INVALID, std::string("scale must be float16 [rows]: ") + d.name);
+          exs[static_cast<size_t>(le) * 3 + pn.proj] = src;
+        } else {
+          if (!need(rows, cols)) return fail(MOE_ERR_INVALID, std::string("expert weight shape: ") + d.name);
+          ex[static_cast<size_t>(le) * 3 + pn.proj] = src;
+        }
+        break;
+      }
+      case K_SHARED: {
+        const int64_t rows = pn.proj == P_DOWN ? H : SI, cols = pn.proj == P_DOWN ? SI : H;
+        if (SI == 0) break;
+        if (pn.scale) {
+          if (dt != SRC_F16 || !need(rows, 1))
+            return fail(MOE_ERR_INVALID, std::string("scale must be float16 [rows]: ") + d.name);
+          shs[pn.proj] = src;
+        } else {
+          if (!need(rows, cols)) return fail(MOE_ERR_INVALID, std::string("shared expert shape: ") + d.name);
+          sh[pn.proj] = src;
+        }
+        break;
+      }
+      default: break;
+    }
+  }
+  if (!norm.ptr) return fail(MOE_ERR_MISSING_TENSOR, "post_attention_layernorm.weight");
+  if (!router.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.gate.weight");
+  if (p.cfg.has_shared_gate && !sgate.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.shared_expert_gate.weight");
+  static const char* pname[3] = {"gate_proj", "up_proj", "down_proj"};
+  for (int le = 0; le < NL; ++le)
+    for (int j = 0; j < 3; ++j) {
+      const Src& w = ex[static_cast<size_t>(le) * 3 + j];
+      if (!w.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.experts." + std::to_string(le + p.e_begin) + "." + pname[j] + ".weight");
+      if (w.dtype == SRC_I8 && !exs[static_cast<size_t>(le) * 3 + j].ptr)
+        return fail(MOE_ERR_MISSING_TENSOR, "mlp.experts." + std::to_string(le + p.e_begin) + "." + pname[j] + ".weight_scale");
+      if (w.dtype == SRC_I8 && !p.int8)
+        return fail(MOE_ERR_UNSUPPORTED, "int8 expert weights need weight_format = MOE_WEIGHTS_INT8_PC");
+    }
+  for (int j = 0; j < 3 && SI > 0; ++j) {
+    if (!sh[j].ptr) return fail(MOE_ERR_MISSING_TENSOR, std::string("shared expert ") + pname[j]);
+    if (sh[j].dtype == SRC_I8 && !shs[j].ptr) return fail(MOE_ERR_MISSING_TENSOR, std::string("shared expert scale ") + pname[j]);
+    if (sh[j].dtype == SRC_I8 && !p.int8)
+      return fail(MOE_ERR_UNSUPPORTED, "int8 shared weights need weight_format = MOE_WEIGHTS_INT8_PC");
+  }
+
+  // ---- allocate the resident layout (once per plan; reused by later binds)
+  const size_t wel = p.int8 ? 1 : 2;
+  size_t o = 0;
+  auto take = [&](size_t b) { size_t at = o; o = align256(o + b); return at; };
+  const size_t o_w13 = take(static_cast<size_t>(NL) * 2 * I * H * wel);
+  const size_t o_w2 = take(static_cast<size_t>(NL) * H * I * wel);
+  const size_t o_ws13 = take(static_cast<size_t>(2) * SI * H * wel);
+  const size_t o_ws2 = take(static_cast<size_t>(H) * SI * wel);
+  const size_t o_s13 = take(p.int8 ? static_cast<size_t>(NL) * 2 * I * 4 : 0);
+  const size_t o_s2 = take(p.int8 ? static_cast<size_t>(NL) * H * 4 : 0);
+  const size_t o_ss13 = take(p.int8 ? static_cast<size_t>(2) * SI * 4 : 0);
+  const size_t o_ss2 = take(p.int8 && SI > 0 ? static_cast<size_t>(H) * 4 : 0);
+  const size_t o_norm = take(static_cast<size_t>(H) * 4);
+  const size_t o_router = take(static_cast<size_t>(p.router_rows) * H * 4);
+  const size_t o_bias = take(static_cast<size_t>(E) * 4);
+  const size_t o_flag = take(16);
+  if (!p.weights_alloc) {
+    MOE_CUDA(cudaMalloc(&p.weights_alloc, o));
+    p.weights_bytes = o;
+  }
+  char* wb = static_cast<char*>(p.weights_alloc);
+  p.w.w13 = wb + o_w13;
+  p.w.w2 = wb + o_w2;
+  p.w.ws13 = SI > 0 ? wb + o_ws13 : nullptr;
+  p.w.ws2 = SI > 0 ? wb + o_ws2 : nullptr;
+  p.w.s13 = p.int8 ? reinterpret_cast<float*>(wb + o_s13) : nullptr;
+  p.w.s2 = p.int8 ? reinterpret_cast<float*>(wb + o_s2) : nullptr;
+  p.w.ss13 = p.int8 && SI > 0 ? reinterpret_cast<float*>(wb + o_ss13) : nullptr;
+  p.w.ss2 = p.int8 && SI > 0 ? reinterpret_cast<float*>(wb + o_ss2) : nullptr;
+  p.w.norm_w = reinterpret_cast<float*>(wb + o_norm);
+  p.w.router_w = reinterpret_cast<float*>(wb + o_router);
+  p.w.bias = (bias.ptr && p.cfg.use_bias) ? reinterpret_cast<float*>(wb + o_bias) : nullptr;
+  int* range_err = reinterpret_cast<int*>(wb + o_flag);
+  MOE_CUDA(cudaMemsetAsync(range_err, 0, sizeof(int), s));
+
+  // ---- pack
+  MOE_CUDA(launch_to_f32(norm.ptr, norm.dtype, p.w.norm_w, H, s));
+  MOE_CUDA(launch_to_f32(router.ptr, router.dtype, p.w.router_w, static_cast<int64_t>(E) * H, s));
+  if (sgate.ptr)
+    MOE_CUDA(launch_to_f32(sgate.ptr, sgate.dtype, p.w.router_w + static_cast<size_t>(E) * H, H, s));
+  if (p.w.bias) MOE_CUDA(launch_to_f32(bias.ptr, bias.dtype, p.w.bias, E, s));
+  for (int le = 0; le < NL; ++le) {
+    const Src& g = ex[le * 3 + P_GATE];
+    const Src& u = ex[le * 3 + P_UP];
+    const Src& dn = ex[le * 3 + P_DOWN];
+    char* d13 = static_cast<char*>(p.w.w13) + static_cast<size_t>(le) * 2 * I * H * wel;
+    char* d2 = static_cast<char*>(p.w.w2) + static_cast<size_t>(le) * H * I * wel;
+    float* s13 = p.int8 ? p.w.s13 + static_cast<size_t>(le) * 2 * I : nullptr;
+    float* s2 = p.int8 ? p.w.s2 + static_cast<size_t>(le) * H : nullptr;
+    if (g.dtype == SRC_I8 || u.dtype == SRC_I8) {
+      if (g.dtype != SRC_I8 || u.dtype != SRC_I8) return fail(MOE_ERR_UNSUPPORTED, "gate/up must share a dtype");
+      MOE_CUDA(launch_copy_i8_w13(reinterpret_cast<const int8_t*>(g.ptr), reinterpret_cast<const int8_t*>(u.ptr),
+                                  reinterpret_cast<const __half*>(exs[le * 3 + P_GATE].ptr),
+                                  reinterpret_cast<const __half*>(exs[le * 3 + P_UP].ptr),
+                                  reinterpret_cast<int8_t*>(d13), s13, I, H, s));
+    } else {
+      if (g.dtype != u.dtype) return fail(MOE_ERR_UNSUPPORTED, "gate/up must share a dtype");
+      MOE_CUDA(launch_pack_w13(g.ptr, u.ptr, g.dtype, d13, p.int8, s13, I, H, range_err, s));
+    }
+    if (dn.dtype == SRC_I8)
+      MOE_CUDA(launch_copy_i8_rows(reinterpret_cast<const int8_t*>(dn.ptr),
+                                   reinterpret_cast<const __half*>(exs[le * 3 + P_DOWN].ptr),
+                                   reinterpret_cast<int8_t*>(d2), s2, H, I, s));
+    else
+      MOE_CUDA(launch_pack_rows(dn.ptr, dn.dtype, d2, p.int8, s2, H, I, range_err, s));
+  }
+  if (SI > 0) {
+    if (sh[P_GATE].dtype == SRC_I8) {
+      MOE_CUDA(launch_copy_i8_w13(reinterpret_cast<const int8_t*>(sh[P_GATE].ptr),
+                                  reinterpret_cast<const int8_t*>(sh[P_UP].ptr),
+                                  reinterpret_cast<const __half*>(shs[P_GATE].ptr),
+                                  reinterpret_cast<const __half*>(shs[P_UP].ptr),
+                                  reinterpret_cast<int8_t*>(p.w.ws13), p.w.ss13, SI, H, s));
+    } else {
+      MOE_CUDA(launch_pack_w13(sh[P_GATE].ptr, sh[P_UP].ptr, sh[P_GATE].dtype, p.w.ws13, p.int8,
+                               p.w.ss13, SI, H, range_err, s));
+    }
+    if (sh[P_DOWN].dtype == SRC_I8)
+      MOE_CUDA(launch_copy_i8_rows(reinterpret_cast<const int8_t*>(sh[P_DOWN].ptr),
+                                   reinterpret_cast<const __half*>(shs[P_DOWN].ptr),
+                                   reinterpret_cast<int8_t*>(p.w.ws2), p.w.ss2, H, SI, s));
+    else
+      MOE_CUDA(launch_pack_rows(sh[P_DOWN].ptr, sh[P_DOWN].dtype, p.w.ws2, p.int8, p.w.ss2, H, SI,
+                                range_err, s));
+  }
+  int h_range = 0;
+  MOE_CUDA(cudaMemcpyAsync(&h_range, range_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MOE_CUDA(cudaStreamSynchronize(s));
+  if (h_range) return fail(MOE_ERR_RANGE, "an expert weight does not fit the packed format (|w| > 65504 for f16)");
+
+  // ---- tensor maps over the resident weights
+  std::string err;
+  const bool i8 = p.int8;
+  const bool sw = !i8;  // f16 tiles are swizzled for the MMA; int8 tiles are staged plain
+  if (!make_tmap_2d(&p.tm_w13, p.w.w13, i8, H, static_cast<uint64_t>(NL) * 2 * I, kBK, kBM, sw, &err) ||
+      !make_tmap_2d(&p.tm_w2, p.w.w2, i8, I, static_cast<uint64_t>(NL) * H, kBK, kBM, sw, &err))
+    return fail(MOE_ERR_CUDA, err);
+  if (SI > 0) {
+    if (!make_tmap_2d(&p.tm_ws13, p.w.ws13, i8, H, 2 * SI, kBK, kBM, sw, &err) ||
+        !make_tmap_2d(&p.tm_ws2, p.w.ws2, i8, SI, H, kBK, kBM, sw, &err))
+      return fail(MOE_ERR_CUDA, err);
+  }
+  p.bound = true;
+  return MOE_OK;
+}
+
+uint64_t moe_workspace_bytes(const MoePlan* plan, int32_t T) {
+  if (!plan || T <= 0) return 0;
+  return ws_layout(plan->p, T).total;
+}
+
+static int check_call(const MoePlan* plan, int32_t T, const void* ws, uint64_t ws_bytes) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  if (!plan->p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
+  if (T < 0 || T > plan->p.cfg.max_tokens)
+    return fail(MOE_ERR_INVALID, "T outside [0, max_tokens]");
+  if (T == 0) return MOE_OK;
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return fail(MOE_ERR_WORKSPACE, "workspace must be a 256-byte aligned device pointer");
+  if (ws_bytes < ws_layout(plan->p, T).total) return fail(MOE_ERR_WORKSPACE, "workspace too small");
+  return MOE_OK;
+}
+
+static int route_impl(Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                      bool gather, cudaStream_t s) {
+  float* h32 = reinterpret_cast<float*>(ws + L.h32);
+  __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + L.ids);
+  float* wts = reinterpret_cast<float*>(ws + L.wts);
+  float* sgate = reinterpret_cast<float*>(ws + L.sgate);
+  MOE_CUDA(launch_rmsnorm(p, x, h32, h16, T, s));
+  MOE_CUDA(launch_router(p, h32, logits, T, s));
+  MOE_CUDA(launch_topk(p, logits, ids, wts, sgate, T, s));
+  MOE_CUDA(launch_permute(p, L, ws, ids, gather ? h16 : nullptr, T, s));
+  return MOE_OK;
+}
+
+int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T, void* workspace,
+                uint64_t workspace_bytes, void* stream) {
+  int rc = check_call(plan, T, workspace, workspace_bytes);
+  if (rc != MOE_OK || T == 0) return rc;
+  if (!x_dev || !out_dev) return fail(MOE_ERR_INVALID, "null x / out");
+  if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  Plan& p = plan->p;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  rc = route_impl(p, L, ws, x_dev, T, true, s);
+  if (rc != MOE_OK) return rc;
+  MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, T, s));
+  MOE_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
+                          reinterpret_cast<float*>(ws + L.y_s),
+                          reinterpret_cast<int32_t*>(ws + L.slot_row),
+                          reinterpret_cast<float*>(ws + L.wts),
+                          reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
+  return MOE_OK;
+}
+
+int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
+                      void* workspace, uint64_t workspace_bytes, float* stage_ms, void* stream) {
+  int rc = check_call(plan, T, workspace, workspace_bytes);
+  if (rc != MOE_OK) return rc;
+  if (!x_dev || !out_dev || !stage_ms) return fail(MOE_ERR_INVALID, "null x / out / stage_ms");
+  if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  for (int i = 0; i < 4; ++i) stage_ms[i] = 0.f;
+  if (T == 0) return MOE_OK;
+  Plan& p = plan->p;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  cudaEvent_t ev[5];
+  for (int i = 0; i < 5; ++i) MOE_CUDA(cudaEventCreate(&ev[i]));
+  struct Guard {
+    cudaEvent_t* e;
+    ~Guard() {
+      for (int i = 0; i < 5; ++i) cudaEventDestroy(e[i]);
+    }
+  } guard{ev};
+  MOE_CUDA(cudaEventRecord(ev[0], s));
+  rc = route_impl(p, L, ws, x_dev, T, true, s);
+  if (rc != MOE_OK) return rc;
+  MOE_CUDA(cudaEventRecord(ev[1], s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
+  MOE_CUDA(cudaEventRecord(ev[2], s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, T, s));
+  MOE_CUDA(cudaEventRecord(ev[3], s));
+  MOE_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
+                          reinterpret_cast<float*>(ws + L.y_s),
+                          reinterpret_cast<int32_t*>(ws + L.slot_row),
+                          reinterpret_cast<float*>(ws + L.wts),
+                          reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
+  MOE_CUDA(cudaEventRecord(ev[4], s));
+  MOE_CUDA(cudaEventSynchronize(ev[4]));
+  for (int i = 0; i < 4; ++i) MOE_CUDA(cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]));
+  return MOE_OK;
+}
+
+int moe_route(MoePlan* plan, const float* x_dev, int32_t T, int32_t* topk_ids, float* topk_w,
+              int32_t* expert_offsets, int32_t* perm, void* workspace, uint64_t workspace_bytes,
+              void* stream) {
+  int rc = check_call(plan, T, workspace, workspace_bytes);
+  if (rc != MOE_OK || T == 0) return rc;
+  if (!x_dev) return fail(MOE_ERR_INVALID, "null x");
+  Plan& p = plan->p;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  rc = route_impl(p, L, ws, x_dev, T, false, s);
+  if (rc != MOE_OK) return rc;
+  const size_t R = static_cast<size_t>(T) * p.K;
+  if (topk_ids) MOE_CUDA(cudaMemcpyAsync(topk_ids, ws + L.ids, R * 4, cudaMemcpyDeviceToDevice, s));
+  if (topk_w) MOE_CUDA(cudaMemcpyAsync(topk_w, ws + L.wts, R * 4, cudaMemcpyDeviceToDevice, s));
+  if (expert_offsets)
+    MOE_CUDA(cudaMemcpyAsync(expert_offsets, ws + L.offsets, (p.E + 1) * 4, cudaMemcpyDeviceToDevice, s));
+  if (perm) MOE_CUDA(cudaMemcpyAsync(perm, ws + L.perm, R * 4, cudaMemcpyDeviceToDevice, s));
+  return MOE_OK;
+}
+
+int moe_status(MoePlan* plan, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  MOE_CUDA(cudaSetDevice(p.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  MOE_CUDA(cudaMemcpyAsync(&h, p.d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MOE_CUDA(cudaMemsetAsync(p.d_err, 0, sizeof(int), s));
+  MOE_CUDA(cudaStreamSynchronize(s));
+  if (h == DEV_OK) return MOE_OK;
+  if (h >= DEV_TIMEOUT_FULL && h <= DEV_TIMEOUT_CONV)
+    return fail(MOE_ERR_TIMEOUT, "a device-side wait ran out of time (code " + std::to_string(h) + ")");
+  return fail(MOE_ERR_DEVICE, "a kernel reported device error code " + std::to_string(h));
+}
+
+// ------------------------------------------------------------ runtime wrappers
+int moe_rt_device_count(int32_t* count) {
+  int n = 0;
+  MOE_CUDA(cudaGetDeviceCount(&n));
+  if (count) *count = n;
+  return MOE_OK;
+}
+int moe_rt_set_device(int32_t device) {
+  MOE_CUDA(cudaSetDevice(device));
+  return MOE_OK;
+}
+int moe_rt_malloc(uint64_t nbytes, void** dev_ptr) {
+  if (!dev_ptr) return fail(MOE_ERR_INVALID, "null out pointer");
+  MOE_CUDA(cudaMalloc(dev_ptr, nbytes));
+  return MOE_OK;
+}
+int moe_rt_free(void* dev_ptr) {
+  MOE_CUDA(cudaFree(dev_ptr));
+  return MOE_OK;
+}
+int moe_rt_malloc_host(uint64_t nbytes, void** host_ptr) {
+  if (!host_ptr) return fail(MOE_ERR_INVALID, "null out pointer");
+  MOE_CUDA(cudaMallocHost(host_ptr, nbytes));
+  return MOE_OK;
+}
+int moe_rt_free_host(void* host_ptr) {
+  MOE_CUDA(cudaFreeHost(host_ptr));
+  return MOE_OK;
+}
+int moe_rt_stream_create(void** stream) {
+  if (!stream) return fail(MOE_ERR_INVALID, "null out pointer");
+  cudaStream_t s;
+  MOE_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = s;
+  return MOE_OK;
+}
+int moe_rt_stream_destroy(void* stream) {
+  MOE_CUDA(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+int moe_rt_memcpy_h2d_async(void* dst_dev, const void* src_host, uint64_t nbytes, void* stream) {
+  MOE_CUDA(cudaMemcpyAsync(dst_dev, src_host, nbytes, cudaMemcpyHostToDevice,
+                           static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+int moe_rt_memcpy_d2h_async(void* dst_host, const void* src_dev, uint64_t nbytes, void* stream) {
+  MOE_CUDA(cudaMemcpyAsync(dst_host, src_dev, nbytes, cudaMemcpyDeviceToHost,
+                           static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+int moe_rt_memcpy_d2d_async(void* dst_dev, const void* src_dev, uint64_t nbytes, void* stream) {
+  MOE_CUDA(cudaMemcpyAsync(dst_dev, src_dev, nbytes, cudaMemcpyDeviceToDevice,
+                           static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+int moe_rt_event_record(void* stream, void** event) {
+  if (!event) return fail(MOE_ERR_INVALID, "null out pointer");
+  cudaEvent_t e;
+  MOE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  MOE_CUDA(cudaEventRecord(e, static_cast<cudaStream_t>(stream)));
+  *event = e;
+  return MOE_OK;
+}
+int moe_rt_event_destroy(void* event) {
+  MOE_CUDA(cudaEventDestroy(static_cast<cudaEvent_t>(event)));
+  return MOE_OK;
+}
+int moe_rt_stream_wait_event(void* stream, void* event) {
+  MOE_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0));
+  return MOE_OK;
+}
+int moe_rt_stream_synchronize(void* stream) {
+  MOE_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+
+}  // extern "C"

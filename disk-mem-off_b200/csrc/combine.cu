@@ -1,0 +1,65 @@
+// Weighted combine + shared expert + residual (K5/K6 epilogue of the MoE block).
+//
+// Reference: glm4_moe.py:226-240 / qwen3_next.py:315-333
+//   output[tok] += w_e * expert_out        (one term per selected expert)
+//   output = output + shared_out           (shared_out * sigmoid(h . w_gate) on Qwen3)
+//   return x + output
+// Here the K routed terms of a token are summed in slot order (descending
+// router weight) from the expert-major y rows, products and sums rounded
+// separately like the reference's numpy expressions.  Deterministic: no atomics.
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+__global__ void __launch_bounds__(256) combine_kernel(
+    const float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ y_s,
+    const int32_t* __restrict__ slot_row, const float* __restrict__ wts,
+    const float* __restrict__ sgate, float* __restrict__ out, int K, int H) {
+  const int t = blockIdx.y;
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
+  if (v >= (H >> 2)) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < K; ++j) {
+    const int row = slot_row[t * K + j];
+    const float w = wts[t * K + j];
+    const float4 yv = reinterpret_cast<const float4*>(y + static_cast<size_t>(row) * H)[v];
+    acc.x = __fadd_rn(acc.x, __fmul_rn(w, yv.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(w, yv.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(w, yv.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(w, yv.w));
+  }
+  if (y_s) {
+    float4 sv = reinterpret_cast<const float4*>(y_s + static_cast<size_t>(t) * H)[v];
+    if (sgate) {
+      const float g = sgate[t];
+      sv.x = __fmul_rn(sv.x, g);
+      sv.y = __fmul_rn(sv.y, g);
+      sv.z = __fmul_rn(sv.z, g);
+      sv.w = __fmul_rn(sv.w, g);
+    }
+    acc.x = __fadd_rn(acc.x, sv.x);
+    acc.y = __fadd_rn(acc.y, sv.y);
+    acc.z = __fadd_rn(acc.z, sv.z);
+    acc.w = __fadd_rn(acc.w, sv.w);
+  }
+  const float4 xv = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H)[v];
+  float4 o;
+  o.x = __fadd_rn(xv.x, acc.x);
+  o.y = __fadd_rn(xv.y, acc.y);
+  o.z = __fadd_rn(xv.z, acc.z);
+  o.w = __fadd_rn(xv.w, acc.w);
+  reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H)[v] = o;
+}
+
+cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,
+                           const int32_t* slot_row, const float* wts, const float* sgate,
+                           float* out, int T, cudaStream_t s) {
+  const int nv = p.H >> 2;
+  dim3 grid((nv + 255) / 256, T);
+  combine_kernel<<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
+                                      p.cfg.has_shared_gate ? sgate : nullptr, out, p.K, p.H);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,195 @@
+// Shared device helpers for the sm_100a MoE kernels: error flags, bounded
+// mbarrier waits, TMA tile loads and the tcgen05 (5th-gen tensor core / TMEM)
+// instruction wrappers.  Everything here is inline PTX written for sm_100a.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MOE_DEV __device__ __forceinline__
+
+namespace moe {
+
+// Device-side status codes written to the plan's error word.  The host reads
+// the word after a forward (moe_status) and maps it to MOE_ERR_TIMEOUT /
+// MOE_ERR_DEVICE.  Kernels never trap: a wait that runs out of time records a
+// code and the kernel drains and returns.
+enum DevErr : int {
+  DEV_OK = 0,
+  DEV_TIMEOUT_FULL = 1,      // MMA waited too long for a TMA stage
+  DEV_TIMEOUT_EMPTY = 2,     // producer waited too long for a free stage
+  DEV_TIMEOUT_TMEM_FULL = 3, // epilogue waited too long for an accumulator
+  DEV_TIMEOUT_TMEM_EMPTY = 4,// MMA waited too long for an accumulator buffer
+  DEV_TIMEOUT_CONV = 5,      // int8 converter waited too long
+  DEV_BAD_TILE = 6,          // tile list entry out of range
+  DEV_BAD_ROUTE = 7,         // router produced an expert id out of range
+};
+
+// ~1 s at the B200 boost clock.  Legitimate waits in these kernels are
+// microseconds; this bound only ends a wait that can no longer complete.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+MOE_DEV void record_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+MOE_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+MOE_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+MOE_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+MOE_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+MOE_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+MOE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity; false if the wait ran out of time
+// or the CTA was told to abort (another role already timed out).
+MOE_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  long long start = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - start > kWaitLimitCycles) return false;
+  }
+}
+
+// Same bound, but not cut short by the abort flag: used when a role drains its
+// own in-flight copies / MMAs before the CTA releases shared memory and TMEM.
+MOE_DEV bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- TMA
+MOE_DEV void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2D tiled load global -> shared (this CTA), completion counted in bytes on bar.
+// c0 is the innermost (K) coordinate in elements, c1 the row coordinate.
+MOE_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+MOE_DEV void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+MOE_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+MOE_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+MOE_DEV void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+MOE_DEV void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulate.
+MOE_DEV void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on bar when every tcgen05.mma issued so far by this thread completes.
+MOE_DEV void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+MOE_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with
+// 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart (SBO), tile base
+// 1024-byte aligned.  Layout code 2 = SWIZZLE_128B, version bits [46,48) = 1.
+MOE_DEV uint64_t sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;              // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;      // SBO
+  d |= static_cast<uint64_t>(1) << 46;              // version
+  d |= static_cast<uint64_t>(2) << 61;              // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: f16 x f16 -> f32, both operands K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+  return (1u << 4)                                  // D format f32
+         | (0u << 7) | (0u << 10)                   // A, B = f16
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+MOE_DEV float silu_f(float g) { return g / (1.0f + expf(-g)); }
+MOE_DEV float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+}  // namespace moe

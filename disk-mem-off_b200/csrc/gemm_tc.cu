@@ -1,0 +1,445 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the per-expert fp32 BLAS calls of the reference
+// (glm4_moe.py:218-224 and qwen3_next.py:307-313, shared expert 234-238 /
+// 321-331) with one persistent launch per projection:
+//
+//   gate/up : D[2I rows of W13, tokens] = W13_e . X_e^T, epilogue silu(g) * u -> act (f16)
+//   down    : D[H rows of W2,  tokens]  = W2_e  . act_e^T, epilogue -> y (fp32)
+//
+// "Swap-AB": the weight matrix is the M operand (128 rows per tile, read from
+// HBM exactly once per token tile) and the tokens routed to an expert are the
+// N operand (16..256 columns), so a decode step with one token per expert is a
+// weight-streaming GEMV on the tensor pipe and a prefill is an ordinary
+// grouped GEMM.  Operands are K-major in shared memory, staged by TMA with
+// 128-byte swizzle; accumulators live in TMEM (two buffers so the epilogue of
+// one tile overlaps the MMAs of the next).
+//
+// INT8 per-channel weights: TMA brings the int8 tile into a staging buffer,
+// four converter warps widen it to f16 (exact for |q| <= 127) straight into the
+// swizzled MMA operand layout, and the per-row scale is applied to the fp32
+// accumulator in the epilogue (scale is per M row = per TMEM lane).
+//
+// Warp roles (192 or 320 threads): warp 0 TMA producer, warp 1 TMEM owner and
+// MMA issuer, warps 2-5 epilogue, warps 6-9 int8 converters.
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+struct GemmArgs {
+  CUtensorMap a_routed;  // weights: f16 or int8 [groups * rows_a][K]
+  CUtensorMap a_shared;  // shared expert weights [m_limit_shared][K]
+  CUtensorMap b_routed;  // activations f16 [rows][K]
+  CUtensorMap b_shared;
+  const Tile* tiles;
+  const int32_t* tile_count;
+  int count_index;
+  int max_tiles;
+  int n_local;           // group id of the shared expert
+  int rows_a_routed;     // A rows per routed expert
+  int m_limit_routed;    // valid A rows per routed expert
+  int m_limit_shared;
+  int k_routed, k_shared;
+  __half* act_routed;    // gate/up outputs [rows][I]
+  __half* act_shared;    // [T][SI]
+  int act_ld_routed, act_ld_shared;
+  float* y_routed;       // down outputs [rows][H]
+  float* y_shared;       // [T][H]
+  int y_ld;
+  const float* scale_routed;  // int8 row scales [groups * rows_a]
+  const float* scale_shared;  // [m_limit_shared]
+  int* err;
+};
+
+template <int BN>
+struct TileCfg {
+  static constexpr int kStageA = kBM * kBK * 2;      // f16 A tile, 16 KiB
+  static constexpr int kStageA8 = kBM * kBK;         // int8 staging tile, 8 KiB
+  static constexpr int kStageB = BN * kBK * 2;
+  static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+};
+
+template <int BN, bool INT8>
+__host__ __device__ constexpr int gemm_stages() {
+  constexpr int per = TileCfg<BN>::kStageA + TileCfg<BN>::kStageB + (INT8 ? TileCfg<BN>::kStageA8 : 0);
+  constexpr int s = (200 * 1024) / per;
+  return s > 8 ? 8 : s;
+}
+
+template <int BN, bool INT8>
+__host__ __device__ constexpr size_t gemm_smem_bytes() {
+  constexpr int st = gemm_stages<BN, INT8>();
+  return 1024 /*align slack*/ +
+         static_cast<size_t>(st) * (TileCfg<BN>::kStageA + TileCfg<BN>::kStageB +
+                                    (INT8 ? TileCfg<BN>::kStageA8 : 0)) +
+         256 /*barriers*/;
+}
+
+// Widen one 128 x 64 int8 row-major tile to f16 in the 128-byte-swizzled
+// K-major layout the MMA descriptor expects (16-byte chunk c of row r lands at
+// chunk c ^ (r & 7)).  int8 -> f16 exactly: bias the byte to u = q + 128, place
+// it in the mantissa of 1024.0 (0x6400 | u = 1024 + u), subtract 1152.
+MOE_DEV void convert_row_i8_f16(const int8_t* src_row, uint8_t* dst_tile, int r) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src_row);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {  // 4 x 16 int8 = 64 elements
+    const uint4 q = s4[v];
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u = words[i] ^ 0x80808080u;
+      uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140);
+      uint32_t hi = __byte_perm(u, 0x64646464u, 0x4342);
+      __half2 l2 = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);
+      __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+      out[2 * i] = *reinterpret_cast<uint32_t*>(&l2);
+      out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    // 16 int8 -> 32 bytes of f16 = chunks 2v and 2v+1 of this row
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int chunk = 2 * v + h;
+      uint4* dst = reinterpret_cast<uint4*>(dst_tile + r * 128 + ((chunk ^ (r & 7)) << 4));
+      *dst = make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+    }
+  }
+}
+
+template <int BN, bool DOWN, bool INT8>
+__global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
+    moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
+  constexpr int STAGES = gemm_stages<BN, INT8>();
+  constexpr int SA = TileCfg<BN>::kStageA, SB = TileCfg<BN>::kStageB, SA8 = TileCfg<BN>::kStageA8;
+  constexpr uint32_t IDESC = idesc_f16_f32(kBM, BN);
+  constexpr uint32_t TMEM_COLS = TileCfg<BN>::kTmemCols;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * SA;
+  uint8_t* sA8 = sB + STAGES * SB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + (INT8 ? STAGES * SA8 : 0));
+  uint64_t* full = bars;                 // TMA landed (A + B)
+  uint64_t* empty = full + STAGES;       // MMA finished reading the stage
+  uint64_t* conv = empty + STAGES;       // int8 tile widened to f16
+  uint64_t* tfull = conv + STAGES;       // accumulator ready
+  uint64_t* tempty = tfull + 2;          // accumulator drained
+  uint64_t* mma_done = tempty + 2;       // final drain of in-flight MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = min(*(args.tile_count + args.count_index), args.max_tiles);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&args.a_routed);
+    tma_prefetch_desc(&args.b_routed);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto tile_ok = [&](const Tile& t) {
+    if (t.group < 0 || t.group > args.n_local || t.nvalid <= 0 || t.nvalid > BN) return false;
+    const int lim = (t.group == args.n_local) ? args.m_limit_shared : args.m_limit_routed;
+    return t.m0 >= 0 && t.m0 < lim;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
+        const Tile t = args.tiles[ti];
+        if (!tile_ok(t)) {
+          record_error(args.err, DEV_BAD_TILE);
+          continue;
+        }
+        const bool sh = t.group == args.n_local;
+        const CUtensorMap* ma = sh ? &args.a_shared : &args.a_routed;
+        const CUtensorMap* mb = sh ? &args.b_shared : &args.b_routed;
+        const int arow = sh ? t.m0 : t.group * args.rows_a_routed + t.m0;
+        const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag)) {
+            *abort_flag = 1;
+            record_error(args.err, DEV_TIMEOUT_EMPTY);
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], (INT8 ? SA8 : SA) + SB);
+          tma_load_2d(INT8 ? sA8 + s * SA8 : sA + s * SA, ma, kb * kBK, arow, &full[s]);
+          tma_load_2d(sB + s * SB, mb, kb * kBK, t.row0, &full[s]);
+        }
+      }
+      // drain: every stage's most recent load must have landed before exit
+      for (int j = 0; j < STAGES && j < it; ++j) {
+        const int i = it - 1 - j;
+        const int s = i % STAGES;
+        mbar_wait_drain(&full[s], (i / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, tl = 0;
+      bool issued = false;
+      for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
+        const Tile t = args.tiles[ti];
+        if (!tile_ok(t)) continue;
+        const bool sh = t.group == args.n_local;
+        const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
+        const int buf = tl & 1;
+        if (!mbar_wait_bounded(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag)) {
+          *abort_flag = 1;
+          record_error(args.err, DEV_TIMEOUT_TMEM_EMPTY);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(INT8 ? &conv[s] : &full[s], ph, abort_flag)) {
+            *abort_flag = 1;
+            record_error(args.err, DEV_TIMEOUT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * SA), b0 = smem_u32(sB + s * SB);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            tc_mma_f16(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          issued = true;
+        }
+        if (!ok) break;
+        tc_commit(&tfull[buf]);
+        ++tl;
+      }
+      if (issued) {  // make sure no MMA still writes TMEM when it is released
+        tc_commit(mma_done);
+        mbar_wait_drain(mma_done, 0);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int tl = 0;
+    for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+      const Tile t = args.tiles[ti];
+      if (!tile_ok(t)) continue;
+      const int buf = tl & 1;
+      // every lane polls; the vote re-converges the warp before the
+      // .sync.aligned TMEM loads and makes the timeout decision warp-uniform
+      const bool ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl >> 1) & 1, abort_flag));
+      if (!ready) {
+        *abort_flag = 1;
+        record_error(args.err, DEV_TIMEOUT_TMEM_FULL);
+        break;
+      }
+      tc_fence_after();
+      const bool sh = t.group == args.n_local;
+      const int mrow = t.m0 + r;  // row inside this group's A matrix
+      const bool row_ok = mrow < (sh ? args.m_limit_shared : args.m_limit_routed);
+      float rs = 1.f;
+      if (INT8 && row_ok) {
+        rs = sh ? args.scale_shared[mrow]
+                : args.scale_routed[static_cast<size_t>(t.group) * args.rows_a_routed + mrow];
+      }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      const int ncol = (t.nvalid + 15) & ~15;
+      for (int c0 = 0; c0 < ncol; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= rs;
+        if constexpr (!DOWN) {
+          // lanes 0-15: gate rows, lanes 16-31: the matching up rows
+          const int feat = (mrow >> 5) * 16 + (lane & 15);
+          const bool feat_ok = row_ok;
+          __half* dst = sh ? args.act_shared : args.act_routed;
+          const int ld = sh ? args.act_ld_shared : args.act_ld_routed;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], 16);
+            if ((i & 1) == (lane >> 4)) {
+              const int col = c0 + i;
+              if (col < t.nvalid && feat_ok) {
+                const float g = (lane < 16) ? v[i] : o;
+                const float u = (lane < 16) ? o : v[i];
+                dst[static_cast<size_t>(t.row0 + col) * ld + feat] = __float2half_rn(silu_f(g) * u);
+              }
+            }
+          }
+        } else {
+          float* dst = sh ? args.y_shared : args.y_routed;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = c0 + i;
+            if (col < t.nvalid && row_ok) dst[static_cast<size_t>(t.row0 + col) * args.y_ld + mrow] = v[i];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+      ++tl;
+    }
+  } else if constexpr (INT8) {
+    // ------------------------------------------------------------ int8 -> f16
+    const int r = (warp - 6) * 32 + lane;  // one A row per thread
+    int it = 0;
+    for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
+      const Tile t = args.tiles[ti];
+      if (!tile_ok(t)) continue;
+      const bool sh = t.group == args.n_local;
+      const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+          *abort_flag = 1;
+          record_error(args.err, DEV_TIMEOUT_CONV);
+          ok = false;
+          break;
+        }
+        convert_row_i8_f16(reinterpret_cast<const int8_t*>(sA8 + s * SA8 + r * kBK), sA + s * SA, r);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&conv[s]);
+      }
+      if (!ok) break;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ launcher
+template <int BN, bool DOWN, bool INT8>
+static cudaError_t run_gemm(const GemmArgs& a, int grid, cudaStream_t s) {
+  constexpr size_t smem = gemm_smem_bytes<BN, INT8>();
+  static bool attr_set[64] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t st = cudaFuncSetAttribute(moe_gemm_kernel<BN, DOWN, INT8>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    if (st != cudaSuccess) return st;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  moe_gemm_kernel<BN, DOWN, INT8><<<grid, INT8 ? 320 : 192, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <bool DOWN, bool INT8>
+static cudaError_t dispatch_bn(const GemmArgs& a, int bn, int grid, cudaStream_t s) {
+  switch (bn) {
+    case 16: return run_gemm<16, DOWN, INT8>(a, grid, s);
+    case 32: return run_gemm<32, DOWN, INT8>(a, grid, s);
+    case 64: return run_gemm<64, DOWN, INT8>(a, grid, s);
+    case 128: return run_gemm<128, DOWN, INT8>(a, grid, s);
+    case 256: return run_gemm<256, DOWN, INT8>(a, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
+                        cudaStream_t s) {
+  GemmArgs a;
+  std::string err;
+  const int rows = T * p.K;
+  const int bn = L.bn;
+  const bool has_sh = p.SI > 0;
+  __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
+  __half* xg = reinterpret_cast<__half*>(ws + L.xg);
+  __half* act = reinterpret_cast<__half*>(ws + L.act);
+  __half* act_s = reinterpret_cast<__half*>(ws + L.act_s);
+  if (!down) {
+    a.a_routed = p.tm_w13;
+    a.a_shared = has_sh ? p.tm_ws13 : p.tm_w13;
+    if (!make_tmap_2d(&a.b_routed, xg, false, p.H, rows, kBK, bn, true, &err) ||
+        !make_tmap_2d(&a.b_shared, h16, false, p.H, T, kBK, bn, true, &err)) {
+      set_error(err);
+      return cudaErrorInvalidValue;
+    }
+    a.rows_a_routed = 2 * p.I;
+    a.m_limit_routed = 2 * p.I;
+    a.m_limit_shared = 2 * p.SI;
+    a.k_routed = p.H;
+    a.k_shared = p.H;
+    a.scale_routed = p.w.s13;
+    a.scale_shared = p.w.ss13;
+    a.count_index = 0;
+    a.max_tiles = L.max_tiles1;
+  } else {
+    a.a_routed = p.tm_w2;
+    a.a_shared = has_sh ? p.tm_ws2 : p.tm_w2;
+    if (!make_tmap_2d(&a.b_routed, act, false, p.I, rows, kBK, bn, true, &err) ||
+        !make_tmap_2d(&a.b_shared, has_sh ? act_s : act, false, has_sh ? p.SI : p.I,
+                      has_sh ? T : rows, kBK, bn, true, &err)) {
+      set_error(err);
+      return cudaErrorInvalidValue;
+    }
+    a.rows_a_routed = p.H;
+    a.m_limit_routed = p.H;
+    a.m_limit_shared = p.H;
+    a.k_routed = p.I;
+    a.k_shared = has_sh ? p.SI : p.I;
+    a.scale_routed = p.w.s2;
+    a.scale_shared = p.w.ss2;
+    a.count_index = 1;
+    a.max_tiles = L.max_tiles2;
+  }
+  a.tiles = reinterpret_cast<const Tile*>(ws + (down ? L.tiles2 : L.tiles1));
+  a.tile_count = reinterpret_cast<const int32_t*>(ws + L.tile_count);
+  a.n_local = p.n_local;
+  a.act_routed = act;
+  a.act_shared = act_s;
+  a.act_ld_routed = p.I;
+  a.act_ld_shared = p.SI;
+  a.y_routed = reinterpret_cast<float*>(ws + L.y);
+  a.y_shared = reinterpret_cast<float*>(ws + L.y_s);
+  a.y_ld = p.H;
+  a.err = p.d_err;
+  const int max_tiles = down ? L.max_tiles2 : L.max_tiles1;
+  const int grid = max_tiles < p.num_sms ? max_tiles : p.num_sms;
+  if (grid <= 0) return cudaSuccess;
+  if (p.int8) return down ? dispatch_bn<true, true>(a, bn, grid, s) : dispatch_bn<false, true>(a, bn, grid, s);
+  return down ? dispatch_bn<true, false>(a, bn, grid, s) : dispatch_bn<false, false>(a, bn, grid, s);
+}
+
+}  // namespace moe

@@ -1,0 +1,111 @@
+// Internal plan / workspace structures shared by the .cu files of libmoe_sm100.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/moe_sm100.h"
+
+namespace moe {
+
+constexpr int kBM = 128;          // GEMM tile rows (weight rows, swap-AB)
+constexpr int kBK = 64;           // GEMM k-block (one 128-byte swizzle atom of f16)
+constexpr int kPermChunk = 1024;  // tokens per permutation chunk (bitmask width)
+constexpr int kMaxTopK = 32;
+
+// One unit of work for the grouped GEMM: weight rows [m0, m0+128) of group
+// `group` (local routed expert index, or n_local for the shared expert)
+// against activation rows [row0, row0 + nvalid) of that group's B matrix.
+struct Tile {
+  int group;
+  int m0;
+  int row0;
+  int nvalid;
+};
+
+struct DeviceWeights {
+  // Packed, HBM-resident weights.  W13 rows are interleaved in groups of 32:
+  // 16 gate_proj rows then the 16 matching up_proj rows, so one TMEM lane
+  // quarter holds both halves of 16 SwiGLU features.
+  void* w13 = nullptr;   // f16 or int8 [E_local][2I][H]
+  void* w2 = nullptr;    // f16 or int8 [E_local][H][I]
+  void* ws13 = nullptr;  // shared expert [2SI][H]
+  void* ws2 = nullptr;   // shared expert [H][SI]
+  float* s13 = nullptr;  // int8 row scales [E_local][2I] (packed-row order)
+  float* s2 = nullptr;   // [E_local][H]
+  float* ss13 = nullptr; // [2SI]
+  float* ss2 = nullptr;  // [H]
+  float* norm_w = nullptr;    // [H]
+  float* router_w = nullptr;  // [E (+1 shared gate row)][H]
+  float* bias = nullptr;      // [E] or null
+};
+
+struct Plan {
+  MoeConfig cfg{};
+  int device = 0;
+  int num_sms = 148;
+  int E = 0, K = 0, H = 0, I = 0, SI = 0;
+  int e_begin = 0, e_end = 0, n_local = 0;
+  int router_rows = 0;
+  bool int8 = false;
+  bool bound = false;
+  DeviceWeights w;
+  void* weights_alloc = nullptr;
+  size_t weights_bytes = 0;
+  int* d_err = nullptr;        // device error word
+  CUtensorMap tm_w13{}, tm_w2{}, tm_ws13{}, tm_ws2{};
+};
+
+// Workspace carve-up for one forward of T tokens (offsets in bytes).
+struct WsLayout {
+  size_t h32, h16, xg, act, act_s, y, y_s, logits, ids, wts, sgate;
+  size_t bm, hist, base, offsets, perm, slot_row, tiles1, tiles2, tile_count;
+  size_t total;
+  int nchunks, max_tiles1, max_tiles2, bn;
+};
+
+WsLayout ws_layout(const Plan& p, int T);
+
+// ------------------------------------------------------------ launchers
+cudaError_t launch_rmsnorm(const Plan& p, const float* x, float* h32, __half* h16, int T,
+                           cudaStream_t s);
+cudaError_t launch_router(const Plan& p, const float* h32, float* logits, int T, cudaStream_t s);
+cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float* wts,
+                        float* sgate, int T, cudaStream_t s);
+cudaError_t launch_permute(const Plan& p, const WsLayout& L, char* ws, const int32_t* ids,
+                           const __half* h16, int T, cudaStream_t s);
+cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
+                        cudaStream_t s);
+cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,
+                           const int32_t* slot_row, const float* wts, const float* sgate,
+                           float* out, int T, cudaStream_t s);
+
+// weight packing (bind)
+cudaError_t launch_pack_rows(const void* src, int src_dtype, void* dst, bool to_int8,
+                             float* dst_scale, int rows, int cols, int* range_err,
+                             cudaStream_t s);
+cudaError_t launch_pack_w13(const void* gate, const void* up, int src_dtype, void* dst,
+                            bool to_int8, float* dst_scale, int inter, int cols,
+                            int* range_err, cudaStream_t s);
+cudaError_t launch_copy_i8_w13(const int8_t* gate, const int8_t* up, const __half* gs,
+                               const __half* us, int8_t* dst, float* dst_scale, int inter,
+                               int cols, cudaStream_t s);
+cudaError_t launch_copy_i8_rows(const int8_t* src, const __half* ss, int8_t* dst,
+                                float* dst_scale, int rows, int cols, cudaStream_t s);
+cudaError_t launch_to_f32(const void* src, int src_dtype, float* dst, int64_t n,
+                          cudaStream_t s);
+
+// source dtypes understood by the packers
+enum SrcDtype { SRC_F32 = 0, SRC_F16 = 1, SRC_BF16 = 2, SRC_I8 = 3 };
+
+// tensor maps
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool int8, uint64_t inner, uint64_t rows,
+                  uint32_t box_inner, uint32_t box_rows, bool swizzle128, std::string* err);
+
+void set_error(const std::string& msg);
+
+}  // namespace moe

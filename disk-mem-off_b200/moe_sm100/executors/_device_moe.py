@@ -1,0 +1,184 @@
+"""Device MoE path shared by the GLM-4 MoE and Qwen3-Next executors.
+
+Drop-in for the reference executors' MoE block:
+
+* ``_moe_mlp_block(x, t)`` keeps the reference signature (glm4_moe.py:176,
+  qwen3_next.py:273): ``x`` is a host fp32 ``[T, H]`` array (or a CUDA fp32
+  tensor), ``t`` the layer's named tensors.  ``t`` may be the reference's dict of
+  host arrays (packed to the device once and cached) or a bound ``MoeLayer``.
+* ``run_layer(layer, activations, device_weights, backend, stream)`` keeps the
+  ``LayerExecutor`` protocol (runtime.py:15-26).  The MoE tensors are packed
+  straight from the device blob; only the non-MoE tensors (attention, input
+  norm) are read back to the host for the attention delegate, instead of the
+  whole blob (_common.py:20-33).
+* Attention and the dense MLP of ``first_k_dense_replace`` layers are not part
+  of this library: pass ``attention=`` / ``dense_mlp=`` callables (for example
+  the reference executor's own methods, see ``reference_delegates``).
+"""
+from __future__ import annotations
+
+from typing import Any, Callable
+
+import numpy as np
+
+from ..config import MoeLayerConfig
+from ..layer import MoeLayer, layer_shapes
+from ..packing import pack_layer
+
+AttentionFn = Callable[[Any, Any, dict[str, Any]], Any]   # (layer, x, t_host) -> x
+DenseFn = Callable[[Any, dict[str, Any]], Any]            # (x, t_host) -> x
+
+_MOE_PREFIXES = ("mlp.", "post_attention_layernorm.")
+
+
+def _short(name: str, layer: Any) -> str:
+    prefix = layer.metadata.get("full_prefix", "") if hasattr(layer, "metadata") else ""
+    return name[len(prefix):] if prefix and name.startswith(prefix) else name
+
+
+def is_moe_tensor(short_name: str) -> bool:
+    return short_name.startswith(_MOE_PREFIXES)
+
+
+class DeviceMoeExecutor:
+    """Common machinery; subclasses set the config parser and the block layout."""
+
+    family = "glm"
+
+    def __init__(self, config: dict[str, Any], *, score_func: str | None = None,
+                 weight_format: str = "f16", max_tokens: int = 4096, device: int = 0,
+                 resident: bool = True, attention: AttentionFn | None = None,
+                 dense_mlp: DenseFn | None = None) -> None:
+        self.config = dict(config)
+        self.weight_format = weight_format
+        self.max_tokens = max_tokens
+        self.device = device
+        self.resident = resident
+        self.attention = attention
+        self.dense_mlp = dense_mlp
+        overrides: dict[str, Any] = dict(weight_format=weight_format, max_tokens=max_tokens,
+                                         device=device)
+        if score_func is not None:
+            overrides["score_func"] = score_func
+        self.moe_config = self._parse(self.config, overrides)
+        self._bound: dict[Any, MoeLayer] = {}
+
+    # -- overridden by the families --------------------------------------------------
+    def _parse(self, config: dict[str, Any], overrides: dict[str, Any]) -> MoeLayerConfig:
+        raise NotImplementedError
+
+    def _is_moe_layer(self, layer: Any) -> bool:
+        return True
+
+    # -- binding ---------------------------------------------------------------------
+    def _layer_config(self, tensor_meta: list[dict[str, Any]]) -> MoeLayerConfig:
+        shp = layer_shapes(tensor_meta)
+        return self.moe_config.with_shapes(shp["inter"] or self.moe_config.inter,
+                                           shp["shared_inter"], shp["has_shared_gate"])
+
+    def bind_device_blob(self, key: Any, blob_ptr: int, blob_bytes: int,
+                         tensor_meta: list[dict[str, Any]], stream: Any = None) -> MoeLayer:
+        """Pack the MoE tensors of a device-resident layer blob (cached under ``key``)."""
+        if self.resident and key in self._bound:
+            return self._bound[key]
+        ml = MoeLayer(self._layer_config(tensor_meta))
+        ml.bind_device(blob_ptr, blob_bytes, tensor_meta, stream)
+        if self.resident:
+            self._bound[key] = ml
+        return ml
+
+    def bind_tensors(self, t: dict[str, Any], expert_format: str = "float32") -> MoeLayer:
+        """Pack a dict of host arrays (reference tensor names) and bind it."""
+        moe_t = {k: np.asarray(v) for k, v in t.items() if is_moe_tensor(k)}
+        blob, meta = pack_layer(moe_t, expert_format=expert_format)
+        ml = MoeLayer(self._layer_config(meta))
+        ml.bind_host(blob, meta)
+        return ml
+
+    def evict(self, key: Any) -> None:
+        ml = self._bound.pop(key, None)
+        if ml is not None:
+            ml.close()
+
+    # -- the block -------------------------------------------------------------------
+    def _moe_mlp_block(self, x: Any, t: Any) -> Any:
+        """``x + MoE(rms_norm(x))`` on the device; same contract as the reference."""
+        if isinstance(t, MoeLayer):
+            ml = t
+        else:
+            key = ("tensors", id(t))
+            ml = self._bound.get(key)
+            if ml is None:
+                ml = self.bind_tensors(t)
+                self._bound[key] = ml
+        if isinstance(x, np.ndarray):
+            return ml.forward_host(x)
+        return ml.forward(x)
+
+    # -- LayerExecutor protocol ----------------------------------------------------------
+    def run_layer(self, layer: Any, activations: Any, device_weights: Any, backend: Any,
+                  stream: Any) -> Any:
+        if getattr(backend, "name", None) != "cuda":
+            raise ValueError("the sm_100a MoE executor runs on the 'cuda' backend only")
+        meta = layer.metadata["tensors"]
+        host_meta = [m for m in meta if not is_moe_tensor(_short(m["name"], layer))]
+        t_host = _read_ranges(backend, device_weights, host_meta, stream) if host_meta else {}
+        x = activations
+        if host_meta:
+            if self.attention is None:
+                raise NotImplementedError(
+                    "layer has attention tensors; pass attention=<callable(layer, x, t)> "
+                    "(e.g. moe_sm100.executors.reference_delegates(ref_executor))")
+            x = self.attention(layer, x, t_host)
+        if self._is_moe_layer(layer):
+            stream_handle = getattr(stream, "value", stream)
+            ml = self.bind_device_blob(layer.layer_id, int(device_weights.handle),
+                                       int(device_weights.nbytes),
+                                       [dict(m, name=_short(m["name"], layer)) for m in meta],
+                                       stream_handle)
+            x = self._moe_mlp_block(x, ml)
+        else:
+            if self.dense_mlp is None:
+                raise NotImplementedError("dense layer: pass dense_mlp=<callable(x, t)>")
+            t_all = _read_ranges(backend, device_weights, meta, stream)
+            x = self.dense_mlp(x, t_all)
+        return x
+
+
+def _read_ranges(backend: Any, buf: Any, metas: list[dict[str, Any]], stream: Any) -> dict[str, Any]:
+    """Read only the listed tensors of a device blob back to host numpy arrays."""
+    out: dict[str, Any] = {}
+    for m in metas:
+        dt = np.dtype("float32" if m["dtype"] in ("float32", "<f4") else
+                      "float16" if m["dtype"] in ("float16", "<f2") else
+                      "int8" if m["dtype"] in ("int8", "|i1") else "uint16")
+        host = np.empty(int(m["nbytes"]), dtype=np.uint8)
+        backend.copy_d2h_range(host, buf, int(m["offset"]), int(m["nbytes"]), stream)
+        backend.synchronize_stream(stream)
+        arr = host.view(dt).reshape(m["shape"])
+        if dt == np.uint16:  # bfloat16 bits -> fp32, as the reference storage does
+            arr = (arr.astype(np.uint32) << 16).view(np.float32)
+        out[m["name"]] = arr
+    return out
+
+
+def reference_delegates(ref_executor: Any) -> dict[str, Any]:
+    """``attention=`` / ``dense_mlp=`` callables built from a reference executor instance.
+
+    GLM-4 MoE: ``_attention_block`` (glm4_moe.py:112) and ``_dense_mlp_block`` (:166).
+    Qwen3-Next: ``_full_attn_block`` / ``_linear_attn_block`` by ``metadata["attn_type"]``
+    (qwen3_next.py:149-154).
+    """
+    def _strip(layer: Any, t: dict[str, Any]) -> dict[str, Any]:
+        return {_short(k, layer): v for k, v in t.items()}
+
+    if hasattr(ref_executor, "_attention_block"):
+        def attention(layer: Any, x: Any, t: dict[str, Any]) -> Any:
+            return ref_executor._attention_block(x, _strip(layer, t))
+    else:
+        def attention(layer: Any, x: Any, t: dict[str, Any]) -> Any:
+            if layer.metadata.get("attn_type", "linear") == "full":
+                return ref_executor._full_attn_block(x, _strip(layer, t))
+            return ref_executor._linear_attn_block(x, _strip(layer, t))
+    dense = getattr(ref_executor, "_dense_mlp_block", None)
+    return {"attention": attention, "dense_mlp": dense}

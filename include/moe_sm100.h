@@ -1,0 +1,162 @@
+/*
+ * libmoe_sm100 -- C ABI of the B200 (sm_100a) MoE feed-forward block.
+ *
+ * Drop-in device path for the sparse expert layer of disk-mem-off's NumPy
+ * executors.  Plain pointers, sizes and int status codes only: every entry
+ * point returns MOE_OK (0) or an MOE_ERR_* code and never aborts; the text of
+ * the last error of the calling thread is available from moe_last_error().
+ * Device pointers are CUDA global-memory addresses; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  All compute calls are
+ * stream-ordered and asynchronous.
+ *
+ * Reference interfaces replaced (paths inside the disk-mem-off project):
+ *   moe_forward      -> GLM4MoeExecutor._moe_mlp_block
+ *                       offload_runtime/executors/glm4_moe.py:176-240, and
+ *                       Qwen3NextExecutor._moe_mlp_block
+ *                       offload_runtime/executors/qwen3_next.py:273-333
+ *   moe_route        -> the router / top-k / dispatch part of the same functions
+ *                       (glm4_moe.py:177-215, qwen3_next.py:274-305)
+ *   moe_bind_layer   -> _unpack_tensors(_readback_device(...), metadata["tensors"])
+ *                       offload_runtime/executors/_common.py:20-58, without the
+ *                       device->host readback: weights stay in HBM
+ *   moe_plan_create  -> GLM4MoeExecutor.__init__ / Qwen3NextExecutor.__init__
+ *                       config parsing (glm4_moe.py:70-84, qwen3_next.py:105-133)
+ *   moe_rt_*         -> CUDABackend (offload_runtime/backends/cuda_backend.py:35-128)
+ */
+#ifndef MOE_SM100_H_
+#define MOE_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- status */
+enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID = 1,        /* bad argument (ValueError in the reference)          */
+  MOE_ERR_CUDA = 2,           /* CUDA runtime/driver error (RuntimeError)            */
+  MOE_ERR_UNSUPPORTED = 3,    /* shape or format outside what the kernels cover      */
+  MOE_ERR_MISSING_TENSOR = 4, /* a required layer tensor is absent (KeyError)        */
+  MOE_ERR_WORKSPACE = 5,      /* workspace too small                                 */
+  MOE_ERR_NOT_BOUND = 6,      /* forward before moe_bind_layer                       */
+  MOE_ERR_DEVICE = 7,         /* a kernel reported an error (bad tile / route)       */
+  MOE_ERR_TIMEOUT = 8,        /* a bounded device-side wait ran out of time          */
+  MOE_ERR_RANGE = 9           /* weight value not representable in the packed format */
+};
+
+/* router scoring */
+enum {
+  MOE_SCORE_SOFTMAX = 0, /* softmax(logits (+ bias)), rank + weight by prob: the
+                            reference rule (glm4_moe.py:181-195, qwen3_next.py:278-289) */
+  MOE_SCORE_SIGMOID = 1  /* HF GLM-4.x: sigmoid(logits); select on score + bias;
+                            weights are the unbiased scores                           */
+};
+
+/* on-device weight format */
+enum {
+  MOE_WEIGHTS_F16 = 0,     /* 16-bit expert weights (bf16 values re-encoded as f16)  */
+  MOE_WEIGHTS_INT8_PC = 1  /* int8 per output row + scale (fp16 in the blob)          */
+};
+
+typedef struct MoePlan MoePlan;
+
+typedef struct MoeConfig {
+  int32_t hidden;                /* H  (hidden_size)                                  */
+  int32_t n_experts;             /* E  (n_routed_experts / num_experts)               */
+  int32_t top_k;                 /* K  (num_experts_per_tok)                          */
+  int32_t inter;                 /* I  (moe_intermediate_size)                        */
+  int32_t shared_inter;          /* SI (shared expert intermediate; 0 = none)         */
+  int32_t score_func;            /* MOE_SCORE_*                                       */
+  int32_t norm_topk_prob;        /* renormalise the top-k weights                     */
+  int32_t use_bias;              /* add mlp.gate.e_score_correction_bias if bound     */
+  int32_t has_shared_gate;       /* Qwen3 sigmoid(h . w_gate) on the shared expert    */
+  int32_t weight_format;         /* MOE_WEIGHTS_*                                     */
+  float routed_scaling_factor;   /* 2.5 for GLM-4.x, 1.0 for Qwen3                    */
+  float rms_norm_eps;            /* post_attention_layernorm epsilon                  */
+  int32_t max_tokens;            /* largest T a forward may be called with            */
+  int32_t expert_begin;          /* locally resident routed experts [begin, end);    */
+  int32_t expert_end;            /*   0,0 = all experts                               */
+  int32_t device;                /* CUDA device ordinal                               */
+} MoeConfig;
+
+/* One entry of LayerSpec.metadata["tensors"]
+ * (offload_runtime/loader/huggingface.py:492-506, 560-575). */
+typedef struct MoeTensorDesc {
+  const char* name;   /* e.g. "mlp.experts.3.gate_proj.weight"; a "model.layers.N."
+                         prefix is accepted; scales of int8 tensors are named
+                         "<weight name>_scale" (fp16, one per output row)        */
+  const char* dtype;  /* "float32" | "float16" | "bfloat16" | "int8"              */
+  int64_t shape[2];
+  int32_t ndim;
+  int64_t offset;     /* byte offset inside the layer blob                        */
+  int64_t nbytes;
+} MoeTensorDesc;
+
+/* ------------------------------------------------------------ plan / bind */
+int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan);
+int moe_plan_destroy(MoePlan* plan);
+
+/* Pack the MoE tensors of one layer blob (already in device memory) into the
+ * plan's HBM-resident layout.  The blob may be freed afterwards.  Tensors that
+ * are not part of the MoE block (attention, input norm) are ignored. */
+int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
+                   const MoeTensorDesc* descs, int32_t n_descs, void* stream);
+
+/* Bytes of device memory the plan holds for packed weights. */
+uint64_t moe_plan_weight_bytes(const MoePlan* plan);
+
+/* ---------------------------------------------------------------- compute */
+/* Scratch bytes a forward / route of T tokens needs (256-byte aligned base). */
+uint64_t moe_workspace_bytes(const MoePlan* plan, int32_t T);
+
+/* out[T,H] = x + MoE(rms_norm(x)) on fp32 device buffers (x and out may not alias). */
+int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
+                void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* moe_forward plus device time per stage, measured with CUDA events on `stream`:
+ * stage_ms[0] route (RMSNorm, router, top-k, permutation + dispatch gather),
+ * stage_ms[1] gate/up grouped GEMM, stage_ms[2] down grouped GEMM,
+ * stage_ms[3] combine.  Synchronises `stream` before returning. */
+int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
+                      void* workspace, uint64_t workspace_bytes, float* stage_ms, void* stream);
+
+/* Router + permutation only (for parity tests and expert-parallel dispatch):
+ *   topk_ids [T,K] int32, topk_w [T,K] f32, expert_offsets [E+1] int32,
+ *   perm [T*K] int32 with perm[r] = t*K + slot listing rows expert-major,
+ *   tokens ascending inside an expert.  Any output pointer may be NULL. */
+int moe_route(MoePlan* plan, const float* x_dev, int32_t T, int32_t* topk_ids, float* topk_w,
+              int32_t* expert_offsets, int32_t* perm, void* workspace,
+              uint64_t workspace_bytes, void* stream);
+
+/* Synchronise `stream`, then read and clear the device error word of the plan.
+ * Returns MOE_OK, MOE_ERR_TIMEOUT or MOE_ERR_DEVICE. */
+int moe_status(MoePlan* plan, void* stream);
+
+const char* moe_last_error(void);
+const char* moe_version(void);
+
+/* ------------------------------------------- runtime (CUDABackend, ctypes) */
+int moe_rt_device_count(int32_t* count);
+int moe_rt_set_device(int32_t device);
+int moe_rt_malloc(uint64_t nbytes, void** dev_ptr);
+int moe_rt_free(void* dev_ptr);
+int moe_rt_malloc_host(uint64_t nbytes, void** host_ptr);
+int moe_rt_free_host(void* host_ptr);
+int moe_rt_stream_create(void** stream);        /* non-blocking stream */
+int moe_rt_stream_destroy(void* stream);
+int moe_rt_memcpy_h2d_async(void* dst_dev, const void* src_host, uint64_t nbytes, void* stream);
+int moe_rt_memcpy_d2h_async(void* dst_host, const void* src_dev, uint64_t nbytes, void* stream);
+int moe_rt_memcpy_d2d_async(void* dst_dev, const void* src_dev, uint64_t nbytes, void* stream);
+int moe_rt_event_record(void* stream, void** event); /* creates + records */
+int moe_rt_event_destroy(void* event);
+int moe_rt_stream_wait_event(void* stream, void* event);
+int moe_rt_stream_synchronize(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_SM100_H_ */

@@ -1,0 +1,211 @@
+"""Host-side logic of moe_sm100 that needs no GPU: packing, formats, config parsing,
+dequantizers (mirroring the reference's tests/test_quantize.py known answers),
+residency pool and executor guards."""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+import pytest
+import torch
+
+from moe_sm100.buffer_pool import DeviceBufferPool, ResidentLayerPool
+from moe_sm100.config import MoeLayerConfig
+from moe_sm100.layer import _descs, layer_shapes
+from moe_sm100.packing import (bf16_bits, bf16_to_f32, dequantize_int8_per_channel, is_expert_weight,
+                               pack_layer, quantize_int8_per_channel)
+from moe_sm100.quantize import (CompositeDequantizer, Float16Dequantizer, Int8Dequantizer,
+                                Int8PerChannelDequantizer)
+from moe_sm100.types import DeviceBuffer, HostBuffer, LayerSpec
+from oracle.moe_oracle import bf16_round, int8_pc_quantize
+
+
+# ------------------------------------------------------------------ formats
+def test_bf16_bits_match_torch_rounding() -> None:
+    rng = np.random.default_rng(0)
+    a = (rng.standard_normal(10000) * 10.0 ** rng.integers(-8, 8, 10000)).astype(np.float32)
+    a[:4] = [0.0, -0.0, np.inf, -np.inf]
+    ours = bf16_bits(a)
+    ref = torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(ours, ref)
+    np.testing.assert_array_equal(bf16_to_f32(ours), bf16_round(a))
+
+
+def test_int8_quantizer_matches_oracle_format() -> None:
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((64, 96)) * 0.02).astype(np.float32)
+    w[3] = 0.0
+    q, s = quantize_int8_per_channel(w)
+    q2, s2 = int8_pc_quantize(w)
+    np.testing.assert_array_equal(q, q2)
+    np.testing.assert_array_equal(s.view(np.uint16), s2.view(np.uint16))
+    assert np.all(q[3] == 0) and s[3] == 0
+    assert np.abs(q).max() == 127
+    err = np.abs(dequantize_int8_per_channel(q, s) - w)
+    assert np.all(err <= s.astype(np.float32)[:, None] * 0.5 + 1e-6)
+
+
+def test_expert_weight_names() -> None:
+    assert is_expert_weight("mlp.experts.12.gate_proj.weight")
+    assert is_expert_weight("model.layers.3.mlp.experts.0.down_proj.weight")
+    assert is_expert_weight("mlp.shared_experts.up_proj.weight")
+    assert is_expert_weight("mlp.shared_expert.down_proj.weight")
+    assert not is_expert_weight("mlp.gate.weight")
+    assert not is_expert_weight("mlp.shared_expert_gate.weight")
+    assert not is_expert_weight("self_attn.q_proj.weight")
+
+
+@pytest.mark.parametrize("fmt", ["float32", "bfloat16", "int8"])
+def test_pack_layer_roundtrip(fmt: str) -> None:
+    rng = np.random.default_rng(2)
+    t = {
+        "post_attention_layernorm.weight": np.ones(32, np.float32),
+        "mlp.gate.weight": rng.standard_normal((4, 32)).astype(np.float32),
+        "mlp.experts.0.gate_proj.weight": (rng.standard_normal((16, 32)) * 0.02).astype(np.float32),
+        "mlp.experts.0.down_proj.weight": (rng.standard_normal((32, 16)) * 0.02).astype(np.float32),
+    }
+    blob, meta = pack_layer(t, expert_format=fmt)
+    names = [m["name"] for m in meta]
+    assert names == sorted(names)  # loader order (huggingface.py:492-506)
+    by = {m["name"]: m for m in meta}
+    for m in meta:
+        assert m["offset"] % 256 == 0
+    router = np.frombuffer(blob, np.float32, count=4 * 32, offset=by["mlp.gate.weight"]["offset"])
+    np.testing.assert_array_equal(router.reshape(4, 32), t["mlp.gate.weight"])
+    m = by["mlp.experts.0.gate_proj.weight"]
+    assert m["dtype"] == {"float32": "float32", "bfloat16": "bfloat16", "int8": "int8"}[fmt]
+    if fmt == "int8":
+        assert "mlp.experts.0.gate_proj.weight_scale" in by
+        s = by["mlp.experts.0.gate_proj.weight_scale"]
+        assert s["dtype"] == "float16" and s["shape"] == [16]
+    d, keep = _descs(meta)
+    assert len(d) == len(meta) and d[0].name == meta[0]["name"].encode()
+
+
+# ------------------------------------------------------------------ config
+def test_glm_config_defaults_follow_reference() -> None:
+    c = MoeLayerConfig.glm4_moe({"hidden_size": 5120, "moe_intermediate_size": 1536})
+    assert (c.n_experts, c.top_k, c.routed_scaling_factor, c.rms_norm_eps) == (160, 8, 2.5, 1e-5)
+    assert c.norm_topk_prob and c.use_bias and not c.has_shared_gate
+    assert c.score_func == "softmax"
+    s = MoeLayerConfig.glm4_moe({"hidden_size": 8}, score_func="sigmoid")
+    assert s.score_func == "sigmoid"
+    cc = c.to_c()
+    assert cc.hidden == 5120 and cc.n_experts == 160 and abs(cc.routed_scaling_factor - 2.5) < 1e-7
+
+
+def test_qwen3_config_defaults_follow_reference() -> None:
+    c = MoeLayerConfig.qwen3_next({"hidden_size": 2048})
+    assert (c.n_experts, c.top_k, c.inter, c.shared_inter) == (512, 10, 512, 512)
+    assert c.routed_scaling_factor == 1.0 and not c.use_bias and c.has_shared_gate
+    c2 = MoeLayerConfig.qwen3_next({"hidden_size": 64, "n_routed_experts": 32})
+    assert c2.n_experts == 32
+    with pytest.raises(ValueError):
+        MoeLayerConfig.qwen3_next({"hidden_size": 64}, score_func="relu").to_c()
+
+
+def test_layer_shapes_from_metadata() -> None:
+    meta = [{"name": "mlp.experts.0.gate_proj.weight", "shape": [96, 64]},
+            {"name": "mlp.shared_expert.gate_proj.weight", "shape": [48, 64]},
+            {"name": "mlp.shared_expert_gate.weight", "shape": [1, 64]}]
+    assert layer_shapes(meta) == {"inter": 96, "shared_inter": 48, "has_shared_gate": True}
+
+
+# ------------------------------------------------------------------ dequantizers
+def test_scalar_int8_dequantizer_known_answers() -> None:
+    d = Int8Dequantizer()
+    layer = LayerSpec(0, "L0", 2, {"dtype": "int8", "scale": 0.5, "zero_point": 0})
+    out = d.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("2b", 4, -2)))))
+    assert struct.unpack("2f", out.view.tobytes()) == (2.0, -1.0)
+    layer = LayerSpec(0, "L0", 1, {"dtype": "int8", "scale": 1.0, "zero_point": 10})
+    out = d.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("1b", 15)))))
+    assert struct.unpack("1f", out.view.tobytes()) == (5.0,)
+    assert d.decompressed_nbytes(LayerSpec(0, "L0", 100, {"dtype": "int8"})) == 400
+
+
+def test_float16_and_composite_dequantizers() -> None:
+    f = Float16Dequantizer()
+    layer = LayerSpec(0, "L0", 4, {"dtype": "float16"})
+    out = f.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("2e", 1.0, 2.0)))))
+    assert struct.unpack("2f", out.view.tobytes()) == (1.0, 2.0)
+    c = CompositeDequantizer()
+    plain = LayerSpec(0, "L0", 16)
+    buf = HostBuffer(memoryview(bytearray(16)))
+    assert not c.needs_dequantize(plain) and c.dequantize(plain, buf) is buf
+    assert c.decompressed_nbytes(LayerSpec(0, "L0", 4, {"dtype": "int8", "scale": 1.0})) == 16
+
+
+def test_per_channel_dequantizer_keeps_blob_compressed_by_default() -> None:
+    rng = np.random.default_rng(3)
+    t = {"mlp.experts.0.up_proj.weight": (rng.standard_normal((16, 32)) * 0.02).astype(np.float32),
+         "mlp.gate.weight": rng.standard_normal((2, 32)).astype(np.float32)}
+    blob, meta = pack_layer(t, expert_format="int8")
+    layer = LayerSpec(0, "L0", len(blob), {"dtype": "int8_per_channel", "tensors": meta})
+    keep = Int8PerChannelDequantizer()
+    assert not keep.needs_dequantize(layer)
+    assert not CompositeDequantizer().needs_dequantize(layer)
+    host = Int8PerChannelDequantizer(keep_on_device=False)
+    assert host.needs_dequantize(layer)
+    out = host.dequantize(layer, HostBuffer(memoryview(blob)))
+    om = {m["name"]: m for m in layer.metadata["dequantized_tensors"]}
+    m = om["mlp.experts.0.up_proj.weight"]
+    w = np.frombuffer(out.view, np.float32, count=16 * 32, offset=m["offset"]).reshape(16, 32)
+    q, s = quantize_int8_per_channel(t["mlp.experts.0.up_proj.weight"])
+    np.testing.assert_array_equal(w, dequantize_int8_per_channel(q, s))
+
+
+# ------------------------------------------------------------------ residency
+class _FakeBackend:
+    name = "fake"
+
+    def __init__(self) -> None:
+        self.live: set[int] = set()
+        self.n = 0
+
+    def alloc_device(self, nbytes: int) -> DeviceBuffer:
+        self.n += 1
+        self.live.add(self.n)
+        return DeviceBuffer(handle=self.n, nbytes=nbytes, backend=self.name)
+
+    def free_device(self, buf: DeviceBuffer) -> None:
+        self.live.remove(buf.handle)
+
+
+def test_buffer_pool_reuses_by_size() -> None:
+    be = _FakeBackend()
+    pool = DeviceBufferPool(be)
+    a = pool.acquire(10)
+    pool.release(a)
+    assert pool.acquire(10) is a
+    pool.release(a)
+    pool.drain()
+    assert not be.live
+
+
+def test_resident_pool_budget_and_lru_eviction() -> None:
+    be = _FakeBackend()
+    evicted: list[int] = []
+    pool = ResidentLayerPool(be, budget_bytes=100, on_evict=evicted.append)
+    for lid in range(3):
+        assert pool.admit(lid, be.alloc_device(40))
+    assert evicted == [0] and pool.resident_bytes == 80
+    pool.get(1)  # touch -> 2 is now the oldest
+    assert pool.admit(3, be.alloc_device(40))
+    assert evicted == [0, 2] and pool.is_resident(1) and pool.is_resident(3)
+    assert not pool.admit(9, DeviceBuffer(handle=-1, nbytes=101, backend="fake"))
+    pool.drain()
+    assert not be.live and pool.resident_bytes == 0
+
+
+def test_executor_rejects_non_cuda_backend() -> None:
+    from moe_sm100.executors import GLM4MoeExecutor
+    ex = GLM4MoeExecutor({"hidden_size": 256, "moe_intermediate_size": 64, "n_routed_experts": 8,
+                          "num_experts_per_tok": 2})
+    assert ex.num_experts_per_tok == 2 and ex.routed_scaling_factor == 2.5
+    layer = LayerSpec(1, "model.layers.1", 0, {"tensors": [], "is_moe": True})
+
+    class _Null:
+        name = "null"
+
+    with pytest.raises(ValueError):
+        ex.run_layer(layer, np.zeros((1, 256), np.float32), DeviceBuffer(0, 0, "null"), _Null(), None)
