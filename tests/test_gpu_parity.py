@@ -156,7 +156,11 @@ def _check_routing(ml, lazy, ocfg, x) -> int:  # noqa: ANN001
     for e in range(ocfg.n_experts):
         seg = perm[offs[e]:offs[e + 1]]
         assert np.all(np.diff(seg) > 0)  # tokens ascending inside an expert
-    np.testing.assert_allclose(r["topk_w"].cpu().numpy()[got == ids], w[got == ids], rtol=1e-5)
+    # Router weights: both sides are fp32, but the 5120-term logit sums are added in a
+    # different order (OpenBLAS blocking vs warp-strided partial sums), ~4e-6 absolute in
+    # a logit of magnitude ~1.4; through exp and the renormalisation that is up to ~1e-5
+    # relative in a weight, so the full-size bound is 5e-5 (1e-5 holds at H <= 1024).
+    np.testing.assert_allclose(r["topk_w"].cpu().numpy()[got == ids], w[got == ids], rtol=5e-5)
     return flips
 
 
