@@ -212,10 +212,6 @@ static size_t dtype_size(int d) { return d == SRC_F32 ? 4 : (d == SRC_I8 ? 1 : 2
 // ====================================================================== C ABI
 using namespace moe;
 
-struct MoePlan {
-  Plan p;
-};
-
 extern "C" {
 
 const char* moe_last_error(void) { return g_last_error.c_str(); }

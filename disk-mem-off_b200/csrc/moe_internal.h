@@ -109,3 +109,8 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool int8, uint64_t inner,
 void set_error(const std::string& msg);
 
 }  // namespace moe
+
+// The opaque handle of the C ABI wraps one plan.
+struct MoePlan {
+  moe::Plan p;
+};

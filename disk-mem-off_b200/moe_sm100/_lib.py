@@ -23,6 +23,8 @@ MOE_ERR_DEVICE = 7
 MOE_ERR_TIMEOUT = 8
 MOE_ERR_RANGE = 9
 
+MOE_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024  # include/moe_sm100.h
+
 MOE_SCORE_SOFTMAX = 0
 MOE_SCORE_SIGMOID = 1
 MOE_WEIGHTS_F16 = 0
@@ -72,6 +74,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_uint64, c_void_p]),
     "moe_forward_timed": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_uint64,
                                     POINTER(c_float), c_void_p]),
+    "moe_forward_static_scratch": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p]),
     "moe_route": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_uint64, c_void_p]),
     "moe_status": (c_int32, [c_void_p, c_void_p]),

@@ -123,6 +123,30 @@ int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
 int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
                       void* workspace, uint64_t workspace_bytes, float* stage_ms, void* stream);
 
+/* Size of the library-owned scratch used by moe_forward_static_scratch. */
+#define MOE_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* moe_forward for callers that cannot allocate device memory (no counterpart in
+ * the reference).  Some callers only own the buffers they pass in: a Go / Java /
+ * C host reached through a thin FFI, a process whose memory pool has already
+ * claimed the GPU, or a serving loop that must not call cudaMalloc because it
+ * synchronises the device.  This entry point allocates nothing: it runs the same
+ * kernels as moe_forward with a 32 MiB scratch array that lives in the library
+ * (MOE_STATIC_SCRATCH_BYTES; every GPU that loads the library holds it until the
+ * process exits).
+ *   - The caller passes x and out as for moe_forward.
+ *   - The first call on a device looks up the scratch's device address (once per
+ *     device, with the plan's device current); make that first call before any
+ *     stream capture.
+ *   - A T whose moe_workspace_bytes(T) exceeds MOE_STATIC_SCRATCH_BYTES is
+ *     rejected with MOE_ERR_WORKSPACE (for the GLM-4.7 shape, T <= 64 fits).
+ *   - All calls in the process share the one scratch array and it keeps the last
+ *     call's contents: calls that overlap on the GPU (different streams, or
+ *     different plans on the same device at the same time) race and corrupt each
+ *     other's results.  Serialise them. */
+int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T,
+                               void* stream);
+
 /* Router + permutation only (for parity tests and expert-parallel dispatch):
  *   topk_ids [T,K] int32, topk_w [T,K] f32, expert_offsets [E+1] int32,
  *   perm [T*K] int32 with perm[r] = t*K + slot listing rows expert-major,
