@@ -233,7 +233,7 @@ def run_ours(args) -> None:  # noqa: ANN001
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
 
     results = {}
-    for T in sorted({1, 8, T_main}):
+    for T in (sorted({1, 8, T_main}) if not args.no_sub else [T_main]):
         x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
         out = torch.empty_like(x)
         ws = ml.workspace(T)
@@ -268,13 +268,15 @@ def run_ours(args) -> None:  # noqa: ANN001
 
     # end-to-end through the host-buffer call
     x_host = main["x"].cpu().numpy()
-    for _ in range(args.warmup):
-        ml.forward_host(x_host)
-    _barrier(world)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        ml.forward_host(x_host)
-    e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    e2e_s = float("nan")
+    if not args.no_e2e:
+        for _ in range(args.warmup):
+            ml.forward_host(x_host)
+        _barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ml.forward_host(x_host)
+        e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -396,9 +398,14 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-sub", action="store_true", help="only the --tokens batch (no T=1/8 lines)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
+    ap.add_argument("--experts", type=int, default=160,
+                    help="routed experts (profiling uses fewer to stay within a few GB)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    GLM["n_experts"] = args.experts
     if args.impl == "reference":
         run_reference(args)
     else:

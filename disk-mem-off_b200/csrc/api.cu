@@ -111,7 +111,7 @@ WsLayout ws_layout(const Plan& p, int T) {
   L.act_s = take(static_cast<size_t>(T) * p.SI * 2);
   L.y = take(R * p.H * 4);
   L.y_s = take(p.SI > 0 ? static_cast<size_t>(T) * p.H * 4 : 0);
-  L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
+  L.logits = take(static_cast<size_t>(router_splits(p, T)) * T * p.router_rows * 4);
   L.ids = take(R * 4);
   L.wts = take(R * 4);
   L.sgate = take(static_cast<size_t>(T) * 4);

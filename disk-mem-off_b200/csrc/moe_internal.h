@@ -73,6 +73,8 @@ WsLayout ws_layout(const Plan& p, int T);
 // ------------------------------------------------------------ launchers
 cudaError_t launch_rmsnorm(const Plan& p, const float* x, float* h32, __half* h16, int T,
                            cudaStream_t s);
+// logits holds router_splits(p, T) partial slices of [T][router_rows] fp32
+int router_splits(const Plan& p, int T);
 cudaError_t launch_router(const Plan& p, const float* h32, float* logits, int T, cudaStream_t s);
 cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float* wts,
                         float* sgate, int T, cudaStream_t s);

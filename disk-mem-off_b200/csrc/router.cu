@@ -64,100 +64,89 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
 }
 
 // ------------------------------------------------------------------ router
-// Decode: one warp per router row, all (<= 16) tokens at once; float4 weight
-// streaming, per-lane strided partial sums, shuffle-tree reduction.
-constexpr int kGemvMaxT = 16;
+// logits = h32 @ Wr^T in fp32, split along K.  CTA (rx, s, ty) computes router
+// rows [32 rx, 32 rx + 32) x tokens [BT ty, BT ty + BT) over its K range, in
+// chunks of 128: the whole chunk of both operands is requested with cp.async at
+// once (so a decode step pays one memory latency, not one per k-step), then
+// each thread accumulates TPT x EPT outputs reading float4s along K.  Partial
+// sums go to part[s][t][r]; the top-k kernel adds the S slices in order s = 0..S-1,
+// so the result is deterministic.
+constexpr int kRouterKc = 128;      // K elements per chunk
+constexpr int kRouterRows = 32;     // router rows per CTA
+constexpr int kRouterPad = 4;       // smem row padding (floats)
 
-__global__ void __launch_bounds__(256) router_gemv_kernel(const float* __restrict__ h32,
-                                                          const float* __restrict__ wr,
-                                                          float* __restrict__ logits, int T,
-                                                          int H, int R) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 8 + warp;
-  if (r >= R) return;
-  float acc[kGemvMaxT];
-#pragma unroll
-  for (int t = 0; t < kGemvMaxT; ++t) acc[t] = 0.f;
-  const float4* wrow = reinterpret_cast<const float4*>(wr + static_cast<size_t>(r) * H);
-  const int nv = H >> 2;
-  for (int k = lane; k < nv; k += 32) {
-    const float4 wv = __ldg(wrow + k);
-#pragma unroll
-    for (int t = 0; t < kGemvMaxT; ++t) {
-      if (t < T) {
-        const float4 hv = __ldg(reinterpret_cast<const float4*>(h32 + static_cast<size_t>(t) * H) + k);
-        float a = acc[t];
-        a = fmaf(hv.x, wv.x, a);
-        a = fmaf(hv.y, wv.y, a);
-        a = fmaf(hv.z, wv.z, a);
-        a = fmaf(hv.w, wv.w, a);
-        acc[t] = a;
-      }
-    }
-  }
-#pragma unroll
-  for (int t = 0; t < kGemvMaxT; ++t) {
-    if (t < T) {
-      float v = acc[t];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) logits[static_cast<size_t>(t) * R + r] = v;
-    }
-  }
+MOE_DEV void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
 }
 
-// Prefill: 64 tokens x 64 router rows per CTA, k-blocks of 16, 4x4 outputs per
-// thread (fp32 FMA on CUDA cores).
-__global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restrict__ h32,
-                                                          const float* __restrict__ wr,
-                                                          float* __restrict__ logits, int T,
-                                                          int H, int R) {
-  __shared__ __align__(16) float As[16][64];
-  __shared__ __align__(16) float Bs[16][64];
+template <int BT>
+__global__ void __launch_bounds__(256) router_splitk_kernel(const float* __restrict__ h32,
+                                                            const float* __restrict__ wr,
+                                                            float* __restrict__ part, int T,
+                                                            int H, int R, int k_per_split) {
+  constexpr int EPT = (BT == 64) ? 4 : 2;     // router rows per thread
+  constexpr int XT = kRouterRows / EPT;       // threads along rows
+  constexpr int YT = 256 / XT;                // threads along tokens
+  constexpr int TPT = BT / YT;                // tokens per thread
+  constexpr int LD = kRouterKc + kRouterPad;  // smem row stride (floats)
+  extern __shared__ __align__(16) float rsm[];
+  float* hs = rsm;                 // [BT][LD]
+  float* ws = rsm + BT * LD;       // [32][LD]
+  const int r0 = blockIdx.x * kRouterRows;
+  const int t0 = blockIdx.z * BT;
+  const int kb = blockIdx.y * k_per_split;
+  const int ke = min(H, kb + k_per_split);
   const int tid = threadIdx.x;
-  const int t0 = blockIdx.y * 64, r0 = blockIdx.x * 64;
-  const int ty = tid >> 4, tx = tid & 15;
-  const int lrow = tid >> 2, lk = (tid & 3) * 4;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < H; k0 += 16) {
-    {
-      const int t = t0 + lrow;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t < T) v = __ldg(reinterpret_cast<const float4*>(h32 + static_cast<size_t>(t) * H + k0 + lk));
-      As[lk + 0][lrow] = v.x;
-      As[lk + 1][lrow] = v.y;
-      As[lk + 2][lrow] = v.z;
-      As[lk + 3][lrow] = v.w;
-      const int r = r0 + lrow;
-      float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < R) u = __ldg(reinterpret_cast<const float4*>(wr + static_cast<size_t>(r) * H + k0 + lk));
-      Bs[lk + 0][lrow] = u.x;
-      Bs[lk + 1][lrow] = u.y;
-      Bs[lk + 2][lrow] = u.z;
-      Bs[lk + 3][lrow] = u.w;
+  const int ty = tid / XT, tx = tid % XT;
+  float acc[TPT][EPT] = {};
+  for (int k0 = kb; k0 < ke; k0 += kRouterKc) {
+    const int kn = min(kRouterKc, ke - k0);  // multiple of 16 (H % 16 == 0)
+    const int nv = kn >> 2;                  // float4 per row in this chunk
+    for (int i = tid; i < BT * (kRouterKc / 4); i += 256) {
+      const int row = i / (kRouterKc / 4), v = i % (kRouterKc / 4);
+      float* dst = hs + row * LD + v * 4;
+      if (t0 + row < T && v < nv) cp_async16(dst, h32 + static_cast<size_t>(t0 + row) * H + k0 + v * 4);
+      else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    for (int i = tid; i < kRouterRows * (kRouterKc / 4); i += 256) {
+      const int row = i / (kRouterKc / 4), v = i % (kRouterKc / 4);
+      float* dst = ws + row * LD + v * 4;
+      if (r0 + row < R && v < nv) cp_async16(dst, wr + static_cast<size_t>(r0 + row) * H + k0 + v * 4);
+      else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < kRouterKc; k += 4) {
+      float4 a[TPT], b[EPT];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[4] = {b.x, b.y, b.z, b.w};
+      for (int i = 0; i < TPT; ++i) a[i] = *reinterpret_cast<const float4*>(hs + (ty + YT * i) * LD + k);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int j = 0; j < EPT; ++j) b[j] = *reinterpret_cast<const float4*>(ws + (tx + XT * j) * LD + k);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      for (int i = 0; i < TPT; ++i)
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          float c = acc[i][j];
+          c = fmaf(a[i].x, b[j].x, c);
+          c = fmaf(a[i].y, b[j].y, c);
+          c = fmaf(a[i].z, b[j].z, c);
+          c = fmaf(a[i].w, b[j].w, c);
+          acc[i][j] = c;
+        }
     }
     __syncthreads();
   }
+  float* out = part + static_cast<size_t>(blockIdx.y) * T * R;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty * 4 + i;
+  for (int i = 0; i < TPT; ++i) {
+    const int t = t0 + ty + YT * i;
     if (t >= T) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = r0 + tx * 4 + j;
-      if (r < R) logits[static_cast<size_t>(t) * R + r] = acc[i][j];
+    for (int j = 0; j < EPT; ++j) {
+      const int r = r0 + tx + XT * j;
+      if (r < R) out[static_cast<size_t>(t) * R + r] = acc[i][j];
     }
   }
 }
@@ -166,17 +155,23 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
 // One warp per token.  Lane l holds experts l, l+32, ...  Scores are ranked by
 // (key desc, id asc); weights follow the reference formulas in fp32.
 template <int VPL>
-__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ part,
                                                    const float* __restrict__ bias,
                                                    int32_t* __restrict__ ids_out,
                                                    float* __restrict__ w_out,
                                                    float* __restrict__ sgate, int T, int E,
-                                                   int R, int K, int score_func, int norm,
-                                                   float scale, int* err) {
+                                                   int R, int K, int nsplit, int score_func,
+                                                   int norm, float scale, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  const float* row = logits + static_cast<size_t>(t) * R;
+  // logit of router row r for this token: split-K partials added in split order
+  auto logit = [&](int r) {
+    const float* p = part + static_cast<size_t>(t) * R + r;
+    float v = p[0];
+    for (int q = 1; q < nsplit; ++q) v += p[static_cast<size_t>(q) * T * R];
+    return v;
+  };
   float key[VPL], val[VPL];
   float m = -FLT_MAX;
 #pragma unroll
@@ -185,7 +180,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     key[j] = -FLT_MAX;
     val[j] = 0.f;
     if (e < E) {
-      float l = row[e];
+      float l = logit(e);
       if (score_func == MOE_SCORE_SOFTMAX) {
         if (bias) l = l + bias[e];
         key[j] = l;
@@ -264,7 +259,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
       ids_out[static_cast<size_t>(t) * K + r] = sel_id[r];
       w_out[static_cast<size_t>(t) * K + r] = wv;
     }
-    if (sgate) sgate[t] = sigmoid_f(row[E]);
+    if (sgate) sgate[t] = sigmoid_f(logit(E));
   }
 }
 
@@ -423,16 +418,42 @@ cudaError_t launch_rmsnorm(const Plan& p, const float* x, float* h32, __half* h1
   return cudaGetLastError();
 }
 
+int router_splits(const Plan& p, int T) {
+  const int nchunks = (p.H + kRouterKc - 1) / kRouterKc;
+  const int bt = T <= 16 ? 16 : 64;
+  const int tiles = ((p.router_rows + kRouterRows - 1) / kRouterRows) * ((T + bt - 1) / bt);
+  // enough CTAs to cover the SMs about twice, never more splits than K chunks
+  int s = (2 * p.num_sms + tiles - 1) / tiles;
+  if (s > nchunks) s = nchunks;
+  return s < 1 ? 1 : s;
+}
+
+template <int BT>
+static cudaError_t run_router(const Plan& p, const float* h32, float* part, int T, int S,
+                              cudaStream_t s) {
+  constexpr size_t smem = static_cast<size_t>(BT + kRouterRows) * (kRouterKc + kRouterPad) * sizeof(float);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t a = cudaFuncSetAttribute(router_splitk_kernel<BT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (a != cudaSuccess) return a;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int nchunks = (p.H + kRouterKc - 1) / kRouterKc;
+  const int k_per_split = ((nchunks + S - 1) / S) * kRouterKc;
+  dim3 grid((p.router_rows + kRouterRows - 1) / kRouterRows, S, (T + BT - 1) / BT);
+  router_splitk_kernel<BT><<<grid, 256, smem, s>>>(h32, p.w.router_w, part, T, p.H,
+                                                    p.router_rows, k_per_split);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_router(const Plan& p, const float* h32, float* logits, int T,
                           cudaStream_t s) {
-  const int R = p.router_rows;
-  if (T <= kGemvMaxT) {
-    router_gemv_kernel<<<(R + 7) / 8, 256, 0, s>>>(h32, p.w.router_w, logits, T, p.H, R);
-  } else {
-    dim3 grid((R + 63) / 64, (T + 63) / 64);
-    router_gemm_kernel<<<grid, 256, 0, s>>>(h32, p.w.router_w, logits, T, p.H, R);
-  }
-  return cudaGetLastError();
+  const int S = router_splits(p, T);
+  return T <= 16 ? run_router<16>(p, h32, logits, T, S, s) : run_router<64>(p, h32, logits, T, S, s);
 }
 
 cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float* wts,
@@ -441,9 +462,10 @@ cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float*
   const float* bias = p.cfg.use_bias ? p.w.bias : nullptr;
   float* sg = p.cfg.has_shared_gate ? sgate : nullptr;
   const int grid = (T + 7) / 8;
+  const int nsplit = router_splits(p, T);
 #define MOE_TOPK_CASE(V)                                                                     \
   topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, p.router_rows, p.K,  \
-                                      p.cfg.score_func, p.cfg.norm_topk_prob,                \
+                                      nsplit, p.cfg.score_func, p.cfg.norm_topk_prob,        \
                                       p.cfg.routed_scaling_factor, p.d_err)
   const int vpl = (E + 31) / 32;
   if (vpl <= 1) MOE_TOPK_CASE(1);
