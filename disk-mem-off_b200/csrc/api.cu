@@ -104,14 +104,18 @@ WsLayout ws_layout(const Plan& p, int T) {
     o = align256(o + bytes);
     return at;
   };
-  L.h32 = take(static_cast<size_t>(T) * p.H * 4);
   L.h16 = take(static_cast<size_t>(T) * p.H * 2);
   L.xg = take(R * p.H * 2);
   L.act = take(R * p.I * 2);
   L.act_s = take(static_cast<size_t>(T) * p.SI * 2);
   L.y = take(R * p.H * 4);
   L.y_s = take(p.SI > 0 ? static_cast<size_t>(T) * p.H * 4 : 0);
-  L.logits = take(static_cast<size_t>(router_splits(p, T)) * T * p.router_rows * 4);
+  const RouterGeom g = router_geometry(p, T);
+  L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
+  L.part = take(g.splits > 1 ? static_cast<size_t>(g.splits) * T * p.router_rows * 4 : 0);
+  L.ss_part = take(static_cast<size_t>(g.rx) * g.splits * T * 4);
+  L.rms = take(static_cast<size_t>(T) * 4);
+  L.counters = take(static_cast<size_t>(g.rx) * g.tz * 4);
   L.ids = take(R * 4);
   L.wts = take(R * 4);
   L.sgate = take(static_cast<size_t>(T) * 4);
@@ -510,17 +514,8 @@ static int check_call(const MoePlan* plan, int32_t T, const void* ws, uint64_t w
 }
 
 static int route_impl(Plan& p, const WsLayout& L, char* ws, const float* x, int T,
-                      bool gather, cudaStream_t s) {
-  float* h32 = reinterpret_cast<float*>(ws + L.h32);
-  __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
-  float* logits = reinterpret_cast<float*>(ws + L.logits);
-  int32_t* ids = reinterpret_cast<int32_t*>(ws + L.ids);
-  float* wts = reinterpret_cast<float*>(ws + L.wts);
-  float* sgate = reinterpret_cast<float*>(ws + L.sgate);
-  MOE_CUDA(launch_rmsnorm(p, x, h32, h16, T, s));
-  MOE_CUDA(launch_router(p, h32, logits, T, s));
-  MOE_CUDA(launch_topk(p, logits, ids, wts, sgate, T, s));
-  MOE_CUDA(launch_permute(p, L, ws, ids, gather ? h16 : nullptr, T, s));
+                      bool dispatch, cudaStream_t s) {
+  MOE_CUDA(launch_route(p, L, ws, x, T, dispatch, s));
   return MOE_OK;
 }
 

@@ -62,7 +62,7 @@ struct Plan {
 
 // Workspace carve-up for one forward of T tokens (offsets in bytes).
 struct WsLayout {
-  size_t h32, h16, xg, act, act_s, y, y_s, logits, ids, wts, sgate;
+  size_t h16, xg, act, act_s, y, y_s, logits, part, ss_part, rms, counters, ids, wts, sgate;
   size_t bm, hist, base, offsets, perm, slot_row, tiles1, tiles2, tile_count;
   size_t total;
   int nchunks, max_tiles1, max_tiles2, bn;
@@ -70,16 +70,20 @@ struct WsLayout {
 
 WsLayout ws_layout(const Plan& p, int T);
 
+// Router launch geometry: rx router-row tiles x splits K-splits x tz token tiles.
+struct RouterGeom {
+  int rx, tz, splits, k_per_split;
+};
+RouterGeom router_geometry(const Plan& p, int T);
+
+constexpr int kTailMaxT = 256;  // decode: one CTA does top-k + permutation + tile lists
+bool route_uses_tail(const Plan& p, int T);
+
 // ------------------------------------------------------------ launchers
-cudaError_t launch_rmsnorm(const Plan& p, const float* x, float* h32, __half* h16, int T,
-                           cudaStream_t s);
-// logits holds router_splits(p, T) partial slices of [T][router_rows] fp32
-int router_splits(const Plan& p, int T);
-cudaError_t launch_router(const Plan& p, const float* h32, float* logits, int T, cudaStream_t s);
-cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float* wts,
-                        float* sgate, int T, cudaStream_t s);
-cudaError_t launch_permute(const Plan& p, const WsLayout& L, char* ws, const int32_t* ids,
-                           const __half* h16, int T, cudaStream_t s);
+// Router (+ RMSNorm), top-k, permutation and tile lists; with `dispatch` also
+// the normalised f16 rows of every routed slot (xg) and of the shared expert (h16).
+cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                         bool dispatch, cudaStream_t s);
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
                         cudaStream_t s);
 cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,

@@ -85,25 +85,19 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   void* scratch = nullptr;
   MOE_NA_CUDA(scratch_address(p.device, &scratch));
 
-  // Same kernel sequence as moe_forward.  Every scratch byte a kernel reads is
-  // written earlier in the same call, so nothing has to be cleared between calls.
+  // Same kernel sequence as moe_forward.  The router's split counters must
+  // start at zero: launch_route clears them with a stream memset at the start of
+  // every call.  Every other scratch byte a kernel reads is written earlier in
+  // the same call, so nothing else has to be cleared between calls.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(scratch);
-  float* h32 = reinterpret_cast<float*>(ws + L.h32);
-  __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
-  float* logits = reinterpret_cast<float*>(ws + L.logits);
-  int32_t* ids = reinterpret_cast<int32_t*>(ws + L.ids);
-  float* wts = reinterpret_cast<float*>(ws + L.wts);
-  float* sgate = reinterpret_cast<float*>(ws + L.sgate);
-  MOE_NA_CUDA(launch_rmsnorm(p, x_dev, h32, h16, T, s));
-  MOE_NA_CUDA(launch_router(p, h32, logits, T, s));
-  MOE_NA_CUDA(launch_topk(p, logits, ids, wts, sgate, T, s));
-  MOE_NA_CUDA(launch_permute(p, L, ws, ids, h16, T, s));
+  MOE_NA_CUDA(launch_route(p, L, ws, x_dev, T, true, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, true, T, s));
   MOE_NA_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
                              reinterpret_cast<float*>(ws + L.y_s),
-                             reinterpret_cast<int32_t*>(ws + L.slot_row), wts, sgate, out_dev, T,
-                             s));
+                             reinterpret_cast<int32_t*>(ws + L.slot_row),
+                             reinterpret_cast<float*>(ws + L.wts),
+                             reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
   return MOE_OK;
 }

@@ -1,4 +1,6 @@
-// Router, top-k and token permutation kernels (K1/K2 of the MoE block).
+// Routing stage of the MoE block (K1/K2): fused RMSNorm + router, top-k, the
+// deterministic expert-major permutation, GEMM tile lists, and the dispatch
+// gather of normalised f16 rows.
 //
 // Reference arithmetic (disk-mem-off, offload_runtime/executors):
 //   rms_norm      _common.py:73-75       h = w * (x / sqrt(mean(x^2) + eps))
@@ -6,8 +8,13 @@
 //   scoring/top-k glm4_moe.py:185-200    softmax, top-k by prob, renormalise, * scale
 //                 qwen3_next.py:278-293  (no bias, no scale)
 //   dispatch      glm4_moe.py:206-215    per expert, tokens ascending
-// Everything on the routing path stays fp32.  Ranking uses the biased logit
-// (softmax is monotone in it), exact ties go to the lower expert id.
+// Everything on the routing path is fp32.  The router uses
+// logit = (sum_k (w_k x_k) Wg_k) / rms, the same quantity as h @ Wg^T with the
+// per-token 1/rms factored out of the sum.  Ranking uses the biased logit
+// (softmax is monotone in it); exact ties go to the lower expert id.
+//
+// Decode (T <= 256): router -> route_tail (one CTA) -> dispatch.
+// Prefill:          router -> topk -> perm_hist -> perm_scan -> perm_scatter -> dispatch.
 #include <float.h>
 
 #include "common.cuh"
@@ -15,62 +22,7 @@
 
 namespace moe {
 
-// ------------------------------------------------------------------ RMSNorm
-// One CTA per token: h32 (router input, fp32) and h16 (expert GEMM operand).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x,
-                                                      const float* __restrict__ w,
-                                                      float* __restrict__ h32,
-                                                      __half* __restrict__ h16, int H,
-                                                      float eps) {
-  const int t = blockIdx.x;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
-  const int nv = H >> 2;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-    float4 v = xr[i];
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
-  }
-  __shared__ float red[32];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float rms = sqrtf(red[0] / static_cast<float>(H) + eps);
-  const float4* wr = reinterpret_cast<const float4*>(w);
-  float4* o32 = reinterpret_cast<float4*>(h32 + static_cast<size_t>(t) * H);
-  __half2* o16 = reinterpret_cast<__half2*>(h16 + static_cast<size_t>(t) * H);
-  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-    float4 v = xr[i];
-    float4 g = wr[i];
-    float4 r;
-    r.x = g.x * (v.x / rms);
-    r.y = g.y * (v.y / rms);
-    r.z = g.z * (v.z / rms);
-    r.w = g.w * (v.w / rms);
-    o32[i] = r;
-    o16[2 * i] = __floats2half2_rn(r.x, r.y);
-    o16[2 * i + 1] = __floats2half2_rn(r.z, r.w);
-  }
-}
-
 // ------------------------------------------------------------------ router
-// logits = h32 @ Wr^T in fp32, split along K.  CTA (rx, s, ty) computes router
-// rows [32 rx, 32 rx + 32) x tokens [BT ty, BT ty + BT) over its K range, in
-// chunks of 128: the whole chunk of both operands is requested with cp.async at
-// once (so a decode step pays one memory latency, not one per k-step), then
-// each thread accumulates TPT x EPT outputs reading float4s along K.  Partial
-// sums go to part[s][t][r]; the top-k kernel adds the S slices in order s = 0..S-1,
-// so the result is deterministic.
 constexpr int kRouterKc = 128;      // K elements per chunk
 constexpr int kRouterRows = 32;     // router rows per CTA
 constexpr int kRouterPad = 4;       // smem row padding (floats)
@@ -80,33 +32,64 @@ MOE_DEV void cp_async16(void* smem, const void* gmem) {
                : "memory");
 }
 
+// sum_{q < n} p[q * stride], added in order q = 0, 1, ...; the loads of a batch
+// of 8 are issued before any is added, so a long split count costs a few
+// memory latencies rather than one per split.
+MOE_DEV float sum_splits(const float* p, size_t stride, int n) {
+  float acc = 0.f;
+  int q = 0;
+  for (; q + 8 <= n; q += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = p[(q + i) * stride];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += v[i];
+  }
+  for (; q < n; ++q) acc += p[q * stride];
+  return acc;
+}
+
+// CTA (rx, s, tz) computes router rows [32 rx, 32 rx + 32) for tokens
+// [BT tz, BT tz + BT) over K split s, in chunks of 128 that are requested with
+// cp.async all at once (one memory latency per chunk).  It also sums x^2 of its
+// tokens over its K range.  With S > 1 splits the partials go to scratch and the
+// CTA that finishes last for a (rx, tz) tile adds them in split order
+// s = 0..S-1 (deterministic), divides by rms and writes the logits.
 template <int BT>
-__global__ void __launch_bounds__(256) router_splitk_kernel(const float* __restrict__ h32,
-                                                            const float* __restrict__ wr,
-                                                            float* __restrict__ part, int T,
-                                                            int H, int R, int k_per_split) {
+__global__ void __launch_bounds__(256) router_kernel(
+    const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ wr,
+    float* __restrict__ part, float* __restrict__ ss_part, float* __restrict__ logits,
+    float* __restrict__ rms_out, int* __restrict__ counters, int T, int H, int R, int S,
+    int k_per_split, float eps) {
   constexpr int EPT = (BT == 64) ? 4 : 2;     // router rows per thread
   constexpr int XT = kRouterRows / EPT;       // threads along rows
   constexpr int YT = 256 / XT;                // threads along tokens
   constexpr int TPT = BT / YT;                // tokens per thread
   constexpr int LD = kRouterKc + kRouterPad;  // smem row stride (floats)
+  constexpr int TPTOK = 256 / BT;             // threads per token for the x^2 sum
+  constexpr int SSV = kRouterKc / 4 / TPTOK;  // float4 per thread per chunk for x^2
   extern __shared__ __align__(16) float rsm[];
-  float* hs = rsm;                 // [BT][LD]
-  float* ws = rsm + BT * LD;       // [32][LD]
-  const int r0 = blockIdx.x * kRouterRows;
-  const int t0 = blockIdx.z * BT;
-  const int kb = blockIdx.y * k_per_split;
+  float* xs = rsm;                       // [BT][LD] raw x
+  float* ws = xs + BT * LD;              // [32][LD] router rows
+  float* wns = ws + kRouterRows * LD;    // [128] norm weight chunk
+  __shared__ float s_rms[BT];
+  __shared__ int s_last;
+  const int rx = blockIdx.x, sp = blockIdx.y, tz = blockIdx.z;
+  const int r0 = rx * kRouterRows;
+  const int t0 = tz * BT;
+  const int kb = sp * k_per_split;
   const int ke = min(H, kb + k_per_split);
   const int tid = threadIdx.x;
   const int ty = tid / XT, tx = tid % XT;
+  const int stok = tid / TPTOK, sseg = tid % TPTOK;
   float acc[TPT][EPT] = {};
+  float ss = 0.f;
   for (int k0 = kb; k0 < ke; k0 += kRouterKc) {
-    const int kn = min(kRouterKc, ke - k0);  // multiple of 16 (H % 16 == 0)
-    const int nv = kn >> 2;                  // float4 per row in this chunk
+    const int nv = min(kRouterKc, ke - k0) >> 2;  // float4 per row (H % 16 == 0)
     for (int i = tid; i < BT * (kRouterKc / 4); i += 256) {
       const int row = i / (kRouterKc / 4), v = i % (kRouterKc / 4);
-      float* dst = hs + row * LD + v * 4;
-      if (t0 + row < T && v < nv) cp_async16(dst, h32 + static_cast<size_t>(t0 + row) * H + k0 + v * 4);
+      float* dst = xs + row * LD + v * 4;
+      if (t0 + row < T && v < nv) cp_async16(dst, x + static_cast<size_t>(t0 + row) * H + k0 + v * 4);
       else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     for (int i = tid; i < kRouterRows * (kRouterKc / 4); i += 256) {
@@ -115,13 +98,30 @@ __global__ void __launch_bounds__(256) router_splitk_kernel(const float* __restr
       if (r0 + row < R && v < nv) cp_async16(dst, wr + static_cast<size_t>(r0 + row) * H + k0 + v * 4);
       else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (tid < kRouterKc / 4) {
+      float* dst = wns + tid * 4;
+      if (tid < nv) cp_async16(dst, wn + k0 + tid * 4);
+      else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+#pragma unroll
+    for (int v = 0; v < SSV; ++v) {
+      const float4 a = *reinterpret_cast<const float4*>(xs + stok * LD + (sseg * SSV + v) * 4);
+      ss = fmaf(a.x, a.x, ss);
+      ss = fmaf(a.y, a.y, ss);
+      ss = fmaf(a.z, a.z, ss);
+      ss = fmaf(a.w, a.w, ss);
+    }
 #pragma unroll 4
     for (int k = 0; k < kRouterKc; k += 4) {
+      const float4 g = *reinterpret_cast<const float4*>(wns + k);
       float4 a[TPT], b[EPT];
 #pragma unroll
-      for (int i = 0; i < TPT; ++i) a[i] = *reinterpret_cast<const float4*>(hs + (ty + YT * i) * LD + k);
+      for (int i = 0; i < TPT; ++i) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + (ty + YT * i) * LD + k);
+        a[i] = make_float4(g.x * xv.x, g.y * xv.y, g.z * xv.z, g.w * xv.w);
+      }
 #pragma unroll
       for (int j = 0; j < EPT; ++j) b[j] = *reinterpret_cast<const float4*>(ws + (tx + XT * j) * LD + k);
 #pragma unroll
@@ -138,7 +138,28 @@ __global__ void __launch_bounds__(256) router_splitk_kernel(const float* __restr
     }
     __syncthreads();
   }
-  float* out = part + static_cast<size_t>(blockIdx.y) * T * R;
+  // x^2 of token stok over this split: reduce the TPTOK consecutive lanes
+#pragma unroll
+  for (int o = TPTOK / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+
+  if (S == 1) {  // whole K in this CTA: finish directly
+    if (sseg == 0) s_rms[stok] = sqrtf(ss / static_cast<float>(H) + eps);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < TPT; ++i) {
+      const int tl = ty + YT * i, t = t0 + tl;
+      if (t >= T) continue;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const int r = r0 + tx + XT * j;
+        if (r < R) logits[static_cast<size_t>(t) * R + r] = acc[i][j] / s_rms[tl];
+      }
+    }
+    if (rx == 0 && sseg == 0 && t0 + stok < T) rms_out[t0 + stok] = s_rms[stok];
+    return;
+  }
+
+  float* out = part + static_cast<size_t>(sp) * T * R;
 #pragma unroll
   for (int i = 0; i < TPT; ++i) {
     const int t = t0 + ty + YT * i;
@@ -149,29 +170,36 @@ __global__ void __launch_bounds__(256) router_splitk_kernel(const float* __restr
       if (r < R) out[static_cast<size_t>(t) * R + r] = acc[i][j];
     }
   }
+  if (sseg == 0 && t0 + stok < T) ss_part[(static_cast<size_t>(rx) * S + sp) * T + t0 + stok] = ss;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(&counters[rx * gridDim.z + tz], 1) == S - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid < BT && t0 + tid < T) {
+    const float tot = sum_splits(ss_part + static_cast<size_t>(rx) * S * T + t0 + tid,
+                                 static_cast<size_t>(T), S);
+    s_rms[tid] = sqrtf(tot / static_cast<float>(H) + eps);
+    if (rx == 0) rms_out[t0 + tid] = s_rms[tid];
+  }
+  __syncthreads();
+  for (int o = tid; o < BT * kRouterRows; o += 256) {
+    const int tl = o / kRouterRows, r = r0 + o % kRouterRows, t = t0 + tl;
+    if (t >= T || r >= R) continue;
+    const float v = sum_splits(part + static_cast<size_t>(t) * R + r, static_cast<size_t>(T) * R, S);
+    logits[static_cast<size_t>(t) * R + r] = v / s_rms[tl];
+  }
 }
 
 // ------------------------------------------------------------------ top-k
-// One warp per token.  Lane l holds experts l, l+32, ...  Scores are ranked by
-// (key desc, id asc); weights follow the reference formulas in fp32.
+// One warp scores and selects for one token.  Lane l holds experts l, l+32, ...
+// Keys rank (desc) with the lower id winning exact ties; weights follow the
+// reference formulas in fp32.  Lane 0 writes ids_out[0..K) / w_out[0..K).
 template <int VPL>
-__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ part,
-                                                   const float* __restrict__ bias,
-                                                   int32_t* __restrict__ ids_out,
-                                                   float* __restrict__ w_out,
-                                                   float* __restrict__ sgate, int T, int E,
-                                                   int R, int K, int nsplit, int score_func,
-                                                   int norm, float scale, int* err) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  // logit of router row r for this token: split-K partials added in split order
-  auto logit = [&](int r) {
-    const float* p = part + static_cast<size_t>(t) * R + r;
-    float v = p[0];
-    for (int q = 1; q < nsplit; ++q) v += p[static_cast<size_t>(q) * T * R];
-    return v;
-  };
+MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
+                       int K, int score_func, int norm, float scale, int lane,
+                       int32_t* ids_out, float* w_out, int* err) {
   float key[VPL], val[VPL];
   float m = -FLT_MAX;
 #pragma unroll
@@ -180,7 +208,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ par
     key[j] = -FLT_MAX;
     val[j] = 0.f;
     if (e < E) {
-      float l = logit(e);
+      float l = lrow[e];
       if (score_func == MOE_SCORE_SOFTMAX) {
         if (bias) l = l + bias[e];
         key[j] = l;
@@ -200,8 +228,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ par
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E) {
+      if (j * 32 + lane < E) {
         val[j] = expf(val[j] - m);
         s += val[j];
       }
@@ -210,7 +237,6 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ par
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     denom = s;
   }
-  // iterative arg-max selection; `taken` marks this lane's retired experts
   int sel_id[kMaxTopK];
   float sel_w[kMaxTopK];
   uint32_t taken = 0u;
@@ -233,8 +259,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ par
       const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
       const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      if (oid != 0x7fffffff &&
-          (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
+      if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
         bk = ok;
         bid = oid;
         bv = ov;
@@ -255,19 +280,184 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ par
     for (int r = 0; r < K; ++r) {
       float wv = sel_w[r];
       if (norm) wv = wv / (sum + 1e-20f);
-      wv = wv * scale;
-      ids_out[static_cast<size_t>(t) * K + r] = sel_id[r];
-      w_out[static_cast<size_t>(t) * K + r] = wv;
+      ids_out[r] = sel_id[r];
+      w_out[r] = wv * scale;
     }
-    if (sgate) sgate[t] = sigmoid_f(logit(E));
   }
 }
 
-// ------------------------------------------------------------------ permutation
-// Per chunk of 1024 tokens: a bitmask per expert (bit = token has the expert in
-// its top-k).  Counts are popcounts; the rank of a token inside its expert is
-// the popcount of the lower bits, so the dispatch order (tokens ascending
-// inside an expert) is deterministic without any ordering of atomics.
+template <int VPL>
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits,
+                                                   const float* __restrict__ bias,
+                                                   int32_t* __restrict__ ids, float* __restrict__ wts,
+                                                   float* __restrict__ sgate, int T, int E, int R,
+                                                   int K, int score_func, int norm, float scale,
+                                                   int* err) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float* lrow = logits + static_cast<size_t>(t) * R;
+  warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, ids + static_cast<size_t>(t) * K,
+                 wts + static_cast<size_t>(t) * K, err);
+  if (sgate && lane == 0) sgate[t] = sigmoid_f(lrow[E]);
+}
+
+// ------------------------------------------------------------------ tile lists
+// Block-wide exclusive scan of one int per thread (blockDim.x == 1024).
+__device__ int block_excl_scan(int v, int* total) {
+  __shared__ int wsum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    wsum[lane] = s;
+  }
+  __syncthreads();
+  const int incl = x + (warp > 0 ? wsum[warp - 1] : 0);
+  if (total) *total = wsum[31];
+  __syncthreads();
+  return incl - v;
+}
+
+struct TileArgs {
+  int E, T, bn, mt1, mt2, mt1s, has_shared, max1, max2;
+  Tile* tiles1;
+  Tile* tiles2;
+  int32_t* tile_count;
+  int* err;
+};
+
+// Expert e = threadIdx.x owns `cnt` rows starting at `off`.  Writes both GEMM
+// tile lists (expert-major; weight m-tile outer, token tile inner, so a weight
+// tile is reused by neighbouring CTAs while it is in L2) with all threads, then
+// the shared-expert tiles.  Called by every thread of a 1024-thread CTA.
+__device__ void build_tile_lists(int cnt, int off, const TileArgs& a, int* s_p1, int* s_p2,
+                                 int* s_cnt, int* s_off) {
+  const int e = threadIdx.x;
+  const int ntn = (e < a.E) ? (cnt + a.bn - 1) / a.bn : 0;
+  int tot1 = 0, tot2 = 0;
+  const int p1 = block_excl_scan(ntn * a.mt1, &tot1);
+  const int p2 = block_excl_scan(ntn * a.mt2, &tot2);
+  if (e < a.E) {
+    s_p1[e] = p1;
+    s_p2[e] = p2;
+    s_cnt[e] = cnt;
+    s_off[e] = off;
+  }
+  if (e == 0) {
+    s_p1[a.E] = tot1;
+    s_p2[a.E] = tot2;
+  }
+  __syncthreads();
+  for (int pass = 0; pass < 2; ++pass) {
+    const int* pre = pass ? s_p2 : s_p1;
+    const int total = pass ? tot2 : tot1;
+    const int lim = pass ? a.max2 : a.max1;
+    Tile* out = pass ? a.tiles2 : a.tiles1;
+    for (int q = threadIdx.x; q < total && q < lim; q += blockDim.x) {
+      int lo = 0, hi = a.E;  // largest ex with pre[ex] <= q
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (pre[mid] <= q) lo = mid;
+        else hi = mid;
+      }
+      const int ex = lo;
+      const int c = s_cnt[ex];
+      const int nt = (c + a.bn - 1) / a.bn;
+      const int l = q - pre[ex];
+      const int m = l / nt, n = l % nt;
+      out[q] = Tile{ex, m * kBM, s_off[ex] + n * a.bn, min(a.bn, c - n * a.bn)};
+    }
+  }
+  const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
+  for (int i = threadIdx.x; i < a.mt1s * nts; i += blockDim.x) {
+    const int m = i / nts, n = i % nts;
+    if (tot1 + i < a.max1) a.tiles1[tot1 + i] = Tile{a.E, m * kBM, n * a.bn, min(a.bn, a.T - n * a.bn)};
+  }
+  for (int i = threadIdx.x; i < a.mt2 * nts; i += blockDim.x) {
+    const int m = i / nts, n = i % nts;
+    if (tot2 + i < a.max2) a.tiles2[tot2 + i] = Tile{a.E, m * kBM, n * a.bn, min(a.bn, a.T - n * a.bn)};
+  }
+  if (threadIdx.x == 0) {
+    const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
+    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_BAD_TILE);
+    a.tile_count[0] = min(c1, a.max1);
+    a.tile_count[1] = min(c2, a.max2);
+  }
+}
+
+// ------------------------------------------------------------------ decode tail
+// One CTA (1024 threads) for T <= kTailMaxT: top-k of every token (a warp per
+// token), per-expert token bitmasks, expert offsets, tile lists and the
+// (token, slot) -> row permutation.  The rank of a token inside its expert is
+// the popcount of the lower bits of the expert's mask, so the dispatch order
+// (tokens ascending) is deterministic without ordering any atomics.
+template <int VPL>
+__global__ void __launch_bounds__(1024) route_tail_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int R, int K,
+    int score_func, int norm, float scale, int32_t* __restrict__ ids, float* __restrict__ wts,
+    float* __restrict__ sgate, int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
+    int32_t* __restrict__ slot_row, TileArgs ta) {
+  extern __shared__ int tsm[];
+  const int words = (T + 31) >> 5;
+  int* s_ids = tsm;                                              // [T*K]
+  uint32_t* bm = reinterpret_cast<uint32_t*>(s_ids + T * K);     // [E][words]
+  int* s_p1 = reinterpret_cast<int*>(bm + E * words);            // [E+1]
+  int* s_p2 = s_p1 + (E + 1);
+  int* s_cnt = s_p2 + (E + 1);
+  int* s_off = s_cnt + (E + 1);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < E * words; i += blockDim.x) bm[i] = 0u;
+  for (int t = warp; t < T; t += 32) {
+    const float* lrow = logits + static_cast<size_t>(t) * R;
+    warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, s_ids + t * K,
+                   wts + static_cast<size_t>(t) * K, ta.err);
+    if (sgate && lane == 0) sgate[t] = sigmoid_f(lrow[E]);
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < T * K; q += blockDim.x) {
+    const int e = s_ids[q];
+    ids[q] = e;
+    const int t = q / K;
+    atomicOr(&bm[e * words + (t >> 5)], 1u << (t & 31));
+  }
+  __syncthreads();
+  int cnt = 0;
+  if (threadIdx.x < E)
+    for (int w = 0; w < words; ++w) cnt += __popc(bm[threadIdx.x * words + w]);
+  int all = 0;
+  const int off = block_excl_scan(threadIdx.x < E ? cnt : 0, &all);
+  if (threadIdx.x < E) offsets[threadIdx.x] = off;
+  if (threadIdx.x == 0) offsets[E] = all;
+  build_tile_lists(cnt, off, ta, s_p1, s_p2, s_cnt, s_off);  // also fills s_off
+  __syncthreads();
+  for (int q = threadIdx.x; q < T * K; q += blockDim.x) {
+    const int e = s_ids[q];
+    const int t = q / K;
+    const uint32_t* row = bm + e * words;
+    int rank = __popc(row[t >> 5] & ((1u << (t & 31)) - 1u));
+    for (int w = 0; w < (t >> 5); ++w) rank += __popc(row[w]);
+    const int r = s_off[e] + rank;
+    perm[r] = q;
+    slot_row[q] = r;
+  }
+}
+
+// ------------------------------------------------------------------ prefill permutation
+// Per chunk of 1024 tokens: a bitmask per expert, written to global with its
+// popcount histogram; a single-CTA scan; then one thread per (token, slot).
 __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restrict__ ids, int T,
                                                          int K, int E, uint32_t* __restrict__ bmg,
                                                          int32_t* __restrict__ hist, int* err) {
@@ -297,41 +487,12 @@ __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restri
   }
 }
 
-// Block-wide exclusive scan of one int per thread (blockDim.x == 1024).
-__device__ int block_excl_scan(int v, int* total) {
-  __shared__ int wsum[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wsum[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int s = wsum[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
-    }
-    wsum[lane] = s;
-  }
-  __syncthreads();
-  const int incl = x + (warp > 0 ? wsum[warp - 1] : 0);
-  if (total) *total = wsum[31];
-  __syncthreads();
-  return incl - v;
-}
-
-// Single CTA: expert offsets, per-chunk bases and the two GEMM tile lists.
-__global__ void __launch_bounds__(1024) perm_scan_kernel(
-    const int32_t* __restrict__ hist, int nchunks, int E, int T, int bn, int mt1, int mt2,
-    int mt1s, int has_shared, int max1, int max2, int32_t* __restrict__ base,
-    int32_t* __restrict__ offsets, Tile* __restrict__ tiles1, Tile* __restrict__ tiles2,
-    int32_t* __restrict__ tile_count, int* err) {
-  const int e = threadIdx.x;
+__global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restrict__ hist,
+                                                         int nchunks, int32_t* __restrict__ base,
+                                                         int32_t* __restrict__ offsets,
+                                                         TileArgs ta) {
+  __shared__ int s_p1[1025], s_p2[1025], s_cnt[1025], s_off[1025];
+  const int e = threadIdx.x, E = ta.E;
   int tot = 0;
   if (e < E) {
     for (int c = 0; c < nchunks; ++c) {
@@ -346,174 +507,218 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(
     for (int c = 0; c < nchunks; ++c) base[static_cast<size_t>(c) * E + e] += off;
   }
   if (e == 0) offsets[E] = all;
-  const int ntile_n = (e < E) ? (tot + bn - 1) / bn : 0;
-  int tot1 = 0, tot2 = 0;
-  const int p1 = block_excl_scan(ntile_n * mt1, &tot1);
-  const int p2 = block_excl_scan(ntile_n * mt2, &tot2);
-  // tile lists: expert-major, m outer, token tiles inner (a weight tile is
-  // reused by neighbouring CTAs while it is still in L2)
-  if (e < E) {
-    int q1 = p1, q2 = p2;
-    for (int m = 0; m < mt1; ++m)
-      for (int n = 0; n < ntile_n; ++n, ++q1)
-        if (q1 < max1) tiles1[q1] = Tile{e, m * kBM, off + n * bn, min(bn, tot - n * bn)};
-    for (int m = 0; m < mt2; ++m)
-      for (int n = 0; n < ntile_n; ++n, ++q2)
-        if (q2 < max2) tiles2[q2] = Tile{e, m * kBM, off + n * bn, min(bn, tot - n * bn)};
-  }
-  __syncthreads();
-  const int nts = has_shared ? (T + bn - 1) / bn : 0;
-  for (int i = threadIdx.x; i < mt1s * nts; i += blockDim.x) {
-    const int m = i / nts, n = i % nts;
-    if (tot1 + i < max1) tiles1[tot1 + i] = Tile{E, m * kBM, n * bn, min(bn, T - n * bn)};
-  }
-  for (int i = threadIdx.x; i < mt2 * nts; i += blockDim.x) {
-    const int m = i / nts, n = i % nts;
-    if (tot2 + i < max2) tiles2[tot2 + i] = Tile{E, m * kBM, n * bn, min(bn, T - n * bn)};
-  }
-  if (threadIdx.x == 0) {
-    const int c1 = tot1 + mt1s * nts, c2 = tot2 + mt2 * nts;
-    if (c1 > max1 || c2 > max2) record_error(err, DEV_BAD_TILE);
-    tile_count[0] = min(c1, max1);
-    tile_count[1] = min(c2, max2);
-  }
+  build_tile_lists(tot, off, ta, s_p1, s_p2, s_cnt, s_off);
 }
 
-// One warp per (token, slot): rank from the chunk bitmask, write perm /
-// slot_row, and copy the token's f16 row into its dispatch slot.
-__global__ void __launch_bounds__(256) perm_scatter_gather_kernel(
-    const int32_t* __restrict__ ids, const uint32_t* __restrict__ bmg,
-    const int32_t* __restrict__ base, const __half* __restrict__ h16, int T, int K, int E, int H,
-    int32_t* __restrict__ perm, int32_t* __restrict__ slot_row, __half* __restrict__ xg) {
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
-  for (int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < T * K; q += nwarps) {
+__global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __restrict__ ids,
+                                                           const uint32_t* __restrict__ bmg,
+                                                           const int32_t* __restrict__ base,
+                                                           int T, int K, int E,
+                                                           int32_t* __restrict__ perm,
+                                                           int32_t* __restrict__ slot_row) {
+  for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < T * K; q += gridDim.x * blockDim.x) {
     const int t = q / K;
     const int e = ids[q];
     if (e < 0 || e >= E) continue;  // reported by perm_hist_kernel
     const int c = t / kPermChunk, tl = t % kPermChunk;
-    const uint32_t word = bmg[(static_cast<size_t>(c) * E + e) * 32 + lane];
-    int cnt = 0;
-    if (lane < (tl >> 5)) cnt = __popc(word);
-    else if (lane == (tl >> 5)) cnt = __popc(word & ((1u << (tl & 31)) - 1u));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    const int row = base[static_cast<size_t>(c) * E + e] + cnt;
-    if (lane == 0) {
-      perm[row] = q;
-      slot_row[q] = row;
+    const uint32_t* row = bmg + (static_cast<size_t>(c) * E + e) * 32;
+    int rank = __popc(row[tl >> 5] & ((1u << (tl & 31)) - 1u));
+    for (int w = 0; w < (tl >> 5); ++w) rank += __popc(row[w]);
+    const int r = base[static_cast<size_t>(c) * E + e] + rank;
+    perm[r] = q;
+    slot_row[q] = r;
+  }
+}
+
+// ------------------------------------------------------------------ dispatch
+// Rows [0, T*K): xg[r] = f16(w * (x[token(r)] / rms)); rows [T*K, T*K+T): h16[t]
+// for the shared expert.  One warp per row, 8 elements per lane per step.
+__global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ wn,
+                                                       const float* __restrict__ rms,
+                                                       const int32_t* __restrict__ perm, int T,
+                                                       int K, int H, int with_shared,
+                                                       __half* __restrict__ xg,
+                                                       __half* __restrict__ h16) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const int rows = T * K + (with_shared ? T : 0);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    int t;
+    __half* dst;
+    if (r < T * K) {
+      t = perm[r] / K;
+      dst = xg + static_cast<size_t>(r) * H;
+    } else {
+      t = r - T * K;
+      dst = h16 + static_cast<size_t>(t) * H;
     }
-    if (xg) {
-      const uint4* src = reinterpret_cast<const uint4*>(h16 + static_cast<size_t>(t) * H);
-      uint4* dst = reinterpret_cast<uint4*>(xg + static_cast<size_t>(row) * H);
-      for (int v = lane; v < (H >> 3); v += 32) dst[v] = src[v];
+    const float inv = 1.0f / rms[t];
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+    const float4* wr = reinterpret_cast<const float4*>(wn);
+    for (int v = lane; v < (H >> 3); v += 32) {
+      const float4 a0 = xr[2 * v], a1 = xr[2 * v + 1];
+      const float4 g0 = wr[2 * v], g1 = wr[2 * v + 1];
+      __half2 o[4];
+      o[0] = __floats2half2_rn(g0.x * (a0.x * inv), g0.y * (a0.y * inv));
+      o[1] = __floats2half2_rn(g0.z * (a0.z * inv), g0.w * (a0.w * inv));
+      o[2] = __floats2half2_rn(g1.x * (a1.x * inv), g1.y * (a1.y * inv));
+      o[3] = __floats2half2_rn(g1.z * (a1.z * inv), g1.w * (a1.w * inv));
+      reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<uint4*>(o);
     }
   }
 }
 
 // ------------------------------------------------------------------ launchers
-cudaError_t launch_rmsnorm(const Plan& p, const float* x, float* h32, __half* h16, int T,
-                           cudaStream_t s) {
-  rmsnorm_kernel<<<T, 256, 0, s>>>(x, p.w.norm_w, h32, h16, p.H, p.cfg.rms_norm_eps);
-  return cudaGetLastError();
+static cudaError_t set_smem_attr(const void* fn, size_t bytes, bool* done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  cudaError_t a = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (a == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+  return a;
 }
 
-int router_splits(const Plan& p, int T) {
+// Decode batches use 16-token tiles (more CTAs, shorter last-CTA reductions);
+// prefill uses 64-token tiles (4 x 4 outputs per thread).
+static int router_bt(int T) { return T <= 64 ? 16 : 64; }
+
+RouterGeom router_geometry(const Plan& p, int T) {
+  RouterGeom g;
   const int nchunks = (p.H + kRouterKc - 1) / kRouterKc;
-  const int bt = T <= 16 ? 16 : 64;
-  const int tiles = ((p.router_rows + kRouterRows - 1) / kRouterRows) * ((T + bt - 1) / bt);
+  const int bt = router_bt(T);
+  g.rx = (p.router_rows + kRouterRows - 1) / kRouterRows;
+  g.tz = (T + bt - 1) / bt;
   // enough CTAs to cover the SMs about twice, never more splits than K chunks
-  int s = (2 * p.num_sms + tiles - 1) / tiles;
+  int s = (2 * p.num_sms + g.rx * g.tz - 1) / (g.rx * g.tz);
   if (s > nchunks) s = nchunks;
-  return s < 1 ? 1 : s;
+  if (s < 1) s = 1;
+  const int per = (nchunks + s - 1) / s;
+  g.splits = (nchunks + per - 1) / per;  // drop splits that would have no K range
+  g.k_per_split = per * kRouterKc;
+  return g;
 }
 
 template <int BT>
-static cudaError_t run_router(const Plan& p, const float* h32, float* part, int T, int S,
+static cudaError_t run_router(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                               cudaStream_t s) {
-  constexpr size_t smem = static_cast<size_t>(BT + kRouterRows) * (kRouterKc + kRouterPad) * sizeof(float);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t a = cudaFuncSetAttribute(router_splitk_kernel<BT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  constexpr size_t smem =
+      (static_cast<size_t>(BT + kRouterRows) * (kRouterKc + kRouterPad) + kRouterKc) * sizeof(float);
+  static bool done[64] = {};
+  cudaError_t a = set_smem_attr(reinterpret_cast<const void*>(router_kernel<BT>), smem, done);
+  if (a != cudaSuccess) return a;
+  const RouterGeom g = router_geometry(p, T);
+  int* counters = reinterpret_cast<int*>(ws + L.counters);
+  if (g.splits > 1) {  // the last-CTA counters must start at zero on every call
+    a = cudaMemsetAsync(counters, 0, static_cast<size_t>(g.rx) * g.tz * sizeof(int), s);
     if (a != cudaSuccess) return a;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const int nchunks = (p.H + kRouterKc - 1) / kRouterKc;
-  const int k_per_split = ((nchunks + S - 1) / S) * kRouterKc;
-  dim3 grid((p.router_rows + kRouterRows - 1) / kRouterRows, S, (T + BT - 1) / BT);
-  router_splitk_kernel<BT><<<grid, 256, smem, s>>>(h32, p.w.router_w, part, T, p.H,
-                                                    p.router_rows, k_per_split);
+  dim3 grid(g.rx, g.splits, g.tz);
+  router_kernel<BT><<<grid, 256, smem, s>>>(
+      x, p.w.norm_w, p.w.router_w, reinterpret_cast<float*>(ws + L.part),
+      reinterpret_cast<float*>(ws + L.ss_part), reinterpret_cast<float*>(ws + L.logits),
+      reinterpret_cast<float*>(ws + L.rms), counters, T, p.H, p.router_rows, g.splits,
+      g.k_per_split, p.cfg.rms_norm_eps);
   return cudaGetLastError();
 }
 
-cudaError_t launch_router(const Plan& p, const float* h32, float* logits, int T,
-                          cudaStream_t s) {
-  const int S = router_splits(p, T);
-  return T <= 16 ? run_router<16>(p, h32, logits, T, S, s) : run_router<64>(p, h32, logits, T, S, s);
+static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T) {
+  TileArgs ta;
+  ta.E = p.E;
+  ta.T = T;
+  ta.bn = L.bn;
+  ta.mt1 = (2 * p.I + kBM - 1) / kBM;
+  ta.mt2 = (p.H + kBM - 1) / kBM;
+  ta.mt1s = p.SI > 0 ? (2 * p.SI + kBM - 1) / kBM : 0;
+  ta.has_shared = p.SI > 0;
+  ta.max1 = L.max_tiles1;
+  ta.max2 = L.max_tiles2;
+  ta.tiles1 = reinterpret_cast<Tile*>(ws + L.tiles1);
+  ta.tiles2 = reinterpret_cast<Tile*>(ws + L.tiles2);
+  ta.tile_count = reinterpret_cast<int32_t*>(ws + L.tile_count);
+  ta.err = p.d_err;
+  return ta;
 }
 
-cudaError_t launch_topk(const Plan& p, const float* logits, int32_t* ids, float* wts,
-                        float* sgate, int T, cudaStream_t s) {
-  const int E = p.E;
+bool route_uses_tail(const Plan& p, int T) { return T <= kTailMaxT && T * p.K <= 8192; }
+
+cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                         bool dispatch, cudaStream_t s) {
+  cudaError_t st = (router_bt(T) == 16) ? run_router<16>(p, L, ws, x, T, s)
+                                        : run_router<64>(p, L, ws, x, T, s);
+  if (st != cudaSuccess) return st;
+  const int E = p.E, K = p.K, R = p.router_rows;
+  const float* logits = reinterpret_cast<const float*>(ws + L.logits);
   const float* bias = p.cfg.use_bias ? p.w.bias : nullptr;
-  float* sg = p.cfg.has_shared_gate ? sgate : nullptr;
-  const int grid = (T + 7) / 8;
-  const int nsplit = router_splits(p, T);
-#define MOE_TOPK_CASE(V)                                                                     \
-  topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, p.router_rows, p.K,  \
-                                      nsplit, p.cfg.score_func, p.cfg.norm_topk_prob,        \
-                                      p.cfg.routed_scaling_factor, p.d_err)
-  const int vpl = (E + 31) / 32;
-  if (vpl <= 1) MOE_TOPK_CASE(1);
-  else if (vpl <= 2) MOE_TOPK_CASE(2);
-  else if (vpl <= 4) MOE_TOPK_CASE(4);
-  else if (vpl <= 8) MOE_TOPK_CASE(8);
-  else if (vpl <= 16) MOE_TOPK_CASE(16);
-  else MOE_TOPK_CASE(32);
-#undef MOE_TOPK_CASE
-  return cudaGetLastError();
-}
-
-cudaError_t launch_permute(const Plan& p, const WsLayout& L, char* ws, const int32_t* ids,
-                           const __half* h16, int T, cudaStream_t s) {
-  const int E = p.E, K = p.K;
-  uint32_t* bmg = reinterpret_cast<uint32_t*>(ws + L.bm);
-  int32_t* hist = reinterpret_cast<int32_t*>(ws + L.hist);
-  int32_t* base = reinterpret_cast<int32_t*>(ws + L.base);
+  float* sg = p.cfg.has_shared_gate ? reinterpret_cast<float*>(ws + L.sgate) : nullptr;
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + L.ids);
+  float* wts = reinterpret_cast<float*>(ws + L.wts);
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  const size_t smem = static_cast<size_t>(E) * 32 * sizeof(uint32_t);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t a = cudaFuncSetAttribute(perm_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         1024 * 32 * static_cast<int>(sizeof(uint32_t)));
-    if (a != cudaSuccess) return a;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  int32_t* perm = reinterpret_cast<int32_t*>(ws + L.perm);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
+  const TileArgs ta = tile_args(p, L, ws, T);
+  const int vpl = (E + 31) / 32;
+  if (route_uses_tail(p, T)) {
+    const int words = (T + 31) / 32;
+    const size_t smem = (static_cast<size_t>(T) * K + static_cast<size_t>(E) * words +
+                         4 * static_cast<size_t>(E + 1)) * sizeof(int);
+#define MOE_TAIL_CASE(V)                                                                        \
+  do {                                                                                          \
+    static bool done[64] = {};                                                                  \
+    st = set_smem_attr(reinterpret_cast<const void*>(route_tail_kernel<V>), 160 * 1024, done);  \
+    if (st != cudaSuccess) return st;                                                           \
+    route_tail_kernel<V><<<1, 1024, smem, s>>>(logits, bias, T, E, R, K, p.cfg.score_func,      \
+                                               p.cfg.norm_topk_prob,                            \
+                                               p.cfg.routed_scaling_factor, ids, wts, sg,       \
+                                               offsets, perm, slot_row, ta);                    \
+  } while (0)
+    if (vpl <= 1) MOE_TAIL_CASE(1);
+    else if (vpl <= 2) MOE_TAIL_CASE(2);
+    else if (vpl <= 4) MOE_TAIL_CASE(4);
+    else if (vpl <= 8) MOE_TAIL_CASE(8);
+    else if (vpl <= 16) MOE_TAIL_CASE(16);
+    else MOE_TAIL_CASE(32);
+#undef MOE_TAIL_CASE
+  } else {
+    const int grid = (T + 7) / 8;
+#define MOE_TOPK_CASE(V)                                                                        \
+  topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, R, K,                   \
+                                      p.cfg.score_func, p.cfg.norm_topk_prob,                   \
+                                      p.cfg.routed_scaling_factor, p.d_err)
+    if (vpl <= 1) MOE_TOPK_CASE(1);
+    else if (vpl <= 2) MOE_TOPK_CASE(2);
+    else if (vpl <= 4) MOE_TOPK_CASE(4);
+    else if (vpl <= 8) MOE_TOPK_CASE(8);
+    else if (vpl <= 16) MOE_TOPK_CASE(16);
+    else MOE_TOPK_CASE(32);
+#undef MOE_TOPK_CASE
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    uint32_t* bmg = reinterpret_cast<uint32_t*>(ws + L.bm);
+    int32_t* hist = reinterpret_cast<int32_t*>(ws + L.hist);
+    int32_t* base = reinterpret_cast<int32_t*>(ws + L.base);
+    static bool done_hist[64] = {};
+    st = set_smem_attr(reinterpret_cast<const void*>(perm_hist_kernel), 1024 * 32 * sizeof(uint32_t),
+                       done_hist);
+    if (st != cudaSuccess) return st;
+    perm_hist_kernel<<<L.nchunks, 1024, static_cast<size_t>(E) * 32 * sizeof(uint32_t), s>>>(
+        ids, T, K, E, bmg, hist, p.d_err);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    perm_scan_kernel<<<1, 1024, 0, s>>>(hist, L.nchunks, base, offsets, ta);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    const int entries = T * K;
+    perm_scatter_kernel<<<min((entries + 255) / 256, p.num_sms * 8), 256, 0, s>>>(
+        ids, bmg, base, T, K, E, perm, slot_row);
   }
-  perm_hist_kernel<<<L.nchunks, 1024, smem, s>>>(ids, T, K, E, bmg, hist, p.d_err);
-  cudaError_t st = cudaGetLastError();
-  if (st != cudaSuccess) return st;
-  const int mt1 = (2 * p.I + kBM - 1) / kBM;
-  const int mt2 = (p.H + kBM - 1) / kBM;
-  const int mt1s = p.SI > 0 ? (2 * p.SI + kBM - 1) / kBM : 0;
-  perm_scan_kernel<<<1, 1024, 0, s>>>(hist, L.nchunks, E, T, L.bn, mt1, mt2, mt1s, p.SI > 0,
-                                      L.max_tiles1, L.max_tiles2, base, offsets,
-                                      reinterpret_cast<Tile*>(ws + L.tiles1),
-                                      reinterpret_cast<Tile*>(ws + L.tiles2),
-                                      reinterpret_cast<int32_t*>(ws + L.tile_count), p.d_err);
   st = cudaGetLastError();
-  if (st != cudaSuccess) return st;
-  const int entries = T * K;
-  const int grid = min((entries + 7) / 8, p.num_sms * 8);
-  perm_scatter_gather_kernel<<<grid, 256, 0, s>>>(
-      ids, bmg, base, h16, T, K, E, p.H, reinterpret_cast<int32_t*>(ws + L.perm),
-      reinterpret_cast<int32_t*>(ws + L.slot_row),
-      h16 ? reinterpret_cast<__half*>(ws + L.xg) : nullptr);
+  if (st != cudaSuccess || !dispatch) return st;
+  const int rows = T * K + (p.SI > 0 ? T : 0);
+  dispatch_kernel<<<min((rows + 7) / 8, p.num_sms * 16), 256, 0, s>>>(
+      x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms), perm, T, K, p.H, p.SI > 0,
+      reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
   return cudaGetLastError();
 }
 
