@@ -125,9 +125,15 @@ WsLayout ws_layout(const Plan& p, int T) {
   L.offsets = take(static_cast<size_t>(E + 1) * 4);
   L.perm = take(R * 4);
   L.slot_row = take(R * 4);
-  L.tiles1 = take(static_cast<size_t>(L.max_tiles1) * sizeof(Tile));
-  L.tiles2 = take(static_cast<size_t>(L.max_tiles2) * sizeof(Tile));
+  // split-K is used only for 16-token tiles when a list has fewer than four
+  // waves of tiles, so its scratch is bounded by 4 * SMs tiles of kMaxKSplit partials
+  L.max_split_tiles = (L.bn == kSplitTileRows) ? 4 * p.num_sms : 0;
+  L.tiles1 = take(static_cast<size_t>(L.max_tiles1) * kMaxKSplit * sizeof(Tile));
+  L.tiles2 = take(static_cast<size_t>(L.max_tiles2) * kMaxKSplit * sizeof(Tile));
   L.tile_count = take(16);
+  L.kpart = take(static_cast<size_t>(L.max_split_tiles) * kMaxKSplit * kBM * kSplitTileRows * 4);
+  L.kcount1 = take(static_cast<size_t>(L.max_split_tiles) * 4);
+  L.kcount2 = take(static_cast<size_t>(L.max_split_tiles) * 4);
   L.total = o;
   return L;
 }

@@ -49,8 +49,13 @@ struct GemmArgs {
   int y_ld;
   const float* scale_routed;  // int8 row scales [groups * rows_a]
   const float* scale_shared;  // [m_limit_shared]
+  float* kpart;               // split-K partials [tile_id * nsplit + split][128][16] f32
+  int* kcount;                // per-tile split arrival counters (zeroed by the tile builder)
   int* err;
 };
+
+// Named barrier of the four epilogue warps (barrier 0 is __syncthreads).
+MOE_DEV void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <int BN>
 struct TileCfg {
@@ -130,6 +135,8 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
   uint64_t* mma_done = tempty + 2;       // final drain of in-flight MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ int s_ready[2][4];   // epilogue warps' per-tile readiness votes
+  __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = min(*(args.tile_count + args.count_index), args.max_tiles);
@@ -162,8 +169,12 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
 
   auto tile_ok = [&](const Tile& t) {
     if (t.group < 0 || t.group > args.n_local || t.nvalid <= 0 || t.nvalid > BN) return false;
-    const int lim = (t.group == args.n_local) ? args.m_limit_shared : args.m_limit_routed;
-    return t.m0 >= 0 && t.m0 < lim;
+    const bool sh = t.group == args.n_local;
+    const int lim = sh ? args.m_limit_shared : args.m_limit_routed;
+    const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
+    const int nsplit = t.split >> 16, sidx = t.split & 0xffff;
+    if (nsplit < 1 || sidx >= nsplit || (nsplit > 1 && BN != kSplitTileRows)) return false;
+    return t.m0 >= 0 && t.m0 < lim && t.kb0 >= 0 && t.kb0 < t.kb1 && t.kb1 <= nk;
   };
 
   if (warp == 0) {
@@ -180,8 +191,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
         const CUtensorMap* ma = sh ? &args.a_shared : &args.a_routed;
         const CUtensorMap* mb = sh ? &args.b_shared : &args.b_routed;
         const int arow = sh ? t.m0 : t.group * args.rows_a_routed + t.m0;
-        const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag)) {
@@ -209,8 +219,6 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
         const Tile t = args.tiles[ti];
         if (!tile_ok(t)) continue;
-        const bool sh = t.group == args.n_local;
-        const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
         const int buf = tl & 1;
         if (!mbar_wait_bounded(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag)) {
           *abort_flag = 1;
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait_bounded(INT8 ? &conv[s] : &full[s], ph, abort_flag)) {
@@ -234,7 +242,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             tc_mma_f16(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
-                       (kb > 0 || k > 0) ? 1u : 0u);
+                       (kb > t.kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit(&empty[s]);
           issued = true;
@@ -257,15 +265,21 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       const Tile t = args.tiles[ti];
       if (!tile_ok(t)) continue;
       const int buf = tl & 1;
-      // every lane polls; the vote re-converges the warp before the
-      // .sync.aligned TMEM loads and makes the timeout decision warp-uniform
-      const bool ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl >> 1) & 1, abort_flag));
+      // every lane polls; the warp vote re-converges the warp before the
+      // .sync.aligned TMEM loads, and the four warps then agree through a
+      // double-buffered flag so that all of them take (or skip) the named
+      // barriers below together
+      const bool my_ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl >> 1) & 1, abort_flag));
+      if (lane == 0) s_ready[tl & 1][q] = my_ready ? 1 : 0;
+      epilogue_bar();
+      const bool ready = s_ready[tl & 1][0] && s_ready[tl & 1][1] && s_ready[tl & 1][2] && s_ready[tl & 1][3];
       if (!ready) {
         *abort_flag = 1;
         record_error(args.err, DEV_TIMEOUT_TMEM_FULL);
         break;
       }
       tc_fence_after();
+      const int nsplit = t.split >> 16;
       const bool sh = t.group == args.n_local;
       const int mrow = t.m0 + r;  // row inside this group's A matrix
       const bool row_ok = mrow < (sh ? args.m_limit_shared : args.m_limit_routed);
@@ -279,6 +293,37 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       for (int c0 = 0; c0 < ncol; c0 += 16) {
         float v[16];
         tmem_ld16(taddr + c0, v);
+        if constexpr (BN == kSplitTileRows) {
+          if (nsplit > 1) {
+            // K split: publish this split's partial, count arrivals; the last
+            // split sums all partials in split order and runs the epilogue
+            const int sidx = t.split & 0xffff;
+            float4* mine = reinterpret_cast<float4*>(
+                args.kpart + ((static_cast<size_t>(t.tile_id) * nsplit + sidx) * kBM + r) * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) mine[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            __threadfence();
+            epilogue_bar();
+            if (threadIdx.x == 64) s_last = (atomicAdd(&args.kcount[t.tile_id], 1) == nsplit - 1) ? 1 : 0;
+            epilogue_bar();
+            if (!s_last) break;  // ncol == 16: this was the only chunk
+            __threadfence();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            for (int sp = 0; sp < nsplit; ++sp) {
+              const float4* pp = reinterpret_cast<const float4*>(
+                  args.kpart + ((static_cast<size_t>(t.tile_id) * nsplit + sp) * kBM + r) * 16);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 a = __ldcg(pp + i);
+                v[4 * i] += a.x;
+                v[4 * i + 1] += a.y;
+                v[4 * i + 2] += a.z;
+                v[4 * i + 3] += a.w;
+              }
+            }
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] *= rs;
         if constexpr (!DOWN) {
@@ -319,10 +364,8 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
       const Tile t = args.tiles[ti];
       if (!tile_ok(t)) continue;
-      const bool sh = t.group == args.n_local;
-      const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb, ++it) {
+      for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
@@ -404,7 +447,6 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, i
     a.scale_routed = p.w.s13;
     a.scale_shared = p.w.ss13;
     a.count_index = 0;
-    a.max_tiles = L.max_tiles1;
   } else {
     a.a_routed = p.tm_w2;
     a.a_shared = has_sh ? p.tm_ws2 : p.tm_w2;
@@ -422,7 +464,6 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, i
     a.scale_routed = p.w.s2;
     a.scale_shared = p.w.ss2;
     a.count_index = 1;
-    a.max_tiles = L.max_tiles2;
   }
   a.tiles = reinterpret_cast<const Tile*>(ws + (down ? L.tiles2 : L.tiles1));
   a.tile_count = reinterpret_cast<const int32_t*>(ws + L.tile_count);
@@ -434,9 +475,13 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, i
   a.y_routed = reinterpret_cast<float*>(ws + L.y);
   a.y_shared = reinterpret_cast<float*>(ws + L.y_s);
   a.y_ld = p.H;
+  a.kpart = reinterpret_cast<float*>(ws + L.kpart);
+  a.kcount = reinterpret_cast<int*>(ws + (down ? L.kcount2 : L.kcount1));
   a.err = p.d_err;
-  const int max_tiles = down ? L.max_tiles2 : L.max_tiles1;
-  const int grid = max_tiles < p.num_sms ? max_tiles : p.num_sms;
+  const int max_units = (down ? L.max_tiles2 : L.max_tiles1) * kMaxKSplit;
+  a.max_tiles = max_units;
+  // persistent: one CTA per SM (extra CTAs exit at once when the list is short)
+  const int grid = max_units < p.num_sms ? max_units : p.num_sms;
   if (grid <= 0) return cudaSuccess;
   if (p.int8) return down ? dispatch_bn<true, true>(a, bn, grid, s) : dispatch_bn<false, true>(a, bn, grid, s);
   return down ? dispatch_bn<true, false>(a, bn, grid, s) : dispatch_bn<false, false>(a, bn, grid, s);

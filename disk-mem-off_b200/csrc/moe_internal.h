@@ -19,13 +19,21 @@ constexpr int kMaxTopK = 32;
 
 // One unit of work for the grouped GEMM: weight rows [m0, m0+128) of group
 // `group` (local routed expert index, or n_local for the shared expert)
-// against activation rows [row0, row0 + nvalid) of that group's B matrix.
+// against activation rows [row0, row0 + nvalid) of that group's B matrix, over
+// k-blocks [kb0, kb1).  A tile whose K is split across `nsplit` units carries
+// its split index and a tile id; the unit that finishes last sums the splits.
 struct Tile {
   int group;
   int m0;
   int row0;
   int nvalid;
+  int kb0, kb1;
+  int split;   // split index | (nsplit << 16)
+  int tile_id;
 };
+
+constexpr int kMaxKSplit = 4;       // K splits per tile for small decode batches
+constexpr int kSplitTileRows = 16;  // split-K only with 16-token tiles (BN = 16)
 
 struct DeviceWeights {
   // Packed, HBM-resident weights.  W13 rows are interleaved in groups of 32:
@@ -64,6 +72,8 @@ struct Plan {
 struct WsLayout {
   size_t h16, xg, act, act_s, y, y_s, logits, part, ss_part, rms, counters, ids, wts, sgate;
   size_t bm, hist, base, offsets, perm, slot_row, tiles1, tiles2, tile_count;
+  size_t kpart, kcount1, kcount2;  // split-K partials [units][128][16] f32, per-tile counters
+  int max_split_tiles;             // tiles a launch may split (0 = never)
   size_t total;
   int nchunks, max_tiles1, max_tiles2, bn;
 };

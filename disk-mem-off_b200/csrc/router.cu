@@ -333,18 +333,54 @@ __device__ int block_excl_scan(int v, int* total) {
 
 struct TileArgs {
   int E, T, bn, mt1, mt2, mt1s, has_shared, max1, max2;
+  int nk1, nk1s, nk2, nk2s;        // k-blocks: gate/up routed / shared, down routed / shared
+  int num_sms, max_split_tiles;
   Tile* tiles1;
   Tile* tiles2;
   int32_t* tile_count;
+  int* kcount1;
+  int* kcount2;
   int* err;
 };
 
+// K splits for a list of `c` tiles on `g` persistent CTAs (each split keeps at
+// least kMinSplitKb k-blocks: shorter splits cost more in partial traffic and
+// epilogue hand-offs than the better wave fill gains; measured on the GLM-4.7
+// down projection, K = 1536).  A list that fits in one wave even when split 4 ways is
+// split as far as K allows (less sequential work per CTA); otherwise the
+// smallest s <= 4 that fills the last wave best.  Only small lists are split.
+constexpr int kMinSplitKb = 16;
+
+MOE_DEV int choose_ksplit(int c, int g, int max_split_tiles, int nk_min) {
+  if (c <= 0 || c >= max_split_tiles || g <= 0) return 1;
+  if (c * kMaxKSplit <= g) {
+    int sp = kMaxKSplit;
+    while (sp > 1 && nk_min / sp < kMinSplitKb) --sp;
+    return sp;
+  }
+  int best = 1;
+  float best_eff = 0.f;
+  for (int sp = 1; sp <= kMaxKSplit; ++sp) {
+    if (nk_min / sp < kMinSplitKb) break;
+    const int units = c * sp;
+    const float eff = static_cast<float>(units) / static_cast<float>(((units + g - 1) / g) * g);
+    if (eff > best_eff + 0.02f) {
+      best_eff = eff;
+      best = sp;
+    }
+  }
+  return best;
+}
+
 // Expert e = threadIdx.x owns `cnt` rows starting at `off`.  Writes both GEMM
-// tile lists (expert-major; weight m-tile outer, token tile inner, so a weight
-// tile is reused by neighbouring CTAs while it is in L2) with all threads, then
-// the shared-expert tiles.  Called by every thread of a 1024-thread CTA.
+// unit lists: tiles expert-major (weight m-tile outer, token tile inner, so a
+// weight tile is reused by neighbouring CTAs while it is in L2), the shared
+// expert's tiles last, each tile expanded into its K splits (adjacent units,
+// so the splits of one tile run side by side).  Called by every thread of a
+// 1024-thread CTA.
 __device__ void build_tile_lists(int cnt, int off, const TileArgs& a, int* s_p1, int* s_p2,
                                  int* s_cnt, int* s_off) {
+  __shared__ int s_split[2];
   const int e = threadIdx.x;
   const int ntn = (e < a.E) ? (cnt + a.bn - 1) / a.bn : 0;
   int tot1 = 0, tot2 = 0;
@@ -356,45 +392,63 @@ __device__ void build_tile_lists(int cnt, int off, const TileArgs& a, int* s_p1,
     s_cnt[e] = cnt;
     s_off[e] = off;
   }
+  const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
+  const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
   if (e == 0) {
     s_p1[a.E] = tot1;
     s_p2[a.E] = tot2;
+    s_split[0] = choose_ksplit(c1, a.num_sms, a.max_split_tiles, min(a.nk1, a.has_shared ? a.nk1s : a.nk1));
+    s_split[1] = choose_ksplit(c2, a.num_sms, a.max_split_tiles, min(a.nk2, a.has_shared ? a.nk2s : a.nk2));
+    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_BAD_TILE);
   }
   __syncthreads();
   for (int pass = 0; pass < 2; ++pass) {
     const int* pre = pass ? s_p2 : s_p1;
-    const int total = pass ? tot2 : tot1;
-    const int lim = pass ? a.max2 : a.max1;
+    const int tot = pass ? tot2 : tot1;
+    const int c = min(pass ? c2 : c1, pass ? a.max2 : a.max1);
+    const int nkr = pass ? a.nk2 : a.nk1, nks = pass ? a.nk2s : a.nk1s;
+    const int S = s_split[pass];
     Tile* out = pass ? a.tiles2 : a.tiles1;
-    for (int q = threadIdx.x; q < total && q < lim; q += blockDim.x) {
-      int lo = 0, hi = a.E;  // largest ex with pre[ex] <= q
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (pre[mid] <= q) lo = mid;
-        else hi = mid;
+    int* kcount = pass ? a.kcount2 : a.kcount1;
+    for (int u = threadIdx.x; u < c * S; u += blockDim.x) {
+      const int q = u / S, sidx = u % S;
+      Tile t;
+      int nk;
+      if (q < tot) {
+        int lo = 0, hi = a.E;  // largest ex with pre[ex] <= q
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (pre[mid] <= q) lo = mid;
+          else hi = mid;
+        }
+        const int ex = lo;
+        const int cc = s_cnt[ex];
+        const int nt = (cc + a.bn - 1) / a.bn;
+        const int l = q - pre[ex];
+        const int m = l / nt, n = l % nt;
+        t.group = ex;
+        t.m0 = m * kBM;
+        t.row0 = s_off[ex] + n * a.bn;
+        t.nvalid = min(a.bn, cc - n * a.bn);
+        nk = nkr;
+      } else {
+        const int i = q - tot;
+        const int m = i / nts, n = i % nts;
+        t.group = a.E;
+        t.m0 = m * kBM;
+        t.row0 = n * a.bn;
+        t.nvalid = min(a.bn, a.T - n * a.bn);
+        nk = nks;
       }
-      const int ex = lo;
-      const int c = s_cnt[ex];
-      const int nt = (c + a.bn - 1) / a.bn;
-      const int l = q - pre[ex];
-      const int m = l / nt, n = l % nt;
-      out[q] = Tile{ex, m * kBM, s_off[ex] + n * a.bn, min(a.bn, c - n * a.bn)};
+      t.kb0 = sidx * nk / S;
+      t.kb1 = (sidx + 1) * nk / S;
+      t.split = sidx | (S << 16);
+      t.tile_id = q;
+      out[u] = t;
     }
-  }
-  const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
-  for (int i = threadIdx.x; i < a.mt1s * nts; i += blockDim.x) {
-    const int m = i / nts, n = i % nts;
-    if (tot1 + i < a.max1) a.tiles1[tot1 + i] = Tile{a.E, m * kBM, n * a.bn, min(a.bn, a.T - n * a.bn)};
-  }
-  for (int i = threadIdx.x; i < a.mt2 * nts; i += blockDim.x) {
-    const int m = i / nts, n = i % nts;
-    if (tot2 + i < a.max2) a.tiles2[tot2 + i] = Tile{a.E, m * kBM, n * a.bn, min(a.bn, a.T - n * a.bn)};
-  }
-  if (threadIdx.x == 0) {
-    const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
-    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_BAD_TILE);
-    a.tile_count[0] = min(c1, a.max1);
-    a.tile_count[1] = min(c2, a.max2);
+    if (S > 1)
+      for (int q = threadIdx.x; q < c; q += blockDim.x) kcount[q] = 0;
+    if (threadIdx.x == 0) a.tile_count[pass] = c * S;
   }
 }
 
@@ -532,7 +586,8 @@ __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __rest
 
 // ------------------------------------------------------------------ dispatch
 // Rows [0, T*K): xg[r] = f16(w * (x[token(r)] / rms)); rows [T*K, T*K+T): h16[t]
-// for the shared expert.  One warp per row, 8 elements per lane per step.
+// for the shared expert.  One CTA per row (decode batches have few rows, so
+// the row itself is spread over 256 threads), 8 elements per thread per step.
 __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__ x,
                                                        const float* __restrict__ wn,
                                                        const float* __restrict__ rms,
@@ -540,10 +595,8 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__
                                                        int K, int H, int with_shared,
                                                        __half* __restrict__ xg,
                                                        __half* __restrict__ h16) {
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
   const int rows = T * K + (with_shared ? T : 0);
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nwarps) {
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     int t;
     __half* dst;
     if (r < T * K) {
@@ -556,7 +609,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__
     const float inv = 1.0f / rms[t];
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
     const float4* wr = reinterpret_cast<const float4*>(wn);
-    for (int v = lane; v < (H >> 3); v += 32) {
+    for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) {
       const float4 a0 = xr[2 * v], a1 = xr[2 * v + 1];
       const float4 g0 = wr[2 * v], g1 = wr[2 * v + 1];
       __half2 o[4];
@@ -634,9 +687,17 @@ static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T) {
   ta.has_shared = p.SI > 0;
   ta.max1 = L.max_tiles1;
   ta.max2 = L.max_tiles2;
+  ta.nk1 = (p.H + kBK - 1) / kBK;
+  ta.nk1s = ta.nk1;
+  ta.nk2 = (p.I + kBK - 1) / kBK;
+  ta.nk2s = p.SI > 0 ? (p.SI + kBK - 1) / kBK : ta.nk2;
+  ta.num_sms = p.num_sms;
+  ta.max_split_tiles = L.max_split_tiles;
   ta.tiles1 = reinterpret_cast<Tile*>(ws + L.tiles1);
   ta.tiles2 = reinterpret_cast<Tile*>(ws + L.tiles2);
   ta.tile_count = reinterpret_cast<int32_t*>(ws + L.tile_count);
+  ta.kcount1 = reinterpret_cast<int*>(ws + L.kcount1);
+  ta.kcount2 = reinterpret_cast<int*>(ws + L.kcount2);
   ta.err = p.d_err;
   return ta;
 }
@@ -716,7 +777,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   st = cudaGetLastError();
   if (st != cudaSuccess || !dispatch) return st;
   const int rows = T * K + (p.SI > 0 ? T : 0);
-  dispatch_kernel<<<min((rows + 7) / 8, p.num_sms * 16), 256, 0, s>>>(
+  dispatch_kernel<<<min(rows, p.num_sms * 8), 256, 0, s>>>(
       x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms), perm, T, K, p.H, p.SI > 0,
       reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
   return cudaGetLastError();
