@@ -20,9 +20,9 @@ D2H of the output inside the timed region.
 (offload_runtime/executors/glm4_moe.py:176-240; same numpy expressions) on the
 box's host cores, all BLAS threads, same config, metric and unit.
 
-N > 1 (torchrun): expert-parallel sharding is not wired into this bench yet, so
-each rank runs an independent replica of the layer on its own tokens
-("parallelism": "replicas", weak scaling, no collective in the data path).
+N > 1 (torchrun): expert parallel -- rank r holds routed experts
+[r*160/N, (r+1)*160/N), router and shared expert replicated, 64 tokens per rank
+(weak scaling); dispatch and combine are NCCL all-to-all exchanges of f16 rows.
 """
 from __future__ import annotations
 
@@ -46,12 +46,23 @@ FALLBACK_HBM_GBS = 6650.0
 GLM = dict(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536)
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
 def _peaks() -> tuple[float, str]:
     try:
         with open(PEAKS_FILE) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def _tc_peak() -> float:
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return FALLBACK_BF16_TFLOPS
 
 
 # ------------------------------------------------------------------ clocks
@@ -222,11 +233,180 @@ def _time_steps(fn, steps: int, warmup: int, world: int) -> float:
     return _max_over_ranks(s.elapsed_time(e) / steps, world)
 
 
+# ------------------------------------------------------------------ other configs
+QWEN3 = dict(hidden=2048, n_experts=512, top_k=10, inter=512, shared_inter=512)
+
+
+def _gemm_flops(T: int, k: int, H: int, I: int, SI: int) -> tuple[float, float]:
+    gateup = 2.0 * T * k * 2 * I * H + 2.0 * T * 2 * SI * H
+    down = 2.0 * T * k * I * H + 2.0 * T * SI * H
+    return gateup, down
+
+
+def _measure(ml, T: int, H: int, steps: int, warmup: int, world: int, gen) -> dict:  # noqa: ANN001
+    import torch
+    x = torch.randn((T, H), generator=gen, device="cuda")
+    out = torch.empty_like(x)
+    ws = ml.workspace(T)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step() -> None:
+        ml.forward_ptr(x.data_ptr(), out.data_ptr(), T, ws.data_ptr(), ws.numel(), stream)
+
+    ms = _time_steps(step, steps, warmup, world)
+    ml.status()
+    stage = np.zeros(4)
+    for _ in range(steps):
+        stage += np.array(ml.forward_timed(x, out))
+    stage /= steps
+    ids = ml.route(x)["topk_ids"].cpu().numpy()
+    counts = np.bincount(ids.reshape(-1), minlength=ml.cfg.n_experts)
+    return {"ms": ms, "stage": stage.tolist(), "unique": int((counts > 0).sum()),
+            "max_load": int(counts.max())}
+
+
+def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -> dict:  # noqa: ANN001
+    """BASELINE config 2 (GLM-4.7 INT8, 4096-token prefill, Zipf routing) and
+    config 3 (Qwen3-Coder-Next shape, 1-token decode and 8192-token prefill)."""
+    import torch
+    from moe_sm100 import MoeLayer, MoeLayerConfig
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer
+    gen = torch.Generator(device="cuda").manual_seed(2000 + local)
+    res: dict = {}
+    runs = [
+        ("cfg2_glm47_int8_prefill", dict(GLM, family="glm", expert_dtype="int8", seed=4321,
+                                         zipf_s=1.1, zipf_amp=1.0),
+         dict(weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5), [4096]),
+        ("cfg3_qwen3_next", dict(QWEN3, family="qwen3", expert_dtype="bfloat16", seed=5678),
+         dict(use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
+              rms_norm_eps=1e-6), [1, 8192]),
+    ]
+    for name, spec_kw, cfg_kw, tokens in runs:
+        spec = SyntheticSpec(**spec_kw)
+        blob, meta = build_device_layer(spec, device=f"cuda:{local}")
+        shape = {k: spec_kw[k] for k in ("hidden", "n_experts", "top_k", "inter", "shared_inter")}
+        ml = MoeLayer(MoeLayerConfig(**shape, **cfg_kw, max_tokens=max(tokens), device=local))
+        ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+        torch.cuda.synchronize()
+        del blob
+        H, I, SI, K = shape["hidden"], shape["inter"], shape["shared_inter"], shape["top_k"]
+        wbytes = 1 if cfg_kw.get("weight_format") == "int8" else 2
+        for T in tokens:
+            steps = max(3, min(args.steps, 20 if T > 1024 else args.steps))
+            m = _measure(ml, T, H, steps, args.warmup, world, gen)
+            fg, fd = _gemm_flops(T, K, H, I, SI)
+            entry = {"tokens_per_s": world * T / (m["ms"] * 1e-3), "ms_per_step": m["ms"],
+                     "stage_ms": m["stage"], "unique_experts": m["unique"],
+                     "max_expert_load": m["max_load"]}
+            if T >= 1024:  # prefill: tensor-core bound
+                entry["tc_frac_gateup"] = fg / (m["stage"][1] * 1e-3) / 1e12 / tflops
+                entry["tc_frac_down"] = fd / (m["stage"][2] * 1e-3) / 1e12 / tflops
+                entry["tc_frac_layer"] = (fg + fd) / (m["ms"] * 1e-3) / 1e12 / tflops
+                entry["tflops_layer"] = (fg + fd) / (m["ms"] * 1e-3) / 1e12
+            else:  # decode: weight streaming
+                wb = (m["unique"] + 1) * 3 * H * I * wbytes
+                entry["layer_hbm_frac"] = wb / (m["ms"] * 1e-3) / 1e9 / hbm
+            res[f"{name}_T{T}"] = entry
+        ml.close()
+        torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------ expert parallel (N > 1)
+def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
+    """N GPUs: experts sharded 160/N per rank, T tokens per rank, NCCL all-to-all."""
+    import torch
+    import torch.distributed as dist
+    from moe_sm100 import MoeLayerConfig
+    from moe_sm100.ep import DeviceEPOps, ExpertParallelMoe
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer
+    hbm, peak_kind = _peaks()
+    T = args.tokens
+    spec = SyntheticSpec(**GLM, family="glm", expert_dtype="bfloat16", seed=1234)
+    blob, meta = build_device_layer(spec, device=f"cuda:{local}")
+    cfg = MoeLayerConfig(**GLM, routed_scaling_factor=2.5, rms_norm_eps=1e-5, max_tokens=T,
+                         device=local)
+    ops = DeviceEPOps(cfg, rank, world)
+    ops.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    del blob
+    torch.cuda.empty_cache()
+    ep = ExpertParallelMoe(ops)
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
+
+    with ClockSampler(local) as clk:
+        ms = _time_steps(lambda: ep.forward(x), args.steps, args.warmup, world)
+    clocks = clk.summary()
+    ops.status()
+    # one instrumented forward per rank: share of the exchanges in the layer time
+    tim = []
+    for _ in range(max(3, min(args.steps, 10))):
+        ep.forward(x, timed=True)
+        tim.append(ep.last_timing)
+    a2a = float(np.median([t["a2a_ms"] for t in tim]))
+    tot = float(np.median([t["total_ms"] for t in tim]))
+    a2a_frac = _max_over_ranks(a2a / tot, world)
+    recv = int(np.median([t["recv_rows"] for t in tim]))
+    # end-to-end with host buffers
+    x_host = x.cpu().numpy()
+    pin = torch.from_numpy(x_host).pin_memory()
+    out_pin = torch.empty_like(pin).pin_memory()
+
+    def e2e_step() -> None:
+        xd = pin.to(f"cuda:{local}", non_blocking=True)
+        out_pin.copy_(ep.forward(xd), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    _barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    # expert weight bytes this rank streams per step (its touched local experts + shared)
+    e_loc = GLM["n_experts"] // world
+    layer_bytes = (min(e_loc, recv) + 1) * 3 * GLM["hidden"] * GLM["inter"] * 2
+    frac = layer_bytes / (ms * 1e-3) / 1e9 / hbm
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoE-layer tokens/s (GLM-4.7-shape decode) and % of HBM roofline",
+            "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 MMA / fp32 accumulate (bf16-valued weights); fp32 routing; f16 exchange",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, random-init)",
+            "config": {"workload": "BASELINE config 1 shape, expert parallel",
+                       "tokens_per_rank": T, "experts_per_rank": e_loc,
+                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)",
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (rank 0)",
+                         "achieved": layer_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": frac, "peak_source": peak_kind, "traffic": None},
+            "a2a_frac_of_layer": a2a_frac, "recv_rows_rank0": recv,
+            "e2e": {"value": world * T / e2e_s, "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * GLM["hidden"] * 4,
+                    "d2h_bytes_per_step": T * GLM["hidden"] * 4, "ms_per_step": e2e_s * 1e3},
+            "cpu_baseline": None,
+            # per forward: router, tail, dispatch, send metadata; hist, scan, scatter,
+            # gather, two GEMMs (experts); scan, two GEMMs (shared); combine
+            "gpu_launches": 14 * args.steps,
+            "clocks": clocks,
+        }))
+    ops.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ arms
 def run_ours(args) -> None:  # noqa: ANN001
     import torch
     world, rank, local = _dist_init()
     torch.cuda.set_device(local)
+    if world > 1:
+        run_ep(args, world, rank, local)
+        return
     hbm, peak_kind = _peaks()
     T_main = args.tokens
     ml, blob, meta = _make_layer(local, seed=1234, max_tokens=max(64, T_main))
@@ -281,6 +461,12 @@ def run_ours(args) -> None:  # noqa: ANN001
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_sample(blob, meta, x_host)
+    other = {}
+    if not args.no_sub and not args.no_other:
+        ml.close()
+        del blob
+        torch.cuda.empty_cache()
+        other = run_other_configs(args, local, world, hbm, _tc_peak())
 
     sub = {}
     for T, r in results.items():
@@ -331,9 +517,12 @@ def run_ours(args) -> None:  # noqa: ANN001
                     "d2h_bytes_per_step": T_main * GLM["hidden"] * 4,
                     "ms_per_step": e2e_s * 1e3},
             "cpu_baseline": cpu,
-            "gpu_launches": 9 * args.steps,
+            # our kernels per forward: router, decode tail (T <= 256; else top-k,
+            # histogram, scan, scatter), dispatch, two grouped GEMMs, combine
+            "gpu_launches": (6 if T_main <= 256 else 9) * args.steps,
             "clocks": clocks,
             "sub": sub,
+            "other_configs": other,
         }
         print(json.dumps(line))
     ml.close()
@@ -400,6 +589,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-sub", action="store_true", help="only the --tokens batch (no T=1/8 lines)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
+    ap.add_argument("--no-other", action="store_true",
+                    help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
     args = ap.parse_args()

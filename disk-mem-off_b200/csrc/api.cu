@@ -85,17 +85,23 @@ static int pick_bn(int T) {
   return 256;
 }
 
-WsLayout ws_layout(const Plan& p, int T) {
+// Workspace for `rows` (tokens or received rows) x `k` routed slots over
+// `groups` expert groups; `shared_rows` rows for the shared expert; the router
+// buffers only when `router`.
+static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, int shared_rows,
+                                  int bn, bool router) {
   WsLayout L{};
-  const size_t R = static_cast<size_t>(T) * p.K;
-  const int E = p.E;
-  L.bn = pick_bn(T);
+  const int T = rows;
+  const size_t R = static_cast<size_t>(T) * k;
+  const int E = groups;
+  const int TS = shared_rows;
+  L.bn = bn;
   L.nchunks = (T + kPermChunk - 1) / kPermChunk;
   const int mt1 = (2 * p.I + kBM - 1) / kBM;
   const int mt2 = (p.H + kBM - 1) / kBM;
-  const int mt1s = p.SI > 0 ? (2 * p.SI + kBM - 1) / kBM : 0;
+  const int mt1s = (p.SI > 0 && TS > 0) ? (2 * p.SI + kBM - 1) / kBM : 0;
   const int ntr = static_cast<int>((R + L.bn - 1) / L.bn) + static_cast<int>(R < (size_t)E ? R : E);
-  const int nts = p.SI > 0 ? (T + L.bn - 1) / L.bn : 0;
+  const int nts = (p.SI > 0 && TS > 0) ? (TS + L.bn - 1) / L.bn : 0;
   L.max_tiles1 = ntr * mt1 + nts * mt1s;
   L.max_tiles2 = ntr * mt2 + nts * mt2;
   size_t o = 0;
@@ -104,21 +110,23 @@ WsLayout ws_layout(const Plan& p, int T) {
     o = align256(o + bytes);
     return at;
   };
-  L.h16 = take(static_cast<size_t>(T) * p.H * 2);
+  L.h16 = take(static_cast<size_t>(TS) * p.H * 2);
   L.xg = take(R * p.H * 2);
   L.act = take(R * p.I * 2);
-  L.act_s = take(static_cast<size_t>(T) * p.SI * 2);
-  L.y = take(R * p.H * 4);
-  L.y_s = take(p.SI > 0 ? static_cast<size_t>(T) * p.H * 4 : 0);
-  const RouterGeom g = router_geometry(p, T);
-  L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
-  L.part = take(g.splits > 1 ? static_cast<size_t>(g.splits) * T * p.router_rows * 4 : 0);
-  L.ss_part = take(static_cast<size_t>(g.rx) * g.splits * T * 4);
-  L.rms = take(static_cast<size_t>(T) * 4);
-  L.counters = take(static_cast<size_t>(g.rx) * g.tz * 4);
-  L.ids = take(R * 4);
-  L.wts = take(R * 4);
-  L.sgate = take(static_cast<size_t>(T) * 4);
+  L.act_s = take(static_cast<size_t>(TS) * p.SI * 2);
+  L.y = take(router ? R * p.H * 4 : 0);
+  L.y_s = take(p.SI > 0 ? static_cast<size_t>(TS) * p.H * 4 : 0);
+  if (router) {
+    const RouterGeom g = router_geometry(p, T);
+    L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
+    L.part = take(g.splits > 1 ? static_cast<size_t>(g.splits) * T * p.router_rows * 4 : 0);
+    L.ss_part = take(static_cast<size_t>(g.rx) * g.splits * T * 4);
+    L.rms = take(static_cast<size_t>(T) * 4);
+    L.counters = take(static_cast<size_t>(g.rx) * g.tz * 4);
+    L.ids = take(R * 4);
+    L.wts = take(R * 4);
+    L.sgate = take(static_cast<size_t>(T) * 4);
+  }
   L.bm = take(static_cast<size_t>(L.nchunks) * E * 32 * 4);
   L.hist = take(static_cast<size_t>(L.nchunks) * E * 4);
   L.base = take(static_cast<size_t>(L.nchunks) * E * 4);
@@ -136,6 +144,17 @@ WsLayout ws_layout(const Plan& p, int T) {
   L.kcount2 = take(static_cast<size_t>(L.max_split_tiles) * 4);
   L.total = o;
   return L;
+}
+
+WsLayout ws_layout(const Plan& p, int T) {
+  return ws_layout_general(p, T, p.K, p.E, p.SI > 0 ? T : 0, pick_bn(T), true);
+}
+
+// Expert side of the expert-parallel path: R received rows grouped by the
+// n_local resident experts, no router, no shared expert.
+WsLayout ws_layout_ep_experts(const Plan& p, int R) {
+  const int per_expert = (2 * R + p.n_local - 1) / (p.n_local > 0 ? p.n_local : 1);
+  return ws_layout_general(p, R, 1, p.n_local, 0, pick_bn(per_expert > 0 ? per_expert : 1), false);
 }
 
 // ------------------------------------------------------------ name parsing
@@ -250,8 +269,9 @@ int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan) {
   int eb = c.expert_begin, ee = c.expert_end;
   if (eb == 0 && ee == 0) ee = c.n_experts;
   if (eb < 0 || ee > c.n_experts || eb >= ee) return fail(MOE_ERR_INVALID, "bad expert range");
-  if (eb != 0 || ee != c.n_experts)
-    return fail(MOE_ERR_UNSUPPORTED, "expert ranges are served by the expert-parallel entry points");
+  if (c.n_experts % (ee - eb) != 0 || eb % (ee - eb) != 0)
+    return fail(MOE_ERR_INVALID,
+                "expert share must be one of n_experts / share equal contiguous ranges");
 
   MOE_CUDA(cudaSetDevice(c.device));
   MoePlan* plan = new MoePlan();
@@ -510,6 +530,9 @@ uint64_t moe_workspace_bytes(const MoePlan* plan, int32_t T) {
 static int check_call(const MoePlan* plan, int32_t T, const void* ws, uint64_t ws_bytes) {
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
   if (!plan->p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
+  if (plan->p.n_local != plan->p.E)
+    return fail(MOE_ERR_UNSUPPORTED,
+                "this plan holds a share of the experts: use the moe_ep_* entry points");
   if (T < 0 || T > plan->p.cfg.max_tokens)
     return fail(MOE_ERR_INVALID, "T outside [0, max_tokens]");
   if (T == 0) return MOE_OK;
@@ -620,6 +643,103 @@ int moe_status(MoePlan* plan, void* stream) {
   if (h >= DEV_TIMEOUT_FULL && h <= DEV_TIMEOUT_CONV)
     return fail(MOE_ERR_TIMEOUT, "a device-side wait ran out of time (code " + std::to_string(h) + ")");
   return fail(MOE_ERR_DEVICE, "a kernel reported device error code " + std::to_string(h));
+}
+
+// ------------------------------------------------------------ expert parallel
+static int check_ep(const MoePlan* plan, int32_t n, const void* ws, uint64_t ws_bytes,
+                    uint64_t need) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  if (!plan->p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
+  if (n < 0) return fail(MOE_ERR_INVALID, "negative row count");
+  if (n == 0) return MOE_OK;
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return fail(MOE_ERR_WORKSPACE, "workspace must be a 256-byte aligned device pointer");
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE, "workspace too small");
+  return MOE_OK;
+}
+
+int moe_ep_dispatch(MoePlan* plan, const float* x_dev, int32_t T, void* send_rows,
+                    int32_t* send_experts, int32_t* send_offsets, void* workspace,
+                    uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T above max_tokens");
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK) return rc;
+  if (!send_offsets) return fail(MOE_ERR_INVALID, "null send_offsets");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    MOE_CUDA(cudaMemsetAsync(send_offsets, 0, sizeof(int32_t) * (p.E / p.n_local + 1), s));
+    return MOE_OK;
+  }
+  if (!x_dev || !send_rows || !send_experts) return fail(MOE_ERR_INVALID, "null argument");
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_route(p, L, ws, x_dev, T, true, s, static_cast<__half*>(send_rows)));
+  MOE_CUDA(launch_ep_meta(p, reinterpret_cast<int32_t*>(ws + L.perm),
+                          reinterpret_cast<int32_t*>(ws + L.ids),
+                          reinterpret_cast<int32_t*>(ws + L.offsets), T * p.K, send_experts,
+                          send_offsets, s));
+  return MOE_OK;
+}
+
+uint64_t moe_ep_workspace_bytes(const MoePlan* plan, int32_t R) {
+  if (!plan || R <= 0) return 0;
+  return ws_layout_ep_experts(plan->p, R).total;
+}
+
+int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_experts, int32_t R,
+                   void* y_out, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  int rc = check_ep(plan, R, workspace, workspace_bytes,
+                    R > 0 ? ws_layout_ep_experts(p, R).total : 0);
+  if (rc != MOE_OK || R == 0) return rc;
+  if (!recv_rows || !recv_experts || !y_out) return fail(MOE_ERR_INVALID, "null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout_ep_experts(p, R);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_group_rows(p, L, ws, recv_experts, static_cast<const __half*>(recv_rows), R, s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true,
+                       GemmIO{R, 0, static_cast<__half*>(y_out),
+                              reinterpret_cast<const int32_t*>(ws + L.perm)},
+                       s));
+  return MOE_OK;
+}
+
+int moe_ep_shared(MoePlan* plan, int32_t T, void* workspace, uint64_t workspace_bytes,
+                  void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK || T == 0 || p.SI == 0) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_shared_tiles(p, L, ws, T, s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{T * p.K, T, nullptr, nullptr}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, GemmIO{T * p.K, T, nullptr, nullptr}, s));
+  return MOE_OK;
+}
+
+int moe_ep_combine(MoePlan* plan, const float* x_dev, int32_t T, const void* y_back,
+                   float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK || T == 0) return rc;
+  if (!x_dev || !y_back || !out_dev) return fail(MOE_ERR_INVALID, "null argument");
+  if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_combine_half(p, x_dev, static_cast<const __half*>(y_back),
+                               reinterpret_cast<float*>(ws + L.y_s),
+                               reinterpret_cast<int32_t*>(ws + L.slot_row),
+                               reinterpret_cast<float*>(ws + L.wts),
+                               reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
+  return MOE_OK;
 }
 
 // ------------------------------------------------------------ runtime wrappers

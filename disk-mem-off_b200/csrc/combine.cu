@@ -12,8 +12,20 @@
 
 namespace moe {
 
+// Expert rows as fp32 (single GPU) or f16 (returned over the expert-parallel exchange).
+MOE_DEV float4 load_row4(const float* y, size_t row, int H, int v) {
+  return reinterpret_cast<const float4*>(y + row * H)[v];
+}
+MOE_DEV float4 load_row4(const __half* y, size_t row, int H, int v) {
+  const uint2 raw = reinterpret_cast<const uint2*>(y + row * H)[v];
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename YT>
 __global__ void __launch_bounds__(256) combine_kernel(
-    const float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ y_s,
+    const float* __restrict__ x, const YT* __restrict__ y, const float* __restrict__ y_s,
     const int32_t* __restrict__ slot_row, const float* __restrict__ wts,
     const float* __restrict__ sgate, float* __restrict__ out, int K, int H) {
   const int t = blockIdx.y;
@@ -23,7 +35,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
   for (int j = 0; j < K; ++j) {
     const int row = slot_row[t * K + j];
     const float w = wts[t * K + j];
-    const float4 yv = reinterpret_cast<const float4*>(y + static_cast<size_t>(row) * H)[v];
+    const float4 yv = load_row4(y, static_cast<size_t>(row), H, v);
     acc.x = __fadd_rn(acc.x, __fmul_rn(w, yv.x));
     acc.y = __fadd_rn(acc.y, __fmul_rn(w, yv.y));
     acc.z = __fadd_rn(acc.z, __fmul_rn(w, yv.z));
@@ -57,8 +69,41 @@ cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const 
                            float* out, int T, cudaStream_t s) {
   const int nv = p.H >> 2;
   dim3 grid((nv + 255) / 256, T);
-  combine_kernel<<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
-                                      p.cfg.has_shared_gate ? sgate : nullptr, out, p.K, p.H);
+  combine_kernel<float><<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
+                                             p.cfg.has_shared_gate ? sgate : nullptr, out, p.K,
+                                             p.H);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_half(const Plan& p, const float* x, const __half* y, const float* y_s,
+                                const int32_t* slot_row, const float* wts, const float* sgate,
+                                float* out, int T, cudaStream_t s) {
+  const int nv = p.H >> 2;
+  dim3 grid((nv + 255) / 256, T);
+  combine_kernel<__half><<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
+                                              p.cfg.has_shared_gate ? sgate : nullptr, out, p.K,
+                                              p.H);
+  return cudaGetLastError();
+}
+
+// Expert-parallel send metadata: the local expert id (on its owner rank) of every
+// send row, and where each destination rank's rows start.
+__global__ void ep_meta_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ ids,
+                               const int32_t* __restrict__ offsets, int n, int e_loc, int world,
+                               int E, int32_t* __restrict__ send_experts,
+                               int32_t* __restrict__ send_offsets) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x)
+    send_experts[r] = ids[perm[r]] % e_loc;
+  if (blockIdx.x == 0)
+    for (int d = threadIdx.x; d <= world; d += blockDim.x) send_offsets[d] = offsets[min(d * e_loc, E)];
+}
+
+cudaError_t launch_ep_meta(const Plan& p, const int32_t* perm, const int32_t* ids,
+                           const int32_t* offsets, int n, int32_t* send_experts,
+                           int32_t* send_offsets, cudaStream_t s) {
+  const int world = p.E / p.n_local;
+  ep_meta_kernel<<<max(1, min((n + 255) / 256, p.num_sms * 4)), 256, 0, s>>>(
+      perm, ids, offsets, n, p.n_local, world, p.E, send_experts, send_offsets);
   return cudaGetLastError();
 }
 

@@ -47,6 +47,8 @@ struct GemmArgs {
   float* y_routed;       // down outputs [rows][H]
   float* y_shared;       // [T][H]
   int y_ld;
+  __half* y_half;        // if set: routed down outputs as f16 at row y_row_map[row] (or row)
+  const int32_t* y_row_map;
   const float* scale_routed;  // int8 row scales [groups * rows_a]
   const float* scale_shared;  // [m_limit_shared]
   float* kpart;               // split-K partials [tile_id * nsplit + split][128][16] f32
@@ -345,11 +347,22 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
             }
           }
         } else {
-          float* dst = sh ? args.y_shared : args.y_routed;
+          if (!sh && args.y_half) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c0 + i;
-            if (col < t.nvalid && row_ok) dst[static_cast<size_t>(t.row0 + col) * args.y_ld + mrow] = v[i];
+            for (int i = 0; i < 16; ++i) {
+              const int col = c0 + i;
+              if (col < t.nvalid && row_ok) {
+                const int orow = args.y_row_map ? args.y_row_map[t.row0 + col] : t.row0 + col;
+                args.y_half[static_cast<size_t>(orow) * args.y_ld + mrow] = __float2half_rn(v[i]);
+              }
+            }
+          } else {
+            float* dst = sh ? args.y_shared : args.y_routed;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c0 + i;
+              if (col < t.nvalid && row_ok) dst[static_cast<size_t>(t.row0 + col) * args.y_ld + mrow] = v[i];
+            }
           }
         }
       }
@@ -422,9 +435,15 @@ static cudaError_t dispatch_bn(const GemmArgs& a, int bn, int grid, cudaStream_t
 
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
                         cudaStream_t s) {
+  return launch_gemm(p, L, ws, down, GemmIO{T * p.K, T, nullptr, nullptr}, s);
+}
+
+cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
+                        cudaStream_t s) {
   GemmArgs a;
   std::string err;
-  const int rows = T * p.K;
+  const int rows = io.routed_rows;
+  const int T = io.shared_rows;
   const int bn = L.bn;
   const bool has_sh = p.SI > 0;
   __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
@@ -475,6 +494,8 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, i
   a.y_routed = reinterpret_cast<float*>(ws + L.y);
   a.y_shared = reinterpret_cast<float*>(ws + L.y_s);
   a.y_ld = p.H;
+  a.y_half = io.y_half;
+  a.y_row_map = io.y_row_map;
   a.kpart = reinterpret_cast<float*>(ws + L.kpart);
   a.kcount = reinterpret_cast<int*>(ws + (down ? L.kcount2 : L.kcount1));
   a.err = p.d_err;

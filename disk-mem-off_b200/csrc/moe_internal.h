@@ -79,6 +79,7 @@ struct WsLayout {
 };
 
 WsLayout ws_layout(const Plan& p, int T);
+WsLayout ws_layout_ep_experts(const Plan& p, int R);
 
 // Router launch geometry: rx router-row tiles x splits K-splits x tz token tiles.
 struct RouterGeom {
@@ -93,12 +94,35 @@ bool route_uses_tail(const Plan& p, int T);
 // Router (+ RMSNorm), top-k, permutation and tile lists; with `dispatch` also
 // the normalised f16 rows of every routed slot (xg) and of the shared expert (h16).
 cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
-                         bool dispatch, cudaStream_t s);
+                         bool dispatch, cudaStream_t s, __half* xg_out = nullptr);
+// Expert-parallel helpers: group `n` received rows by their local expert key
+// (stable: receive order inside an expert), gather them into L.xg and build the
+// tile lists; and the tile lists of the shared expert alone for T local tokens.
+cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
+                              const __half* rows, int n, cudaStream_t s);
+cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
+                        cudaStream_t s);
+// Rows of the routed / shared B operands and an optional f16 routed output
+// (expert-parallel path: written straight into receive order through y_row_map).
+struct GemmIO {
+  int routed_rows;
+  int shared_rows;
+  __half* y_half;
+  const int32_t* y_row_map;
+};
+cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
                         cudaStream_t s);
 cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,
                            const int32_t* slot_row, const float* wts, const float* sgate,
                            float* out, int T, cudaStream_t s);
+
+cudaError_t launch_combine_half(const Plan& p, const float* x, const __half* y, const float* y_s,
+                                const int32_t* slot_row, const float* wts, const float* sgate,
+                                float* out, int T, cudaStream_t s);
+cudaError_t launch_ep_meta(const Plan& p, const int32_t* perm, const int32_t* ids,
+                           const int32_t* offsets, int n, int32_t* send_experts,
+                           int32_t* send_offsets, cudaStream_t s);
 
 // weight packing (bind)
 cudaError_t launch_pack_rows(const void* src, int src_dtype, void* dst, bool to_int8,

@@ -69,6 +69,9 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
   Plan& p = plan->p;
   if (!p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
+  if (p.n_local != p.E)
+    return fail(MOE_ERR_UNSUPPORTED,
+                "this plan holds a share of the experts: use the moe_ep_* entry points");
   if (T < 0 || T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T outside [0, max_tokens]");
   if (T == 0) return MOE_OK;
   if (!x_dev || !out_dev) return fail(MOE_ERR_INVALID, "null x / out");

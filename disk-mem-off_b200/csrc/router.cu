@@ -676,15 +676,16 @@ static cudaError_t run_router(const Plan& p, const WsLayout& L, char* ws, const 
   return cudaGetLastError();
 }
 
-static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T) {
+static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T, int groups,
+                          bool shared) {
   TileArgs ta;
-  ta.E = p.E;
+  ta.E = groups;
   ta.T = T;
   ta.bn = L.bn;
   ta.mt1 = (2 * p.I + kBM - 1) / kBM;
   ta.mt2 = (p.H + kBM - 1) / kBM;
-  ta.mt1s = p.SI > 0 ? (2 * p.SI + kBM - 1) / kBM : 0;
-  ta.has_shared = p.SI > 0;
+  ta.mt1s = (shared && p.SI > 0) ? (2 * p.SI + kBM - 1) / kBM : 0;
+  ta.has_shared = shared && p.SI > 0;
   ta.max1 = L.max_tiles1;
   ta.max2 = L.max_tiles2;
   ta.nk1 = (p.H + kBK - 1) / kBK;
@@ -705,7 +706,7 @@ static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T) {
 bool route_uses_tail(const Plan& p, int T) { return T <= kTailMaxT && T * p.K <= 8192; }
 
 cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
-                         bool dispatch, cudaStream_t s) {
+                         bool dispatch, cudaStream_t s, __half* xg_out) {
   cudaError_t st = (router_bt(T) == 16) ? run_router<16>(p, L, ws, x, T, s)
                                         : run_router<64>(p, L, ws, x, T, s);
   if (st != cudaSuccess) return st;
@@ -718,7 +719,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
   int32_t* perm = reinterpret_cast<int32_t*>(ws + L.perm);
   int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
-  const TileArgs ta = tile_args(p, L, ws, T);
+  const TileArgs ta = tile_args(p, L, ws, T, p.E, true);
   const int vpl = (E + 31) / 32;
   if (route_uses_tail(p, T)) {
     const int words = (T + 31) / 32;
@@ -779,7 +780,58 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   const int rows = T * K + (p.SI > 0 ? T : 0);
   dispatch_kernel<<<min(rows, p.num_sms * 8), 256, 0, s>>>(
       x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms), perm, T, K, p.H, p.SI > 0,
-      reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
+      xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ expert-parallel helpers
+// dst[s] = src[perm[s]] for f16 rows of H elements (one CTA per row).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ src,
+                                                          const int32_t* __restrict__ perm, int n,
+                                                          int H, __half* __restrict__ dst) {
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r]) * H);
+    uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * H);
+    for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
+  }
+}
+
+cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
+                              const __half* rows, int n, cudaStream_t s) {
+  const int E = p.n_local;
+  uint32_t* bmg = reinterpret_cast<uint32_t*>(ws + L.bm);
+  int32_t* hist = reinterpret_cast<int32_t*>(ws + L.hist);
+  int32_t* base = reinterpret_cast<int32_t*>(ws + L.base);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* perm = reinterpret_cast<int32_t*>(ws + L.perm);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
+  const TileArgs ta = tile_args(p, L, ws, 0, E, false);
+  static bool done_hist[64] = {};
+  cudaError_t st = set_smem_attr(reinterpret_cast<const void*>(perm_hist_kernel),
+                                 1024 * 32 * sizeof(uint32_t), done_hist);
+  if (st != cudaSuccess) return st;
+  if (n > 0) {
+    perm_hist_kernel<<<L.nchunks, 1024, static_cast<size_t>(E) * 32 * sizeof(uint32_t), s>>>(
+        keys, n, 1, E, bmg, hist, p.d_err);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+  }
+  perm_scan_kernel<<<1, 1024, 0, s>>>(hist, L.nchunks, base, offsets, ta);
+  st = cudaGetLastError();
+  if (st != cudaSuccess || n == 0) return st;
+  perm_scatter_kernel<<<min((n + 255) / 256, p.num_sms * 8), 256, 0, s>>>(keys, bmg, base, n, 1, E,
+                                                                         perm, slot_row);
+  st = cudaGetLastError();
+  if (st != cudaSuccess) return st;
+  gather_rows_kernel<<<min(n, p.num_sms * 8), 256, 0, s>>>(rows, perm, n, p.H,
+                                                          reinterpret_cast<__half*>(ws + L.xg));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s) {
+  const TileArgs ta = tile_args(p, L, ws, T, 0, true);
+  perm_scan_kernel<<<1, 1024, 0, s>>>(nullptr, 0, nullptr, reinterpret_cast<int32_t*>(ws + L.offsets),
+                                      ta);
   return cudaGetLastError();
 }
 

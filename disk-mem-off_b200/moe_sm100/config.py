@@ -28,6 +28,8 @@ class MoeLayerConfig:
     rms_norm_eps: float = 1e-6
     max_tokens: int = 4096
     device: int = 0
+    expert_begin: int = 0            # expert parallel: this rank's share [begin, end)
+    expert_end: int = 0              # 0, 0 = all experts
 
     def to_c(self) -> _lib.MoeConfigC:
         if self.score_func not in SCORE_FUNCS:
@@ -42,7 +44,7 @@ class MoeLayerConfig:
             weight_format=WEIGHT_FORMATS[self.weight_format],
             routed_scaling_factor=float(self.routed_scaling_factor),
             rms_norm_eps=float(self.rms_norm_eps), max_tokens=self.max_tokens,
-            expert_begin=0, expert_end=0, device=self.device)
+            expert_begin=self.expert_begin, expert_end=self.expert_end, device=self.device)
 
     def with_shapes(self, inter: int, shared_inter: int, has_shared_gate: bool) -> "MoeLayerConfig":
         return replace(self, inter=inter, shared_inter=shared_inter, has_shared_gate=has_shared_gate)

@@ -1,0 +1,176 @@
+"""Expert-parallel MoE layer: one process per GPU, experts sharded across ranks.
+
+Rank r of N holds routed experts [r*E/N, (r+1)*E/N) (packed from the same layer
+blob), the router and the shared expert are replicated, and every rank routes its
+own tokens.  One forward (weak scaling: T tokens per rank):
+
+  1. dispatch   route the local tokens; normalised f16 rows grouped by owner rank
+  2. counts     all_to_all of the per-rank row counts (the only host sync)
+  3. exchange   all_to_all of the rows and of their local expert ids
+  4. experts    grouped GEMMs of the resident experts on the received rows
+  5. return     all_to_all of the f16 expert outputs back to their source rank
+  6. combine    x + sum_k w * y + shared expert
+
+The exchanges are torch.distributed collectives (NCCL over NVLink on B200; gloo
+on CPU in the tests).  The device work is libmoe_sm100's moe_ep_* entry points.
+"""
+from __future__ import annotations
+
+from ctypes import c_void_p
+from dataclasses import replace
+from typing import Any, Protocol
+
+from ._lib import check, lib
+from .config import MoeLayerConfig
+from .layer import MoeLayer, _stream_handle
+
+
+def _torch():
+    import torch
+    return torch
+
+
+class EPOps(Protocol):
+    """Per-rank compute of the expert-parallel block (device or test stand-in)."""
+
+    def dispatch(self, x: Any) -> tuple[Any, Any, Any]: ...      # rows, local expert ids, offsets
+
+    def experts(self, rows: Any, expert_ids: Any) -> Any: ...   # expert outputs, same order
+
+    def combine(self, x: Any, y_back: Any) -> Any: ...          # x + MoE(x)
+
+
+class ExpertParallelMoe:
+    """Runs the dispatch / expert / combine protocol of one rank."""
+
+    def __init__(self, ops: EPOps, group: Any = None) -> None:
+        self.ops = ops
+        self.group = group
+        self.last_timing: dict[str, float] = {}
+
+    def forward(self, x: Any, timed: bool = False) -> Any:
+        torch = _torch()
+        import torch.distributed as dist
+        g = self.group
+        ev = {}
+
+        def mark(name: str) -> None:
+            if timed and x.is_cuda:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                ev[name] = e
+
+        mark("start")
+        send_rows, send_experts, send_offsets = self.ops.dispatch(x)
+        mark("dispatched")
+        offs = send_offsets.tolist()
+        if len(offs) != dist.get_world_size(g) + 1 or offs[0] != 0 or offs[-1] != send_rows.shape[0] \
+                or any(b < a for a, b in zip(offs, offs[1:])):
+            raise ValueError(f"malformed send offsets {offs} for {send_rows.shape[0]} rows")
+        send_counts = (send_offsets[1:] - send_offsets[:-1]).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=g)
+        sc = send_counts.tolist()
+        rc = recv_counts.tolist()
+        n_recv = int(sum(rc))
+        h = send_rows.shape[1]
+        recv_rows = send_rows.new_empty((n_recv, h))
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=g)
+        recv_experts = send_experts.new_empty((n_recv,))
+        dist.all_to_all_single(recv_experts, send_experts, rc, sc, group=g)
+        mark("exchanged")
+        y = self.ops.experts(recv_rows, recv_experts)
+        mark("computed")
+        y_back = y.new_empty((send_rows.shape[0], h))
+        dist.all_to_all_single(y_back, y, sc, rc, group=g)
+        mark("returned")
+        out = self.ops.combine(x, y_back)
+        mark("end")
+        if timed and x.is_cuda:
+            torch.cuda.synchronize()
+            t = lambda a, b: ev[a].elapsed_time(ev[b])  # noqa: E731
+            self.last_timing = {
+                "dispatch_ms": t("start", "dispatched"),
+                "a2a_ms": t("dispatched", "exchanged") + t("computed", "returned"),
+                "experts_ms": t("exchanged", "computed"),
+                "combine_ms": t("returned", "end"),
+                "total_ms": t("start", "end"),
+                "recv_rows": n_recv,
+            }
+        return out
+
+
+class DeviceEPOps:
+    """EPOps over libmoe_sm100 for this rank's expert share (CUDA tensors)."""
+
+    def __init__(self, cfg: MoeLayerConfig, rank: int, world: int) -> None:
+        if cfg.n_experts % world:
+            raise ValueError("n_experts must be divisible by the number of ranks")
+        e_loc = cfg.n_experts // world
+        self.cfg = replace(cfg, expert_begin=rank * e_loc, expert_end=(rank + 1) * e_loc)
+        self.layer = MoeLayer(self.cfg)
+        self.world = world
+        self._ws = None
+        self._ws_ep = None
+        self._T = 0
+
+    def bind_device(self, blob_ptr: int, blob_bytes: int, tensor_meta: list[dict[str, Any]],
+                    stream: Any = None) -> None:
+        self.layer.bind_device(blob_ptr, blob_bytes, tensor_meta, stream)
+
+    def _buf(self, attr: str, nbytes: int) -> Any:
+        torch = _torch()
+        cur = getattr(self, attr)
+        if cur is None or cur.numel() < nbytes:
+            cur = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=f"cuda:{self.cfg.device}")
+            setattr(self, attr, cur)
+        return cur
+
+    def dispatch(self, x: Any) -> tuple[Any, Any, Any]:
+        torch = _torch()
+        t = x.shape[0]
+        k, h = self.cfg.top_k, self.cfg.hidden
+        plan = self.layer._plan
+        ws = self._buf("_ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
+        rows = torch.empty((t * k, h), dtype=torch.float16, device=x.device)
+        experts = torch.empty((t * k,), dtype=torch.int32, device=x.device)
+        offsets = torch.empty((self.world + 1,), dtype=torch.int32, device=x.device)
+        check(lib().moe_ep_dispatch(plan, c_void_p(x.data_ptr()), t, c_void_p(rows.data_ptr()),
+                                    c_void_p(experts.data_ptr()), c_void_p(offsets.data_ptr()),
+                                    c_void_p(ws.data_ptr()), ws.numel(),
+                                    c_void_p(_stream_handle(None))))
+        self._T = t
+        return rows, experts, offsets
+
+    def experts(self, rows: Any, expert_ids: Any) -> Any:
+        torch = _torch()
+        r = rows.shape[0]
+        y = torch.empty((r, self.cfg.hidden), dtype=torch.float16, device=rows.device)
+        if r == 0:
+            return y
+        plan = self.layer._plan
+        ws = self._buf("_ws_ep", int(lib().moe_ep_workspace_bytes(plan, r)))
+        check(lib().moe_ep_experts(plan, c_void_p(rows.data_ptr()), c_void_p(expert_ids.data_ptr()),
+                                   r, c_void_p(y.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(),
+                                   c_void_p(_stream_handle(None))))
+        return y
+
+    def combine(self, x: Any, y_back: Any) -> Any:
+        torch = _torch()
+        out = torch.empty_like(x)
+        t = x.shape[0]
+        if t == 0:
+            return out
+        plan = self.layer._plan
+        ws = self._ws
+        s = c_void_p(_stream_handle(None))
+        check(lib().moe_ep_shared(plan, t, c_void_p(ws.data_ptr()), ws.numel(), s))
+        check(lib().moe_ep_combine(plan, c_void_p(x.data_ptr()), t, c_void_p(y_back.data_ptr()),
+                                   c_void_p(out.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(), s))
+        return out
+
+    def status(self) -> None:
+        self.layer.status()
+
+    def close(self) -> None:
+        self.layer.close()

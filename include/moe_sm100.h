@@ -78,7 +78,7 @@ typedef struct MoeConfig {
   float rms_norm_eps;            /* post_attention_layernorm epsilon                  */
   int32_t max_tokens;            /* largest T a forward may be called with            */
   int32_t expert_begin;          /* locally resident routed experts [begin, end);    */
-  int32_t expert_end;            /*   0,0 = all experts                               */
+  int32_t expert_end;            /*   0,0 = all (expert parallel: this rank's share)  */
   int32_t device;                /* CUDA device ordinal                               */
 } MoeConfig;
 
@@ -154,6 +154,36 @@ int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, float* out_dev
 int moe_route(MoePlan* plan, const float* x_dev, int32_t T, int32_t* topk_ids, float* topk_w,
               int32_t* expert_offsets, int32_t* perm, void* workspace,
               uint64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------- expert parallelism
+ * New in this build (the reference runs one process on one device): the routed
+ * experts are split across ranks, one process per GPU, and the caller moves
+ * rows between ranks (e.g. NCCL all-to-all over NVLink).  Create each rank's
+ * plan with expert_begin/expert_end = its equal, contiguous share, and bind the
+ * layer blob on every rank (each packs only its own experts; router and shared
+ * expert are replicated).  Per forward of T local tokens:
+ *   1. moe_ep_dispatch: route the local tokens; send_rows [T*K, H] f16 holds the
+ *      normalised rows grouped by destination rank (rows for rank d are
+ *      send_offsets[d] .. send_offsets[d+1]), send_experts [T*K] the expert id
+ *      local to the destination, send_offsets [world+1].
+ *   2. caller: exchange the per-rank counts, then rows and expert ids.
+ *   3. moe_ep_experts: the resident experts on the R received rows; y_out [R, H]
+ *      f16 answers received row r in place.
+ *   4. caller: send the y rows back (reverse exchange); they arrive in send order.
+ *   5. moe_ep_shared (any time after step 1) and moe_ep_combine:
+ *      out = x + sum_k w * y + shared expert.
+ * Steps 1, 5 share one workspace of moe_workspace_bytes(plan, T) that must be
+ * left untouched in between; step 3 uses moe_ep_workspace_bytes(plan, R). */
+int moe_ep_dispatch(MoePlan* plan, const float* x_dev, int32_t T, void* send_rows,
+                    int32_t* send_experts, int32_t* send_offsets, void* workspace,
+                    uint64_t workspace_bytes, void* stream);
+uint64_t moe_ep_workspace_bytes(const MoePlan* plan, int32_t R);
+int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_experts, int32_t R,
+                   void* y_out, void* workspace, uint64_t workspace_bytes, void* stream);
+int moe_ep_shared(MoePlan* plan, int32_t T, void* workspace, uint64_t workspace_bytes,
+                  void* stream);
+int moe_ep_combine(MoePlan* plan, const float* x_dev, int32_t T, const void* y_back,
+                   float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* Synchronise `stream`, then read and clear the device error word of the plan.
  * Returns MOE_OK, MOE_ERR_TIMEOUT or MOE_ERR_DEVICE. */

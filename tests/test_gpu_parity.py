@@ -197,3 +197,47 @@ def test_full_shape_properties(glm_full, T: int) -> None:  # noqa: ANN001
     for i in (0, T // 2, T - 1):
         single = ml.forward(x[i:i + 1].clone())
         assert torch.allclose(single[0], a[i], rtol=2e-3, atol=2e-3)
+
+
+# ------------------------------------------------------------------ INT8 prefill / Qwen3 shapes
+def _synthetic_parity(spec_kw: dict, cfg_kw: dict, T: int, tol: float, seed: int) -> float:
+    spec = SyntheticSpec(**spec_kw)
+    blob, meta = build_device_layer(spec)
+    ml = MoeLayer(MoeLayerConfig(**cfg_kw, max_tokens=T))
+    ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    x = np.random.default_rng(seed).standard_normal((T, spec.hidden), dtype=np.float32)
+    out = ml.forward(torch.from_numpy(x).cuda())
+    ml.status()
+    glm = spec.family == "glm"
+    ocfg = OracleConfig(hidden=spec.hidden, n_experts=spec.n_experts, top_k=spec.top_k,
+                        inter=spec.inter, shared_inter=spec.shared_inter, use_bias=glm,
+                        routed_scaling_factor=cfg_kw["routed_scaling_factor"],
+                        eps=cfg_kw["rms_norm_eps"],
+                        shared_prefix="mlp.shared_experts." if glm else "mlp.shared_expert.")
+    ref, _aux = moe_block(x, LazyHostTensors(blob, meta), ocfg)
+    err = rel_l2(out.cpu().numpy(), ref)
+    ml.close()
+    assert err <= tol, f"rel-L2 {err:.3e}"
+    return err
+
+
+def test_int8_prefill_glm_dims() -> None:
+    """GLM-4.7 dimensions with 32 experts, INT8 per-channel weights, Zipf-skewed
+    routing, 1024 tokens: the 256-token tiles and the int8 -> f16 converter path."""
+    _synthetic_parity(dict(hidden=5120, n_experts=32, top_k=8, inter=1536, shared_inter=1536,
+                           family="glm", expert_dtype="int8", seed=21, zipf_s=1.1),
+                      dict(hidden=5120, n_experts=32, top_k=8, inter=1536, shared_inter=1536,
+                           weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5),
+                      T=1024, tol=TOL_I8, seed=31)
+
+
+@pytest.mark.parametrize("T", [1, 300])
+def test_qwen3_next_shape(T: int) -> None:
+    """Qwen3-Coder-Next shape (H 2048, 512 experts, top-10, I 512, gated shared expert)."""
+    _synthetic_parity(dict(hidden=2048, n_experts=512, top_k=10, inter=512, shared_inter=512,
+                           family="qwen3", expert_dtype="bfloat16", seed=22),
+                      dict(hidden=2048, n_experts=512, top_k=10, inter=512, shared_inter=512,
+                           use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
+                           rms_norm_eps=1e-6),
+                      T=T, tol=TOL_16, seed=40 + T)
