@@ -333,6 +333,7 @@ __device__ int block_excl_scan(int v, int* total) {
 
 struct TileArgs {
   int E, T, bn, mt1, mt2, mt1s, has_shared, max1, max2;
+  int shared_group;                // group id the GEMM treats as the shared expert (n_local)
   int nk1, nk1s, nk2, nk2s;        // k-blocks: gate/up routed / shared, down routed / shared
   int num_sms, max_split_tiles;
   Tile* tiles1;
@@ -434,7 +435,7 @@ __device__ void build_tile_lists(int cnt, int off, const TileArgs& a, int* s_p1,
       } else {
         const int i = q - tot;
         const int m = i / nts, n = i % nts;
-        t.group = a.E;
+        t.group = a.shared_group;
         t.m0 = m * kBM;
         t.row0 = n * a.bn;
         t.nvalid = min(a.bn, a.T - n * a.bn);
@@ -686,6 +687,7 @@ static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T, int
   ta.mt2 = (p.H + kBM - 1) / kBM;
   ta.mt1s = (shared && p.SI > 0) ? (2 * p.SI + kBM - 1) / kBM : 0;
   ta.has_shared = shared && p.SI > 0;
+  ta.shared_group = p.n_local;
   ta.max1 = L.max_tiles1;
   ta.max2 = L.max_tiles2;
   ta.nk1 = (p.H + kBK - 1) / kBK;
