@@ -407,6 +407,10 @@ def run_ours(args) -> None:  # noqa: ANN001
     if world > 1:
         run_ep(args, world, rank, local)
         return
+    if args.only_other:  # profiling aid: BASELINE configs 2 and 3 only
+        print(json.dumps({"other_configs": run_other_configs(args, local, world, _peaks()[0],
+                                                              _tc_peak())}))
+        return
     hbm, peak_kind = _peaks()
     T_main = args.tokens
     ml, blob, meta = _make_layer(local, seed=1234, max_tokens=max(64, T_main))
@@ -589,6 +593,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-sub", action="store_true", help="only the --tokens batch (no T=1/8 lines)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
+    ap.add_argument("--only-other", action="store_true",
+                    help="only BASELINE configs 2 and 3 (profiling aid)")
     ap.add_argument("--no-other", action="store_true",
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,

@@ -110,15 +110,17 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
     o = align256(o + bytes);
     return at;
   };
-  L.h16 = take(static_cast<size_t>(TS) * p.H * 2);
+  L.h16 = take(static_cast<size_t>(router ? T : TS) * p.H * 2);
   L.xg = take(R * p.H * 2);
   L.act = take(R * p.I * 2);
   L.act_s = take(static_cast<size_t>(TS) * p.SI * 2);
-  L.y = take(router ? R * p.H * 4 : 0);
+  L.y = take(router ? R * p.H * 2 : 0);  // routed expert outputs, f16, dispatch order
   L.y_s = take(p.SI > 0 ? static_cast<size_t>(TS) * p.H * 4 : 0);
   if (router) {
     const RouterGeom g = router_geometry(p, T);
-    L.logits = take(static_cast<size_t>(T) * p.router_rows * 4);
+    // prefill batches may route on the tensor cores: one logit plane per K split
+    const size_t planes = route_uses_tail(p, T) ? 1 : kRouterMaxSplit;
+    L.logits = take(planes * T * p.router_rows * 4);
     L.part = take(g.splits > 1 ? static_cast<size_t>(g.splits) * T * p.router_rows * 4 : 0);
     L.ss_part = take(static_cast<size_t>(g.rx) * g.splits * T * 4);
     L.rms = take(static_cast<size_t>(T) * 4);
@@ -431,6 +433,7 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   const size_t o_norm = take(static_cast<size_t>(H) * 4);
   const size_t o_router = take(static_cast<size_t>(p.router_rows) * H * 4);
   const size_t o_bias = take(static_cast<size_t>(E) * 4);
+  const size_t o_rw16 = take(static_cast<size_t>(p.router_rows) * H * 2);
   const size_t o_flag = take(16);
   if (!p.weights_alloc) {
     MOE_CUDA(cudaMalloc(&p.weights_alloc, o));
@@ -448,8 +451,10 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   p.w.norm_w = reinterpret_cast<float*>(wb + o_norm);
   p.w.router_w = reinterpret_cast<float*>(wb + o_router);
   p.w.bias = (bias.ptr && p.cfg.use_bias) ? reinterpret_cast<float*>(wb + o_bias) : nullptr;
+  p.w.rw16 = reinterpret_cast<__half*>(wb + o_rw16);
   int* range_err = reinterpret_cast<int*>(wb + o_flag);
-  MOE_CUDA(cudaMemsetAsync(range_err, 0, sizeof(int), s));
+  int* rw16_err = range_err + 1;
+  MOE_CUDA(cudaMemsetAsync(range_err, 0, 2 * sizeof(int), s));
 
   // ---- pack
   MOE_CUDA(launch_to_f32(norm.ptr, norm.dtype, p.w.norm_w, H, s));
@@ -457,6 +462,7 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   if (sgate.ptr)
     MOE_CUDA(launch_to_f32(sgate.ptr, sgate.dtype, p.w.router_w + static_cast<size_t>(E) * H, H, s));
   if (p.w.bias) MOE_CUDA(launch_to_f32(bias.ptr, bias.dtype, p.w.bias, E, s));
+  MOE_CUDA(launch_scale_router_weights(p.w.router_w, p.w.rw16, p.router_rows, H, rw16_err, s));
   for (int le = 0; le < NL; ++le) {
     const Src& g = ex[le * 3 + P_GATE];
     const Src& u = ex[le * 3 + P_UP];
@@ -501,10 +507,17 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
       MOE_CUDA(launch_pack_rows(sh[P_DOWN].ptr, sh[P_DOWN].dtype, p.w.ws2, p.int8, p.w.ss2, H, SI,
                                 range_err, s));
   }
-  int h_range = 0;
-  MOE_CUDA(cudaMemcpyAsync(&h_range, range_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  int h_range[2] = {0, 0};
+  MOE_CUDA(cudaMemcpyAsync(h_range, range_err, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
   MOE_CUDA(cudaStreamSynchronize(s));
-  if (h_range) return fail(MOE_ERR_RANGE, "an expert weight does not fit the packed format (|w| > 65504 for f16)");
+  if (h_range[0]) return fail(MOE_ERR_RANGE, "an expert weight does not fit the packed format (|w| > 65504 for f16)");
+  // Prefill batches pick candidate experts on the tensor cores and recompute
+  // the chosen logits in fp32.  Two cases keep the fp32 CUDA-core router of
+  // decode batches instead: router weights beyond |w| ~ 64 (no scaled f16
+  // copy), and softmax weights without renormalisation, whose denominator
+  // would carry the f16 error of every non-selected logit.
+  p.router_tc = h_range[1] == 0 &&
+                !(p.cfg.score_func == MOE_SCORE_SOFTMAX && !p.cfg.norm_topk_prob);
 
   // ---- tensor maps over the resident weights
   std::string err;
@@ -512,6 +525,9 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   const bool sw = !i8;  // f16 tiles are swizzled for the MMA; int8 tiles are staged plain
   if (!make_tmap_2d(&p.tm_w13, p.w.w13, i8, H, static_cast<uint64_t>(NL) * 2 * I, kBK, kBM, sw, &err) ||
       !make_tmap_2d(&p.tm_w2, p.w.w2, i8, I, static_cast<uint64_t>(NL) * H, kBK, kBM, sw, &err))
+    return fail(MOE_ERR_CUDA, err);
+  if (!make_tmap_2d(&p.tm_rw16, p.w.rw16, false, static_cast<uint64_t>(H), p.router_rows,
+                    kBK, kBM, true, &err))
     return fail(MOE_ERR_CUDA, err);
   if (SI > 0) {
     if (!make_tmap_2d(&p.tm_ws13, p.w.ws13, i8, H, 2 * SI, kBK, kBM, sw, &err) ||
@@ -554,6 +570,8 @@ int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T, vo
   if (rc != MOE_OK || T == 0) return rc;
   if (!x_dev || !out_dev) return fail(MOE_ERR_INVALID, "null x / out");
   if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  if (misaligned16(x_dev) || misaligned16(out_dev))
+    return fail(MOE_ERR_INVALID, "x and out must be 16-byte aligned");
   Plan& p = plan->p;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const WsLayout L = ws_layout(p, T);
@@ -561,8 +579,9 @@ int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T, vo
   rc = route_impl(p, L, ws, x_dev, T, true, s);
   if (rc != MOE_OK) return rc;
   MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
-  MOE_CUDA(launch_gemm(p, L, ws, true, T, s));
-  MOE_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
+  MOE_CUDA(launch_gemm(p, L, ws, true,
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
+  MOE_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                           reinterpret_cast<float*>(ws + L.y_s),
                           reinterpret_cast<int32_t*>(ws + L.slot_row),
                           reinterpret_cast<float*>(ws + L.wts),
@@ -576,6 +595,8 @@ int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t
   if (rc != MOE_OK) return rc;
   if (!x_dev || !out_dev || !stage_ms) return fail(MOE_ERR_INVALID, "null x / out / stage_ms");
   if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  if (misaligned16(x_dev) || misaligned16(out_dev))
+    return fail(MOE_ERR_INVALID, "x and out must be 16-byte aligned");
   for (int i = 0; i < 4; ++i) stage_ms[i] = 0.f;
   if (T == 0) return MOE_OK;
   Plan& p = plan->p;
@@ -596,9 +617,10 @@ int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t
   MOE_CUDA(cudaEventRecord(ev[1], s));
   MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_CUDA(cudaEventRecord(ev[2], s));
-  MOE_CUDA(launch_gemm(p, L, ws, true, T, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true,
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
   MOE_CUDA(cudaEventRecord(ev[3], s));
-  MOE_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
+  MOE_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                           reinterpret_cast<float*>(ws + L.y_s),
                           reinterpret_cast<int32_t*>(ws + L.slot_row),
                           reinterpret_cast<float*>(ws + L.wts),
@@ -615,6 +637,7 @@ int moe_route(MoePlan* plan, const float* x_dev, int32_t T, int32_t* topk_ids, f
   int rc = check_call(plan, T, workspace, workspace_bytes);
   if (rc != MOE_OK || T == 0) return rc;
   if (!x_dev) return fail(MOE_ERR_INVALID, "null x");
+  if (misaligned16(x_dev)) return fail(MOE_ERR_INVALID, "x must be 16-byte aligned");
   Plan& p = plan->p;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const WsLayout L = ws_layout(p, T);
@@ -673,6 +696,7 @@ int moe_ep_dispatch(MoePlan* plan, const float* x_dev, int32_t T, void* send_row
     return MOE_OK;
   }
   if (!x_dev || !send_rows || !send_experts) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(x_dev)) return fail(MOE_ERR_INVALID, "x must be 16-byte aligned");
   const WsLayout L = ws_layout(p, T);
   char* ws = static_cast<char*>(workspace);
   MOE_CUDA(launch_route(p, L, ws, x_dev, T, true, s, static_cast<__half*>(send_rows)));

@@ -12,10 +12,8 @@
 
 namespace moe {
 
-// Expert rows as fp32 (single GPU) or f16 (returned over the expert-parallel exchange).
-MOE_DEV float4 load_row4(const float* y, size_t row, int H, int v) {
-  return reinterpret_cast<const float4*>(y + row * H)[v];
-}
+// Expert rows are f16: written so by the down GEMM (single GPU) or returned over
+// the expert-parallel exchange.
 MOE_DEV float4 load_row4(const __half* y, size_t row, int H, int v) {
   const uint2 raw = reinterpret_cast<const uint2*>(y + row * H)[v];
   const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
@@ -62,17 +60,6 @@ __global__ void __launch_bounds__(256) combine_kernel(
   o.z = __fadd_rn(xv.z, acc.z);
   o.w = __fadd_rn(xv.w, acc.w);
   reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H)[v] = o;
-}
-
-cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,
-                           const int32_t* slot_row, const float* wts, const float* sgate,
-                           float* out, int T, cudaStream_t s) {
-  const int nv = p.H >> 2;
-  dim3 grid((nv + 255) / 256, T);
-  combine_kernel<float><<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
-                                             p.cfg.has_shared_gate ? sgate : nullptr, out, p.K,
-                                             p.H);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_combine_half(const Plan& p, const float* x, const __half* y, const float* y_s,

@@ -25,6 +25,7 @@ enum DevErr : int {
   DEV_TIMEOUT_CONV = 5,      // int8 converter waited too long
   DEV_BAD_TILE = 6,          // tile list entry out of range
   DEV_BAD_ROUTE = 7,         // router produced an expert id out of range
+  DEV_RANGE = 8,             // an activation does not fit the f16 router operand
 };
 
 // ~1 s at the B200 boost clock.  Legitimate waits in these kernels are

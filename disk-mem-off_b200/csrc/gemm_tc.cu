@@ -49,6 +49,11 @@ struct GemmArgs {
   int y_ld;
   __half* y_half;        // if set: routed down outputs as f16 at row y_row_map[row] (or row)
   const int32_t* y_row_map;
+  // router mode (tiles == nullptr: implicit m x n x split grid over implicit_rows tokens)
+  int implicit_ntn, implicit_rows, implicit_splits;
+  float* logits;         // [split][tokens][logit_ld] partial logit planes
+  int logit_ld;
+  float logit_scale;
   const float* scale_routed;  // int8 row scales [groups * rows_a]
   const float* scale_shared;  // [m_limit_shared]
   float* kpart;               // split-K partials [tile_id * nsplit + split][128][16] f32
@@ -115,9 +120,12 @@ MOE_DEV void convert_row_i8_f16(const int8_t* src_row, uint8_t* dst_tile, int r)
   }
 }
 
-template <int BN, bool DOWN, bool INT8>
+enum GemmMode { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_ROUTER = 2 };
+
+template <int BN, int MODE, bool INT8>
 __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
+  constexpr bool DOWN = MODE == MODE_DOWN;
   constexpr int STAGES = gemm_stages<BN, INT8>();
   constexpr int SA = TileCfg<BN>::kStageA, SB = TileCfg<BN>::kStageB, SA8 = TileCfg<BN>::kStageA8;
   constexpr uint32_t IDESC = idesc_f16_f32(kBM, BN);
@@ -141,7 +149,26 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntiles = min(*(args.tile_count + args.count_index), args.max_tiles);
+  const int ntiles = args.tiles ? min(*(args.tile_count + args.count_index), args.max_tiles)
+                                : args.max_tiles;
+  // Tile lists come from the routing kernels; the router GEMM's units are a
+  // plain (m, n, K split) grid derived from the index.
+  auto fetch_tile = [&](int ti) {
+    if (args.tiles) return args.tiles[ti];
+    Tile t;
+    const int ntn = args.implicit_ntn, ns = args.implicit_splits;
+    const int sidx = ti % ns, mn = ti / ns;
+    const int nk = (args.k_routed + kBK - 1) / kBK;
+    t.group = 0;
+    t.m0 = (mn / ntn) * kBM;
+    t.row0 = (mn % ntn) * BN;
+    t.nvalid = min(BN, args.implicit_rows - t.row0);
+    t.kb0 = sidx * nk / ns;
+    t.kb1 = (sidx + 1) * nk / ns;
+    t.split = sidx | (ns << 16);
+    t.tile_id = mn;
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -175,7 +202,8 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     const int lim = sh ? args.m_limit_shared : args.m_limit_routed;
     const int nk = ((sh ? args.k_shared : args.k_routed) + kBK - 1) / kBK;
     const int nsplit = t.split >> 16, sidx = t.split & 0xffff;
-    if (nsplit < 1 || sidx >= nsplit || (nsplit > 1 && BN != kSplitTileRows)) return false;
+    if (nsplit < 1 || sidx >= nsplit) return false;
+    if (nsplit > 1 && BN != kSplitTileRows && MODE != MODE_ROUTER) return false;
     return t.m0 >= 0 && t.m0 < lim && t.kb0 >= 0 && t.kb0 < t.kb1 && t.kb1 <= nk;
   };
 
@@ -184,7 +212,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     if (lane == 0) {
       int it = 0;
       for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
-        const Tile t = args.tiles[ti];
+        const Tile t = fetch_tile(ti);
         if (!tile_ok(t)) {
           record_error(args.err, DEV_BAD_TILE);
           continue;
@@ -219,7 +247,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       int it = 0, tl = 0;
       bool issued = false;
       for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
-        const Tile t = args.tiles[ti];
+        const Tile t = fetch_tile(ti);
         if (!tile_ok(t)) continue;
         const int buf = tl & 1;
         if (!mbar_wait_bounded(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag)) {
@@ -264,7 +292,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     const int r = q * 32 + lane;
     int tl = 0;
     for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
-      const Tile t = args.tiles[ti];
+      const Tile t = fetch_tile(ti);
       if (!tile_ok(t)) continue;
       const int buf = tl & 1;
       // every lane polls; the warp vote re-converges the warp before the
@@ -328,32 +356,57 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] *= rs;
-        if constexpr (!DOWN) {
-          // lanes 0-15: gate rows, lanes 16-31: the matching up rows
-          const int feat = (mrow >> 5) * 16 + (lane & 15);
-          const bool feat_ok = row_ok;
-          __half* dst = sh ? args.act_shared : args.act_routed;
-          const int ld = sh ? args.act_ld_shared : args.act_ld_routed;
+        if constexpr (MODE == MODE_ROUTER) {
+          // router logits: D[router row, token] * 2^-10 -> plane[split][token][row]
+          float* plane = args.logits + static_cast<size_t>(t.split & 0xffff) * args.implicit_rows *
+                                           args.logit_ld;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[i], 16);
-            if ((i & 1) == (lane >> 4)) {
-              const int col = c0 + i;
-              if (col < t.nvalid && feat_ok) {
-                const float g = (lane < 16) ? v[i] : o;
-                const float u = (lane < 16) ? o : v[i];
-                dst[static_cast<size_t>(t.row0 + col) * ld + feat] = __float2half_rn(silu_f(g) * u);
-              }
-            }
+            const int col = c0 + i;
+            if (col < t.nvalid && row_ok)
+              plane[static_cast<size_t>(t.row0 + col) * args.logit_ld + mrow] = v[i] * args.logit_scale;
+          }
+        } else if constexpr (!DOWN) {
+          // lanes 0-15: gate rows, lanes 16-31: the matching up rows.  Lane l < 16
+          // forms the activation of feature l for the even columns, lane l + 16
+          // for the odd ones; neighbouring features then pair up across lanes
+          // l, l ^ 1 so that every store is a 4-byte half2 (2-byte scattered
+          // stores cost the epilogue more than twice the time).
+          const int feat = (mrow >> 5) * 16 + (lane & 15);
+          __half* dst = sh ? args.act_shared : args.act_routed;
+          const int ld = sh ? args.act_ld_shared : args.act_ld_routed;
+          float a[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float o = __shfl_xor_sync(0xffffffffu, (lane < 16) ? v[2 * j + 1] : v[2 * j], 16);
+            const float g = (lane < 16) ? v[2 * j] : o;
+            const float u = (lane < 16) ? o : v[2 * j + 1];
+            a[j] = silu_f(g) * u;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const float o = __shfl_xor_sync(0xffffffffu, (lane & 1) ? a[j] : a[j + 1], 1);
+            const float lo = (lane & 1) ? o : a[j];
+            const float hi = (lane & 1) ? a[j + 1] : o;
+            const int col = c0 + 2 * (j + (lane & 1)) + (lane >> 4);
+            if (col < t.nvalid && row_ok)
+              *reinterpret_cast<__half2*>(dst + static_cast<size_t>(t.row0 + col) * ld + (feat & ~1)) =
+                  __floats2half2_rn(lo, hi);
           }
         } else {
           if (!sh && args.y_half) {
+            // features mrow & ~1 and | 1 pair up across lanes l, l ^ 1: even lanes
+            // store column i, odd lanes column i + 1, each as one half2
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int col = c0 + i;
+            for (int i = 0; i < 16; i += 2) {
+              const float o = __shfl_xor_sync(0xffffffffu, (lane & 1) ? v[i] : v[i + 1], 1);
+              const float lo = (lane & 1) ? o : v[i];
+              const float hi = (lane & 1) ? v[i + 1] : o;
+              const int col = c0 + i + (lane & 1);
               if (col < t.nvalid && row_ok) {
                 const int orow = args.y_row_map ? args.y_row_map[t.row0 + col] : t.row0 + col;
-                args.y_half[static_cast<size_t>(orow) * args.y_ld + mrow] = __float2half_rn(v[i]);
+                *reinterpret_cast<__half2*>(args.y_half + static_cast<size_t>(orow) * args.y_ld + (mrow & ~1)) =
+                    __floats2half2_rn(lo, hi);
               }
             }
           } else {
@@ -375,7 +428,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     const int r = (warp - 6) * 32 + lane;  // one A row per thread
     int it = 0;
     for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
-      const Tile t = args.tiles[ti];
+      const Tile t = fetch_tile(ti);
       if (!tile_ok(t)) continue;
       bool ok = true;
       for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
@@ -404,31 +457,32 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
 }
 
 // ------------------------------------------------------------------ launcher
-template <int BN, bool DOWN, bool INT8>
+template <int BN, int MODE, bool INT8>
 static cudaError_t run_gemm(const GemmArgs& a, int grid, cudaStream_t s) {
   constexpr size_t smem = gemm_smem_bytes<BN, INT8>();
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t st = cudaFuncSetAttribute(moe_gemm_kernel<BN, DOWN, INT8>,
+    cudaError_t st = cudaFuncSetAttribute(moe_gemm_kernel<BN, MODE, INT8>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(smem));
     if (st != cudaSuccess) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  moe_gemm_kernel<BN, DOWN, INT8><<<grid, INT8 ? 320 : 192, smem, s>>>(a);
+  moe_gemm_kernel<BN, MODE, INT8><<<grid, INT8 ? 320 : 192, smem, s>>>(a);
   return cudaGetLastError();
 }
 
 template <bool DOWN, bool INT8>
 static cudaError_t dispatch_bn(const GemmArgs& a, int bn, int grid, cudaStream_t s) {
+  constexpr int M = DOWN ? MODE_DOWN : MODE_GATEUP;
   switch (bn) {
-    case 16: return run_gemm<16, DOWN, INT8>(a, grid, s);
-    case 32: return run_gemm<32, DOWN, INT8>(a, grid, s);
-    case 64: return run_gemm<64, DOWN, INT8>(a, grid, s);
-    case 128: return run_gemm<128, DOWN, INT8>(a, grid, s);
-    case 256: return run_gemm<256, DOWN, INT8>(a, grid, s);
+    case 16: return run_gemm<16, M, INT8>(a, grid, s);
+    case 32: return run_gemm<32, M, INT8>(a, grid, s);
+    case 64: return run_gemm<64, M, INT8>(a, grid, s);
+    case 128: return run_gemm<128, M, INT8>(a, grid, s);
+    case 256: return run_gemm<256, M, INT8>(a, grid, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -506,6 +560,63 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, c
   if (grid <= 0) return cudaSuccess;
   if (p.int8) return down ? dispatch_bn<true, true>(a, bn, grid, s) : dispatch_bn<false, true>(a, bn, grid, s);
   return down ? dispatch_bn<true, false>(a, bn, grid, s) : dispatch_bn<false, false>(a, bn, grid, s);
+}
+
+// Router logits on the tensor cores for prefill batches: D = A . B^T with
+// A = f16(W * 2^10) (router rows, bind time) and B = h16 (the normalised f16
+// token rows that dispatch gathers), K = H split into `splits` ranges whose
+// fp32 partial logits land in separate planes; the selection kernel adds the
+// planes in split order.  These logits carry f16 operand error (~2e-3 absolute
+// at most for GLM-4.7 shapes): they only pick candidates, and the selection
+// kernel recomputes the chosen logits in fp32.
+int router_tc_splits(const Plan& p, int T) {
+  const int units = ((p.router_rows + kBM - 1) / kBM) * ((T + 255) / 256);
+  const int nk = (p.H + kBK - 1) / kBK;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= kRouterMaxSplit && nk / s >= 8; ++s) {
+    const int u = units * s;
+    const int rounds = (u + p.num_sms - 1) / p.num_sms;
+    const double eff = static_cast<double>(u) / (static_cast<double>(rounds) * p.num_sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s) {
+  constexpr int BN = 256;
+  GemmArgs a{};
+  std::string err;
+  a.a_routed = p.tm_rw16;
+  a.a_shared = p.tm_rw16;
+  if (!make_tmap_2d(&a.b_routed, ws + L.h16, false, p.H, T, kBK, BN, true, &err)) {
+    set_error(err);
+    return cudaErrorInvalidValue;
+  }
+  a.b_shared = a.b_routed;
+  a.tiles = nullptr;
+  a.tile_count = nullptr;
+  a.count_index = 0;
+  const int mt = (p.router_rows + kBM - 1) / kBM;
+  a.implicit_ntn = (T + BN - 1) / BN;
+  a.implicit_rows = T;
+  a.implicit_splits = router_tc_splits(p, T);
+  a.max_tiles = mt * a.implicit_ntn * a.implicit_splits;
+  a.n_local = 1;  // no shared group in this launch
+  a.rows_a_routed = 0;
+  a.m_limit_routed = p.router_rows;
+  a.m_limit_shared = p.router_rows;
+  a.k_routed = p.H;
+  a.k_shared = p.H;
+  a.logits = reinterpret_cast<float*>(ws + L.logits);
+  a.logit_ld = p.router_rows;
+  a.logit_scale = 1.0f / kRouterWeightScale;
+  a.err = p.d_err;
+  const int grid = a.max_tiles < p.num_sms ? a.max_tiles : p.num_sms;
+  return run_gemm<BN, MODE_ROUTER, false>(a, grid, s);
 }
 
 }  // namespace moe

@@ -16,6 +16,11 @@ constexpr int kBM = 128;          // GEMM tile rows (weight rows, swap-AB)
 constexpr int kBK = 64;           // GEMM k-block (one 128-byte swizzle atom of f16)
 constexpr int kPermChunk = 1024;  // tokens per permutation chunk (bitmask width)
 constexpr int kMaxTopK = 32;
+// Router weights are scaled by 2^10 before their f16 copy for the prefill
+// tensor-core router, so that ~1e-2 weights keep full f16 precision.
+constexpr float kRouterWeightScale = 1024.0f;
+// The prefill router GEMM splits K into at most this many partial logit planes.
+constexpr int kRouterMaxSplit = 4;
 
 // One unit of work for the grouped GEMM: weight rows [m0, m0+128) of group
 // `group` (local routed expert index, or n_local for the shared expert)
@@ -50,6 +55,7 @@ struct DeviceWeights {
   float* norm_w = nullptr;    // [H]
   float* router_w = nullptr;  // [E (+1 shared gate row)][H]
   float* bias = nullptr;      // [E] or null
+  __half* rw16 = nullptr;     // [E (+1)][H] f16(W * 2^10) (prefill tensor-core router)
 };
 
 struct Plan {
@@ -66,6 +72,8 @@ struct Plan {
   size_t weights_bytes = 0;
   int* d_err = nullptr;        // device error word
   CUtensorMap tm_w13{}, tm_w2{}, tm_ws13{}, tm_ws2{};
+  CUtensorMap tm_rw16{};
+  bool router_tc = false;      // tensor-core router available for prefill batches
 };
 
 // Workspace carve-up for one forward of T tokens (offsets in bytes).
@@ -101,6 +109,13 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
                               const __half* rows, int n, cudaStream_t s);
 cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
+cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
+bool route_uses_tc_router(const Plan& p, int T);
+int router_tc_splits(const Plan& p, int T);
+// Token rows are read as float4 vectors and by bulk copies.
+inline bool misaligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
+cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, int H, int* err,
+                                        cudaStream_t s);
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
                         cudaStream_t s);
 // Rows of the routed / shared B operands and an optional f16 routed output
@@ -113,9 +128,6 @@ struct GemmIO {
 };
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
                         cudaStream_t s);
-cudaError_t launch_combine(const Plan& p, const float* x, const float* y, const float* y_s,
-                           const int32_t* slot_row, const float* wts, const float* sgate,
-                           float* out, int T, cudaStream_t s);
 
 cudaError_t launch_combine_half(const Plan& p, const float* x, const __half* y, const float* y_s,
                                 const int32_t* slot_row, const float* wts, const float* sgate,

@@ -75,6 +75,8 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   if (T < 0 || T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T outside [0, max_tokens]");
   if (T == 0) return MOE_OK;
   if (!x_dev || !out_dev) return fail(MOE_ERR_INVALID, "null x / out");
+  if (moe::misaligned16(x_dev) || moe::misaligned16(out_dev))
+    return fail(MOE_ERR_INVALID, "x and out must be 16-byte aligned");
   if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
   if (p.device < 0 || p.device >= kMaxDevices)
     return fail(MOE_ERR_UNSUPPORTED, "device ordinal beyond the static scratch table");
@@ -96,8 +98,9 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   char* ws = static_cast<char*>(scratch);
   MOE_NA_CUDA(launch_route(p, L, ws, x_dev, T, true, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, false, T, s));
-  MOE_NA_CUDA(launch_gemm(p, L, ws, true, T, s));
-  MOE_NA_CUDA(launch_combine(p, x_dev, reinterpret_cast<float*>(ws + L.y),
+  MOE_NA_CUDA(launch_gemm(p, L, ws, true,
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
+  MOE_NA_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                              reinterpret_cast<float*>(ws + L.y_s),
                              reinterpret_cast<int32_t*>(ws + L.slot_row),
                              reinterpret_cast<float*>(ws + L.wts),

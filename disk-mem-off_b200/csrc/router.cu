@@ -286,6 +286,332 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
   }
 }
 
+// Prefill tensor-core router, selection stage.  The tensor-core logits use f16
+// operands (~2e-3 absolute error at most for GLM-4.7 shapes, 2.5e-4 typical),
+// so they only choose candidates: each warp sums its token's partial logit
+// planes and takes the C = K + 4 best keys.  The CTA then recomputes in fp32
+// on the CUDA cores (sum_k (w_k x_k) Wg_k / rms, in a fixed order), at one of
+// three levels per token:
+//   0: the K chosen experts, when the K-th and (K+1)-th keys are at least
+//      kRefineGap * max(1, |best key|) apart (the set is certain; the order
+//      and weights come from the fp32 logits);
+//   1: all C candidates, when that boundary gap is smaller;
+//   2: every expert, when even the K-th and C-th keys are that close (rare:
+//      eight ranks past the boundary).
+// kRefineGap is ~8x the largest f16 logit error seen, so the final selection,
+// tie rule and weights are those of the fp32 router.  The shared-expert gate
+// logit is always recomputed.
+//
+// The recomputation streams rows from L2 as jobs (token, group of up to
+// kSelRows rows, chunk of kSelChunk floats of H).  Thread t owns float4 slot t
+// of every row of a job: it stages its slots with cp.async into a
+// double-buffered shared-memory ring (job i+1 in flight while job i is used)
+// and reads back only its own slots, so jobs need no CTA barrier; the CTA
+// synchronises once per row group to add the 256 partial sums in a fixed order.
+constexpr int kRefineMargin = 8;
+constexpr float kRefineGap = 1.6e-2f;
+constexpr int kSelRows = 20;     // Wg rows per job (besides the x chunk)
+constexpr int kSelChunk = 1024;  // floats of H per job: one float4 per thread
+constexpr int kSelStages = 2;
+constexpr size_t kSelStageFloats = static_cast<size_t>(kSelRows + 1) * kSelChunk;
+constexpr size_t kSelSmemBytes = kSelStages * kSelStageFloats * sizeof(float);  // 168 KiB
+
+template <int VPL>
+__global__ void __launch_bounds__(256, 1) route_select_kernel(
+    float* __restrict__ logits, int nplanes, const float* __restrict__ x,
+    const float* __restrict__ wn, const float* __restrict__ wr, const float* __restrict__ rms,
+    const float* __restrict__ bias, int32_t* __restrict__ ids, float* __restrict__ wts,
+    float* __restrict__ sgate, int T, int E, int R, int H, int K, int score_func, int norm,
+    float scale, int* err) {
+  constexpr int CMAX = kMaxTopK + kRefineMargin;  // <= 64: two candidate slots per lane
+  extern __shared__ __align__(128) float sel_stage[];
+  __shared__ int s_cand[8][CMAX];
+  __shared__ float s_logit[8][CMAX];
+  __shared__ float s_part[8][kSelRows];
+  __shared__ float s_gate[8];
+  __shared__ int s_level[8];
+  __shared__ int s_jobbase[9];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = min(E, K + kRefineMargin);
+  const int nq = (H + kSelChunk - 1) / kSelChunk;
+  const bool gate = sgate != nullptr;
+  const size_t plane = static_cast<size_t>(T) * R;
+
+  // rows of job (token j, group g): level 2 walks all R rows, else the
+  // candidates then the gate row E
+  auto row_count = [&](int lev) { return lev == 2 ? R : (lev == 0 ? K : C) + (gate ? 1 : 0); };
+  auto row_id = [&](int j, int lev, int idx) {
+    if (lev == 2) return idx;
+    return idx < (lev == 0 ? K : C) ? s_cand[j][idx] : E;
+  };
+  for (int grp = blockIdx.x; grp * 8 < T; grp += gridDim.x) {
+    const int t = grp * 8 + warp;
+    const bool live = t < T;
+    const float* lrow = logits + static_cast<size_t>(live ? t : 0) * R;
+    float lg[VPL];  // tensor-core logits of this lane's experts
+    int cidx[VPL];  // candidate index of expert j*32+lane, or -1
+    // 1. candidates on the tensor-core keys (same keys and tie rule as warp_topk)
+    if (live) {
+      float key[VPL];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int e = j * 32 + lane;
+        key[j] = -FLT_MAX;
+        lg[j] = 0.f;
+        cidx[j] = -1;
+        if (e < E) {
+          float l = lrow[e];
+          for (int sp = 1; sp < nplanes; ++sp) l += lrow[sp * plane + e];
+          lg[j] = l;
+          key[j] = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bias[e] : l)
+                                                     : (bias ? sigmoid_f(l) + bias[e] : sigmoid_f(l));
+        }
+      }
+      float thr = 0.f, k_last = 0.f;
+      int level = 0;
+      for (int r = 0; r < C; ++r) {
+        float bk = -FLT_MAX;
+        int bid = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+          const int e = j * 32 + lane;
+          if (e < E && cidx[j] < 0 && (bid == 0x7fffffff || key[j] > bk || (key[j] == bk && e < bid))) {
+            bk = key[j];
+            bid = e;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+          if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
+            bk = ok;
+            bid = oid;
+          }
+        }
+        if (bid >= E) {  // a NaN key leaves no winner
+          record_error(err, DEV_BAD_ROUTE);
+          bid = 0;
+        }
+        if (r == 0) thr = kRefineGap * fmaxf(1.f, fabsf(bk));
+        if (r == K - 1) k_last = bk;
+        if (r == K && k_last - bk < thr) level = max(level, 1);
+        if (r == C - 1 && C < E && k_last - bk < thr) level = 2;
+        float mine = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+          if (j == (bid >> 5)) {
+            mine = lg[j];
+            if (lane == (bid & 31)) cidx[j] = r;
+          }
+        }
+        const float l = __shfl_sync(0xffffffffu, mine, bid & 31);
+        if (lane == 0) {
+          s_cand[warp][r] = bid;
+          s_logit[warp][r] = l;
+        }
+      }
+      if (lane == 0) s_level[warp] = level;
+    } else if (lane == 0) {
+      s_level[warp] = -1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int b = 0;
+      for (int j = 0; j < 8; ++j) {
+        s_jobbase[j] = b;
+        if (s_level[j] >= 0) b += ((row_count(s_level[j]) + kSelRows - 1) / kSelRows) * nq;
+      }
+      s_jobbase[8] = b;
+    }
+    __syncthreads();
+    const int njobs = s_jobbase[8];
+    // job i -> (token j, row group g, chunk q)
+    auto decode = [&](int i, int& j, int& g, int& q) {
+      j = 0;
+      while (j < 7 && s_jobbase[j + 1] <= i) ++j;
+      const int rel = i - s_jobbase[j];
+      g = rel / nq;
+      q = rel % nq;
+    };
+    const int k4 = threadIdx.x * 4;
+    // this thread's slots of job i -> ring stage i % kSelStages (one commit group per job)
+    auto issue = [&](int i) {
+      int j, g, q;
+      decode(i, j, g, q);
+      const int lev = s_level[j];
+      const int rows = min(kSelRows, row_count(lev) - g * kSelRows);
+      const int len = min(kSelChunk, H - q * kSelChunk);
+      if (k4 < len) {
+        float* dst = sel_stage + (i % kSelStages) * kSelStageFloats + k4;
+        const size_t col = static_cast<size_t>(q) * kSelChunk + k4;
+        cp_async16(dst, x + static_cast<size_t>(grp * 8 + j) * H + col);
+        for (int r = 0; r < rows; ++r)
+          cp_async16(dst + (r + 1) * kSelChunk,
+                     wr + static_cast<size_t>(row_id(j, lev, g * kSelRows + r)) * H + col);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // 2. fp32 logits, job by job
+    if (njobs > 0) issue(0);
+    float acc[kSelRows];
+    for (int i = 0; i < njobs; ++i) {
+      if (i + 1 < njobs) issue(i + 1);
+      else asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // job i's slots have landed
+      int j, g, q;
+      decode(i, j, g, q);
+      const int lev = s_level[j];
+      const int rows = min(kSelRows, row_count(lev) - g * kSelRows);
+      const int len = min(kSelChunk, H - q * kSelChunk);
+      if (q == 0) {
+#pragma unroll
+        for (int r = 0; r < kSelRows; ++r) acc[r] = 0.f;
+      }
+      const float* sx = sel_stage + (i % kSelStages) * kSelStageFloats;
+      if (k4 < len) {
+        const float4 xv = *reinterpret_cast<const float4*>(sx + k4);
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(wn + q * kSelChunk + k4));
+        const float4 u = make_float4(gv.x * xv.x, gv.y * xv.y, gv.z * xv.z, gv.w * xv.w);
+#pragma unroll
+        for (int r = 0; r < kSelRows; ++r) {
+          if (r < rows) {
+            const float4 wv = *reinterpret_cast<const float4*>(sx + (r + 1) * kSelChunk + k4);
+            float a2 = acc[r];
+            a2 = fmaf(u.x, wv.x, a2);
+            a2 = fmaf(u.y, wv.y, a2);
+            a2 = fmaf(u.z, wv.z, a2);
+            a2 = fmaf(u.w, wv.w, a2);
+            acc[r] = a2;
+          }
+        }
+      }
+      if (q == nq - 1) {  // last chunk of this row group: reduce over the CTA in a fixed order
+#pragma unroll
+        for (int r = 0; r < kSelRows; ++r) {
+          if (r < rows) {
+            float v = acc[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) s_part[warp][r] = v;
+          }
+        }
+        __syncthreads();
+        if (warp == j && lane < rows) {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) v += s_part[w][lane];
+          const int tj = grp * 8 + j;
+          v = v / rms[tj];
+          const int idx = g * kSelRows + lane;
+          if (lev == 2) {
+            logits[static_cast<size_t>(tj) * R + idx] = v;  // plane 0 row becomes exact
+            if (gate && idx == E) s_gate[j] = v;
+          } else if (idx < (lev == 0 ? K : C)) {
+            s_logit[j][idx] = v;
+          } else {
+            s_gate[j] = v;
+          }
+        }
+        __syncthreads();  // s_part is reusable
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (!live) continue;
+    if (gate && lane == 0) sgate[t] = sigmoid_f(s_gate[warp]);
+    if (s_level[warp] == 2) {  // every logit of plane 0's row is exact now
+      warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, ids + static_cast<size_t>(t) * K,
+                     wts + static_cast<size_t>(t) * K, err);
+      continue;
+    }
+    // 3. softmax over all experts, candidates with their recomputed logits
+    float denom = 1.f, m = -FLT_MAX;
+    if (score_func == MOE_SCORE_SOFTMAX) {
+      float lv[VPL];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int e = j * 32 + lane;
+        lv[j] = -FLT_MAX;
+        if (e < E) {
+          const float l = cidx[j] >= 0 ? s_logit[warp][cidx[j]] : lg[j];
+          lv[j] = bias ? l + bias[e] : l;
+          m = fmaxf(m, lv[j]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float ssum = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        if (j * 32 + lane < E) ssum += expf(lv[j] - m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+      denom = ssum;
+    }
+    // 4. final top-k among the candidates: lane holds candidates lane and lane + 32
+    float ck[2], cv[2];
+    int ce[2], rank[2];
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+      const int c = lane + 32 * qq;
+      ce[qq] = 0x7fffffff;
+      ck[qq] = -FLT_MAX;
+      cv[qq] = 0.f;
+      rank[qq] = -1;
+      if (c < C) {
+        const int e = s_cand[warp][c];
+        const float l = s_logit[warp][c];
+        ce[qq] = e;
+        if (score_func == MOE_SCORE_SOFTMAX) {
+          ck[qq] = bias ? l + bias[e] : l;
+          cv[qq] = expf(ck[qq] - m) / denom;
+        } else {
+          cv[qq] = sigmoid_f(l);
+          ck[qq] = bias ? cv[qq] + bias[e] : cv[qq];
+        }
+      }
+    }
+    float sum = 0.f;
+    for (int r = 0; r < K; ++r) {
+      float bk = -FLT_MAX, bv = 0.f;
+      int bid = 0x7fffffff;
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq) {
+        if (ce[qq] != 0x7fffffff && rank[qq] < 0 &&
+            (bid == 0x7fffffff || ck[qq] > bk || (ck[qq] == bk && ce[qq] < bid))) {
+          bk = ck[qq];
+          bid = ce[qq];
+          bv = cv[qq];
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+        const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
+          bk = ok;
+          bid = oid;
+          bv = ov;
+        }
+      }
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq)
+        if (ce[qq] == bid) rank[qq] = r;
+      if (norm) sum += bv;  // rank order, like warp_topk
+    }
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+      if (rank[qq] >= 0) {
+        float wv = cv[qq];
+        if (norm) wv = wv / (sum + 1e-20f);
+        ids[static_cast<size_t>(t) * K + rank[qq]] = ce[qq];
+        wts[static_cast<size_t>(t) * K + rank[qq]] = wv * scale;
+      }
+    }
+  }
+}
+
 template <int VPL>
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits,
                                                    const float* __restrict__ bias,
@@ -585,6 +911,91 @@ __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __rest
   }
 }
 
+// dst[r] = src[perm[r] / div] for f16 rows of H elements (one CTA per row).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ src,
+                                                          const int32_t* __restrict__ perm, int n,
+                                                          int H, int div, __half* __restrict__ dst) {
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r] / div) * H);
+    uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * H);
+    for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
+  }
+}
+
+// ------------------------------------------------------------------ prefill router operands
+// Prefill routing prologue, one CTA per token: rms = sqrt(mean(x^2) + eps) and
+// h16 = f16(w * (x / rms)), the B operand of the router GEMM and the rows that
+// dispatch gathers for the experts.
+__global__ void __launch_bounds__(256) router_prep_kernel(const float* __restrict__ x,
+                                                          const float* __restrict__ wn, int H,
+                                                          float eps, float* __restrict__ rms_out,
+                                                          __half* __restrict__ h16, int* err) {
+  const int t = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+  const float4* wr = reinterpret_cast<const float4*>(wn);
+  const int nv = H >> 2;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    const float4 v = xr[i];
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  __shared__ float red[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += red[w];
+  const float rms = sqrtf(tot / static_cast<float>(H) + eps);
+  if (threadIdx.x == 0) rms_out[t] = rms;
+  const float inv = 1.0f / rms;
+  __half* hrow = h16 + static_cast<size_t>(t) * H;
+  bool bad = false;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    const float4 v = xr[i], g = wr[i];
+    __half2 hh[2];
+    hh[0] = __floats2half2_rn(g.x * (v.x * inv), g.y * (v.y * inv));
+    hh[1] = __floats2half2_rn(g.z * (v.z * inv), g.w * (v.w * inv));
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float2 f = __half22float2(hh[j]);
+      bad |= !isfinite(f.x) || !isfinite(f.y);
+    }
+    reinterpret_cast<uint2*>(hrow)[i] = *reinterpret_cast<uint2*>(hh);
+  }
+  if (bad) record_error(err, DEV_RANGE);
+}
+
+// Bind time: rw16[r] = f16(router row * 2^10); err is set when a weight overflows.
+__global__ void __launch_bounds__(256) scale_router_kernel(const float* __restrict__ w,
+                                                           __half* __restrict__ rw16, int H,
+                                                           int* err) {
+  const int r = blockIdx.x;
+  const float* row = w + static_cast<size_t>(r) * H;
+  __half* out = rw16 + static_cast<size_t>(r) * H;
+  bool bad = false;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const __half v = __float2half_rn(row[k] * kRouterWeightScale);
+    bad |= !isfinite(__half2float(v));
+    out[k] = v;
+  }
+  if (bad) atomicExch(err, 1);
+}
+
+cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, int H, int* err,
+                                        cudaStream_t s) {
+  scale_router_kernel<<<rows, 256, 0, s>>>(w, rw16, H, err);
+  return cudaGetLastError();
+}
+
+// Prefill batches (the decode tail is not used) route with the tensor-core
+// router when the bound router weights fit the scaled f16 split.
+bool route_uses_tc_router(const Plan& p, int T) { return p.router_tc && !route_uses_tail(p, T); }
+
 // ------------------------------------------------------------------ dispatch
 // Rows [0, T*K): xg[r] = f16(w * (x[token(r)] / rms)); rows [T*K, T*K+T): h16[t]
 // for the shared expert.  One CTA per row (decode batches have few rows, so
@@ -709,11 +1120,21 @@ bool route_uses_tail(const Plan& p, int T) { return T <= kTailMaxT && T * p.K <=
 
 cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                          bool dispatch, cudaStream_t s, __half* xg_out) {
-  cudaError_t st = (router_bt(T) == 16) ? run_router<16>(p, L, ws, x, T, s)
-                                        : run_router<64>(p, L, ws, x, T, s);
+  const bool tc = route_uses_tc_router(p, T);
+  cudaError_t st;
+  if (tc) {
+    router_prep_kernel<<<T, 256, 0, s>>>(x, p.w.norm_w, p.H, p.cfg.rms_norm_eps,
+                                         reinterpret_cast<float*>(ws + L.rms),
+                                         reinterpret_cast<__half*>(ws + L.h16), p.d_err);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    st = launch_router_gemm(p, L, ws, T, s);
+  } else {
+    st = (router_bt(T) == 16) ? run_router<16>(p, L, ws, x, T, s) : run_router<64>(p, L, ws, x, T, s);
+  }
   if (st != cudaSuccess) return st;
   const int E = p.E, K = p.K, R = p.router_rows;
-  const float* logits = reinterpret_cast<const float*>(ws + L.logits);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);
   const float* bias = p.cfg.use_bias ? p.w.bias : nullptr;
   float* sg = p.cfg.has_shared_gate ? reinterpret_cast<float*>(ws + L.sgate) : nullptr;
   int32_t* ids = reinterpret_cast<int32_t*>(ws + L.ids);
@@ -747,9 +1168,21 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   } else {
     const int grid = (T + 7) / 8;
 #define MOE_TOPK_CASE(V)                                                                        \
-  topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, R, K,                   \
-                                      p.cfg.score_func, p.cfg.norm_topk_prob,                   \
-                                      p.cfg.routed_scaling_factor, p.d_err)
+  do {                                                                                          \
+    if (tc) {                                                                                   \
+      static bool done[64] = {};                                                                \
+      st = set_smem_attr(reinterpret_cast<const void*>(route_select_kernel<V>),                 \
+                         static_cast<int>(kSelSmemBytes), done);                                \
+      if (st != cudaSuccess) return st;                                                         \
+      route_select_kernel<V><<<min(grid, p.num_sms), 256, kSelSmemBytes, s>>>(                  \
+          logits, router_tc_splits(p, T), x, p.w.norm_w, p.w.router_w,                          \
+          reinterpret_cast<const float*>(ws + L.rms), bias, ids, wts, sg, T, E, R, p.H, K,      \
+          p.cfg.score_func, p.cfg.norm_topk_prob, p.cfg.routed_scaling_factor, p.d_err);        \
+    } else                                                                                      \
+      topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, R, K,               \
+                                          p.cfg.score_func, p.cfg.norm_topk_prob,               \
+                                          p.cfg.routed_scaling_factor, p.d_err);                \
+  } while (0)
     if (vpl <= 1) MOE_TOPK_CASE(1);
     else if (vpl <= 2) MOE_TOPK_CASE(2);
     else if (vpl <= 4) MOE_TOPK_CASE(4);
@@ -779,6 +1212,12 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   }
   st = cudaGetLastError();
   if (st != cudaSuccess || !dispatch) return st;
+  if (tc) {  // h16 already holds the normalised rows: gather them per slot
+    gather_rows_kernel<<<min(T * K, p.num_sms * 16), 256, 0, s>>>(
+        reinterpret_cast<const __half*>(ws + L.h16), perm, T * K, p.H, K,
+        xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg));
+    return cudaGetLastError();
+  }
   const int rows = T * K + (p.SI > 0 ? T : 0);
   dispatch_kernel<<<min(rows, p.num_sms * 8), 256, 0, s>>>(
       x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms), perm, T, K, p.H, p.SI > 0,
@@ -787,17 +1226,6 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 }
 
 // ------------------------------------------------------------------ expert-parallel helpers
-// dst[s] = src[perm[s]] for f16 rows of H elements (one CTA per row).
-__global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ src,
-                                                          const int32_t* __restrict__ perm, int n,
-                                                          int H, __half* __restrict__ dst) {
-  for (int r = blockIdx.x; r < n; r += gridDim.x) {
-    const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r]) * H);
-    uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * H);
-    for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
-  }
-}
-
 cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
                               const __half* rows, int n, cudaStream_t s) {
   const int E = p.n_local;
@@ -825,7 +1253,7 @@ cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const 
                                                                          perm, slot_row);
   st = cudaGetLastError();
   if (st != cudaSuccess) return st;
-  gather_rows_kernel<<<min(n, p.num_sms * 8), 256, 0, s>>>(rows, perm, n, p.H,
+  gather_rows_kernel<<<min(n, p.num_sms * 8), 256, 0, s>>>(rows, perm, n, p.H, 1,
                                                           reinterpret_cast<__half*>(ws + L.xg));
   return cudaGetLastError();
 }

@@ -8,7 +8,8 @@
 * full GLM-4.7 shape (H 5120, E 160, top-8, I 1536): routing exact against the
   oracle at T = 1, 8, 64 and 4096 (a flip is tolerated only at an oracle score gap
   below 1e-6 relative, and is counted), output parity at T = 1 and 4 on the
-  experts the tokens touch, size-independent properties at T = 64 / 4096.
+  experts the tokens touch, size-independent properties at T = 64 / 4096;
+* prefill routing (tensor-core candidates, fp32 decision) on exact ties.
 """
 from __future__ import annotations
 
@@ -111,6 +112,8 @@ def test_empty_batch_and_limits() -> None:
     assert ml.forward(empty).shape == (0, spec.hidden)
     with pytest.raises(ValueError):
         ml.forward(torch.zeros((5, spec.hidden), device="cuda"))  # > max_tokens
+    with pytest.raises(ValueError):  # token rows must start on a 16-byte boundary
+        ml.forward(torch.zeros(spec.hidden + 1, device="cuda")[1:].view(1, spec.hidden))
     with pytest.raises(KeyError):
         bad = [m for m in meta if m["name"] != "mlp.experts.3.up_proj.weight"]
         MoeLayer(_layer_cfg(spec, "f16", 4)).bind_host(blob, bad)
@@ -170,6 +173,50 @@ def test_full_shape_routing(glm_full, T: int) -> None:  # noqa: ANN001
     x = np.random.default_rng(100 + T).standard_normal((T, 5120), dtype=np.float32)
     flips = _check_routing(ml, lazy, ocfg, x)
     assert flips <= max(1, T // 1000)
+
+
+@pytest.mark.parametrize("score_func", ["softmax", "sigmoid"])
+def test_prefill_router_exact_ties(score_func: str) -> None:
+    """Prefill batches route on the tensor cores and re-decide in fp32.  Twelve
+    identical router rows with equal bias make exact ties at the top-k boundary
+    and whole runs of tied candidates past it, which is where the selection
+    kernel widens its recomputation; ids must follow the oracle's lower-id rule."""
+    H, E, K, T = 512, 64, 8, 1024
+    rng = np.random.default_rng(31)
+    t = {"post_attention_layernorm.weight": (1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
+         "mlp.gate.weight": (rng.standard_normal((E, H)) * 0.02).astype(np.float32),
+         "mlp.gate.e_score_correction_bias": (rng.standard_normal(E) * 0.01).astype(np.float32)}
+    t["mlp.gate.weight"][1:12] = t["mlp.gate.weight"][0]
+    t["mlp.gate.e_score_correction_bias"][:12] = 0.0
+    for e in range(E):
+        t[f"mlp.experts.{e}.gate_proj.weight"] = (rng.standard_normal((64, H)) * 0.02).astype(np.float32)
+        t[f"mlp.experts.{e}.up_proj.weight"] = (rng.standard_normal((64, H)) * 0.02).astype(np.float32)
+        t[f"mlp.experts.{e}.down_proj.weight"] = (rng.standard_normal((H, 64)) * 0.02).astype(np.float32)
+    blob, meta = pack_layer(t, expert_format="bfloat16")
+    ml = MoeLayer(MoeLayerConfig(hidden=H, n_experts=E, top_k=K, inter=64, shared_inter=0,
+                                 score_func=score_func, routed_scaling_factor=2.5,
+                                 rms_norm_eps=1e-5, max_tokens=T))
+    ml.bind_host(blob, meta)
+    # a component along the tied router row lifts the tie group to the boundary often
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    d = t["mlp.gate.weight"][0] / np.linalg.norm(t["mlp.gate.weight"][0])
+    x += (rng.uniform(0, 5, (T, 1)) * d).astype(np.float32)
+    r = ml.route(torch.from_numpy(x).cuda())
+    ml.status()
+    ocfg = OracleConfig(hidden=H, n_experts=E, top_k=K, inter=64, score_func=score_func,
+                        routed_scaling_factor=2.5, eps=1e-5)
+    h = rms_norm(x, t["post_attention_layernorm.weight"], ocfg.eps)
+    ids, w, logits = route(h, t["mlp.gate.weight"], t["mlp.gate.e_score_correction_bias"], ocfg)
+    got = r["topk_ids"].cpu().numpy()
+    tied = np.isin(ids, np.arange(12)).sum(axis=1)
+    assert np.count_nonzero((tied > 0) & (tied < K)) > 10  # the tie group straddles the boundary
+    for row in np.nonzero((got != ids).any(axis=1))[0]:
+        srt = np.sort(logits[row])[::-1]
+        gap = np.min(np.abs(np.diff(srt[: K + 1]))) / max(abs(srt[K - 1]), 1e-30)
+        assert gap < 1e-6 and not np.all(logits[row, :12] == logits[row, 0]), \
+            f"token {row}: {got[row]} vs {ids[row]}"
+    np.testing.assert_allclose(r["topk_w"].cpu().numpy()[got == ids], w[got == ids], rtol=1e-5)
+    ml.close()
 
 
 @pytest.mark.parametrize("T", [1, 4])
