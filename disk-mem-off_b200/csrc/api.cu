@@ -138,9 +138,8 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
   // split-K is used only for 16-token tiles when a list has fewer than four
   // waves of tiles, so its scratch is bounded by 4 * SMs tiles of kMaxKSplit partials
   L.max_split_tiles = (L.bn == kSplitTileRows) ? 4 * p.num_sms : 0;
-  L.tiles1 = take(static_cast<size_t>(L.max_tiles1) * kMaxKSplit * sizeof(Tile));
-  L.tiles2 = take(static_cast<size_t>(L.max_tiles2) * kMaxKSplit * sizeof(Tile));
-  L.tile_count = take(16);
+  L.tile_pre = take(static_cast<size_t>(2) * (E + 1) * 4);
+  L.tile_info = take(32);
   L.kpart = take(static_cast<size_t>(L.max_split_tiles) * kMaxKSplit * kBM * kSplitTileRows * 4);
   L.kcount1 = take(static_cast<size_t>(L.max_split_tiles) * 4);
   L.kcount2 = take(static_cast<size_t>(L.max_split_tiles) * 4);
@@ -580,7 +579,7 @@ int moe_forward(MoePlan* plan, const float* x_dev, float* out_dev, int32_t T, vo
   if (rc != MOE_OK) return rc;
   MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
-                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr, p.n_local}, s));
   MOE_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                           reinterpret_cast<float*>(ws + L.y_s),
                           reinterpret_cast<int32_t*>(ws + L.slot_row),
@@ -618,7 +617,7 @@ int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t
   MOE_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_CUDA(cudaEventRecord(ev[2], s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
-                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr, p.n_local}, s));
   MOE_CUDA(cudaEventRecord(ev[3], s));
   MOE_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                           reinterpret_cast<float*>(ws + L.y_s),
@@ -724,10 +723,10 @@ int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_exp
   const WsLayout L = ws_layout_ep_experts(p, R);
   char* ws = static_cast<char*>(workspace);
   MOE_CUDA(launch_group_rows(p, L, ws, recv_experts, static_cast<const __half*>(recv_rows), R, s));
-  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr, p.n_local}, s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
                        GemmIO{R, 0, static_cast<__half*>(y_out),
-                              reinterpret_cast<const int32_t*>(ws + L.perm)},
+                              reinterpret_cast<const int32_t*>(ws + L.perm), p.n_local},
                        s));
   return MOE_OK;
 }
@@ -742,8 +741,8 @@ int moe_ep_shared(MoePlan* plan, int32_t T, void* workspace, uint64_t workspace_
   const WsLayout L = ws_layout(p, T);
   char* ws = static_cast<char*>(workspace);
   MOE_CUDA(launch_shared_tiles(p, L, ws, T, s));
-  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{T * p.K, T, nullptr, nullptr}, s));
-  MOE_CUDA(launch_gemm(p, L, ws, true, GemmIO{T * p.K, T, nullptr, nullptr}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{T * p.K, T, nullptr, nullptr, 0}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, GemmIO{T * p.K, T, nullptr, nullptr, 0}, s));
   return MOE_OK;
 }
 

@@ -32,9 +32,8 @@ struct GemmArgs {
   CUtensorMap a_shared;  // shared expert weights [m_limit_shared][K]
   CUtensorMap b_routed;  // activations f16 [rows][K]
   CUtensorMap b_shared;
-  const Tile* tiles;
-  const int32_t* tile_count;
-  int count_index;
+  TileMap map;           // routed / shared unit list (grouped GEMMs)
+  int router_grid;       // 1: router mode, units form a plain (m, n, split) grid
   int max_tiles;
   int n_local;           // group id of the shared expert
   int rows_a_routed;     // A rows per routed expert
@@ -122,6 +121,56 @@ MOE_DEV void convert_row_i8_f16(const int8_t* src_row, uint8_t* dst_tile, int r)
 
 enum GemmMode { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_ROUTER = 2 };
 
+// Unit u of a tile map (see TileMap).  A map that does not describe u (a
+// corrupted count) yields a tile that tile_ok rejects.
+MOE_DEV Tile tile_at(const TileMap& m, int u, int tot, int splits) {
+  Tile t;
+  t.group = -1;
+  t.m0 = 0;
+  t.row0 = 0;
+  t.nvalid = 0;
+  t.kb0 = t.kb1 = 0;
+  t.tile_id = 0;
+  t.split = 1 << 16;
+  if (splits < 1) return t;
+  const int q = u / splits, sidx = u - q * splits;
+  int nk;
+  if (q < tot) {
+    if (m.groups <= 0) return t;
+    int lo = 0, hi = m.groups;  // the last group g with pre[g] <= q owns tile q
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(m.pre + mid) <= q) lo = mid;
+      else hi = mid;
+    }
+    const int o0 = __ldg(m.off + lo);
+    const int cc = __ldg(m.off + lo + 1) - o0;
+    const int nt = (cc + m.bn - 1) / m.bn;
+    if (nt <= 0) return t;
+    const int l = q - __ldg(m.pre + lo);
+    const int mm = l / nt, n = l - mm * nt;
+    t.group = lo;
+    t.m0 = mm * kBM;
+    t.row0 = o0 + n * m.bn;
+    t.nvalid = min(m.bn, cc - n * m.bn);
+    nk = m.nk;
+  } else {
+    if (m.shared_ntn <= 0) return t;
+    const int i = q - tot;
+    const int mm = i / m.shared_ntn, n = i - mm * m.shared_ntn;
+    t.group = m.shared_group;
+    t.m0 = mm * kBM;
+    t.row0 = n * m.bn;
+    t.nvalid = min(m.bn, m.shared_rows - n * m.bn);
+    nk = m.nk_shared;
+  }
+  t.kb0 = sidx * nk / splits;
+  t.kb1 = (sidx + 1) * nk / splits;
+  t.split = sidx | (splits << 16);
+  t.tile_id = q;
+  return t;
+}
+
 template <int BN, int MODE, bool INT8>
 __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
@@ -149,12 +198,14 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntiles = args.tiles ? min(*(args.tile_count + args.count_index), args.max_tiles)
-                                : args.max_tiles;
-  // Tile lists come from the routing kernels; the router GEMM's units are a
-  // plain (m, n, K split) grid derived from the index.
+  // Grouped GEMMs read their unit count and K split from the tile map the
+  // routing kernels wrote; the router GEMM's units are a plain (m, n, K split)
+  // grid derived from the index.
+  const int map_tot = args.router_grid ? 0 : __ldg(args.map.info);
+  const int map_splits = args.router_grid ? 1 : __ldg(args.map.info + 1);
+  const int ntiles = args.router_grid ? args.max_tiles : min(__ldg(args.map.info + 2), args.max_tiles);
   auto fetch_tile = [&](int ti) {
-    if (args.tiles) return args.tiles[ti];
+    if (!args.router_grid) return tile_at(args.map, ti, map_tot, map_splits);
     Tile t;
     const int ntn = args.implicit_ntn, ns = args.implicit_splits;
     const int sidx = ti % ns, mn = ti / ns;
@@ -489,7 +540,7 @@ static cudaError_t dispatch_bn(const GemmArgs& a, int bn, int grid, cudaStream_t
 
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, int T,
                         cudaStream_t s) {
-  return launch_gemm(p, L, ws, down, GemmIO{T * p.K, T, nullptr, nullptr}, s);
+  return launch_gemm(p, L, ws, down, GemmIO{T * p.K, T, nullptr, nullptr, p.n_local}, s);
 }
 
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
@@ -519,7 +570,6 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, c
     a.k_shared = p.H;
     a.scale_routed = p.w.s13;
     a.scale_shared = p.w.ss13;
-    a.count_index = 0;
   } else {
     a.a_routed = p.tm_w2;
     a.a_shared = has_sh ? p.tm_ws2 : p.tm_w2;
@@ -536,10 +586,21 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, c
     a.k_shared = has_sh ? p.SI : p.I;
     a.scale_routed = p.w.s2;
     a.scale_shared = p.w.ss2;
-    a.count_index = 1;
   }
-  a.tiles = reinterpret_cast<const Tile*>(ws + (down ? L.tiles2 : L.tiles1));
-  a.tile_count = reinterpret_cast<const int32_t*>(ws + L.tile_count);
+  const int32_t* pre = reinterpret_cast<const int32_t*>(ws + L.tile_pre);
+  a.map.pre = down ? pre + (io.groups + 1) : pre;
+  a.map.off = reinterpret_cast<const int32_t*>(ws + L.offsets);
+  a.map.info = reinterpret_cast<const int32_t*>(ws + L.tile_info) + (down ? 4 : 0);
+  a.map.groups = io.groups;
+  a.map.bn = bn;
+  a.map.mt = (a.m_limit_routed + kBM - 1) / kBM;
+  a.map.mt_shared = (a.m_limit_shared + kBM - 1) / kBM;
+  a.map.shared_ntn = (has_sh && T > 0) ? (T + bn - 1) / bn : 0;
+  a.map.shared_rows = T;
+  a.map.shared_group = p.n_local;
+  a.map.nk = (a.k_routed + kBK - 1) / kBK;
+  a.map.nk_shared = (a.k_shared + kBK - 1) / kBK;
+  a.router_grid = 0;
   a.n_local = p.n_local;
   a.act_routed = act;
   a.act_shared = act_s;
@@ -597,9 +658,7 @@ cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T
     return cudaErrorInvalidValue;
   }
   a.b_shared = a.b_routed;
-  a.tiles = nullptr;
-  a.tile_count = nullptr;
-  a.count_index = 0;
+  a.router_grid = 1;
   const int mt = (p.router_rows + kBM - 1) / kBM;
   a.implicit_ntn = (T + BN - 1) / BN;
   a.implicit_rows = T;

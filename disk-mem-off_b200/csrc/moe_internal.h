@@ -37,6 +37,23 @@ struct Tile {
   int tile_id;
 };
 
+// The unit list of one grouped-GEMM launch, in device memory, written by the
+// routing kernels: routed tiles are numbered expert-major (group g owns tiles
+// [pre[g], pre[g+1]), weight m-tile outer, token tile inner), the shared
+// expert's tiles follow, and each tile expands into `splits` adjacent K-split
+// units.  The GEMM derives unit u's Tile from this map (tile_at), so routing
+// writes E+1 prefix entries per launch instead of a list of every unit.
+struct TileMap {
+  const int32_t* pre;   // [groups + 1] routed tile prefix; pre[groups] = routed tiles
+  const int32_t* off;   // [groups + 1] first row of each group in the B operand
+  const int32_t* info;  // [3]: routed tiles, K splits, units
+  int groups;           // routed groups (experts of this launch)
+  int bn;               // token rows per tile
+  int mt;               // weight m-tiles per routed group
+  int mt_shared, shared_ntn, shared_rows, shared_group;
+  int nk, nk_shared;    // k-blocks of routed / shared tiles
+};
+
 constexpr int kMaxKSplit = 4;       // K splits per tile for small decode batches
 constexpr int kSplitTileRows = 16;  // split-K only with 16-token tiles (BN = 16)
 
@@ -79,7 +96,9 @@ struct Plan {
 // Workspace carve-up for one forward of T tokens (offsets in bytes).
 struct WsLayout {
   size_t h16, xg, act, act_s, y, y_s, logits, part, ss_part, rms, counters, ids, wts, sgate;
-  size_t bm, hist, base, offsets, perm, slot_row, tiles1, tiles2, tile_count;
+  size_t bm, hist, base, offsets, perm, slot_row;
+  size_t tile_pre;   // [2][groups + 1] routed tile prefix per GEMM (gate/up, down)
+  size_t tile_info;  // [2][4]: routed tiles, K splits, units per GEMM
   size_t kpart, kcount1, kcount2;  // split-K partials [units][128][16] f32, per-tile counters
   int max_split_tiles;             // tiles a launch may split (0 = never)
   size_t total;
@@ -125,6 +144,7 @@ struct GemmIO {
   int shared_rows;
   __half* y_half;
   const int32_t* y_row_map;
+  int groups;  // routed groups whose tile map the routing kernels wrote
 };
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
                         cudaStream_t s);

@@ -99,7 +99,7 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   MOE_NA_CUDA(launch_route(p, L, ws, x_dev, T, true, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, true,
-                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr}, s));
+                       GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr, p.n_local}, s));
   MOE_NA_CUDA(launch_combine_half(p, x_dev, reinterpret_cast<const __half*>(ws + L.y),
                              reinterpret_cast<float*>(ws + L.y_s),
                              reinterpret_cast<int32_t*>(ws + L.slot_row),

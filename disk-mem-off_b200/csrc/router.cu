@@ -662,9 +662,9 @@ struct TileArgs {
   int shared_group;                // group id the GEMM treats as the shared expert (n_local)
   int nk1, nk1s, nk2, nk2s;        // k-blocks: gate/up routed / shared, down routed / shared
   int num_sms, max_split_tiles;
-  Tile* tiles1;
-  Tile* tiles2;
-  int32_t* tile_count;
+  int32_t* pre1;                   // [E + 1] gate/up routed tile prefix
+  int32_t* pre2;                   // [E + 1] down routed tile prefix
+  int32_t* info;                   // [2][4]: routed tiles, K splits, units per GEMM
   int* kcount1;
   int* kcount2;
   int* err;
@@ -699,83 +699,47 @@ MOE_DEV int choose_ksplit(int c, int g, int max_split_tiles, int nk_min) {
   return best;
 }
 
-// Expert e = threadIdx.x owns `cnt` rows starting at `off`.  Writes both GEMM
-// unit lists: tiles expert-major (weight m-tile outer, token tile inner, so a
-// weight tile is reused by neighbouring CTAs while it is in L2), the shared
-// expert's tiles last, each tile expanded into its K splits (adjacent units,
-// so the splits of one tile run side by side).  Called by every thread of a
-// 1024-thread CTA.
-__device__ void build_tile_lists(int cnt, int off, const TileArgs& a, int* s_p1, int* s_p2,
-                                 int* s_cnt, int* s_off) {
-  __shared__ int s_split[2];
+// Expert e = threadIdx.x owns `cnt` rows.  Writes both GEMMs' tile maps: the
+// routed tile prefix over experts (ceil(cnt / bn) token tiles times the weight
+// m-tiles), the unit counts with the shared expert's tiles appended, and the K
+// split chosen for each list; zeroes the split arrival counters.  Called by
+// every thread of a 1024-thread CTA.
+__device__ void build_tile_lists(int cnt, const TileArgs& a) {
+  __shared__ int s_c[2], s_split[2];
   const int e = threadIdx.x;
   const int ntn = (e < a.E) ? (cnt + a.bn - 1) / a.bn : 0;
   int tot1 = 0, tot2 = 0;
   const int p1 = block_excl_scan(ntn * a.mt1, &tot1);
   const int p2 = block_excl_scan(ntn * a.mt2, &tot2);
   if (e < a.E) {
-    s_p1[e] = p1;
-    s_p2[e] = p2;
-    s_cnt[e] = cnt;
-    s_off[e] = off;
+    a.pre1[e] = p1;
+    a.pre2[e] = p2;
   }
-  const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
-  const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
   if (e == 0) {
-    s_p1[a.E] = tot1;
-    s_p2[a.E] = tot2;
-    s_split[0] = choose_ksplit(c1, a.num_sms, a.max_split_tiles, min(a.nk1, a.has_shared ? a.nk1s : a.nk1));
-    s_split[1] = choose_ksplit(c2, a.num_sms, a.max_split_tiles, min(a.nk2, a.has_shared ? a.nk2s : a.nk2));
+    const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
+    const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
+    const int s1 = choose_ksplit(c1, a.num_sms, a.max_split_tiles, min(a.nk1, a.has_shared ? a.nk1s : a.nk1));
+    const int s2 = choose_ksplit(c2, a.num_sms, a.max_split_tiles, min(a.nk2, a.has_shared ? a.nk2s : a.nk2));
     if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_BAD_TILE);
+    a.pre1[a.E] = tot1;
+    a.pre2[a.E] = tot2;
+    s_c[0] = min(c1, a.max1);
+    s_c[1] = min(c2, a.max2);
+    s_split[0] = s1;
+    s_split[1] = s2;
+    a.info[0] = tot1;
+    a.info[1] = s1;
+    a.info[2] = s_c[0] * s1;
+    a.info[4] = tot2;
+    a.info[5] = s2;
+    a.info[6] = s_c[1] * s2;
   }
   __syncthreads();
   for (int pass = 0; pass < 2; ++pass) {
-    const int* pre = pass ? s_p2 : s_p1;
-    const int tot = pass ? tot2 : tot1;
-    const int c = min(pass ? c2 : c1, pass ? a.max2 : a.max1);
-    const int nkr = pass ? a.nk2 : a.nk1, nks = pass ? a.nk2s : a.nk1s;
-    const int S = s_split[pass];
-    Tile* out = pass ? a.tiles2 : a.tiles1;
-    int* kcount = pass ? a.kcount2 : a.kcount1;
-    for (int u = threadIdx.x; u < c * S; u += blockDim.x) {
-      const int q = u / S, sidx = u % S;
-      Tile t;
-      int nk;
-      if (q < tot) {
-        int lo = 0, hi = a.E;  // largest ex with pre[ex] <= q
-        while (hi - lo > 1) {
-          const int mid = (lo + hi) >> 1;
-          if (pre[mid] <= q) lo = mid;
-          else hi = mid;
-        }
-        const int ex = lo;
-        const int cc = s_cnt[ex];
-        const int nt = (cc + a.bn - 1) / a.bn;
-        const int l = q - pre[ex];
-        const int m = l / nt, n = l % nt;
-        t.group = ex;
-        t.m0 = m * kBM;
-        t.row0 = s_off[ex] + n * a.bn;
-        t.nvalid = min(a.bn, cc - n * a.bn);
-        nk = nkr;
-      } else {
-        const int i = q - tot;
-        const int m = i / nts, n = i % nts;
-        t.group = a.shared_group;
-        t.m0 = m * kBM;
-        t.row0 = n * a.bn;
-        t.nvalid = min(a.bn, a.T - n * a.bn);
-        nk = nks;
-      }
-      t.kb0 = sidx * nk / S;
-      t.kb1 = (sidx + 1) * nk / S;
-      t.split = sidx | (S << 16);
-      t.tile_id = q;
-      out[u] = t;
+    if (s_split[pass] > 1) {
+      int* kcount = pass ? a.kcount2 : a.kcount1;
+      for (int q = threadIdx.x; q < s_c[pass]; q += blockDim.x) kcount[q] = 0;
     }
-    if (S > 1)
-      for (int q = threadIdx.x; q < c; q += blockDim.x) kcount[q] = 0;
-    if (threadIdx.x == 0) a.tile_count[pass] = c * S;
   }
 }
 
@@ -795,10 +759,7 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
   const int words = (T + 31) >> 5;
   int* s_ids = tsm;                                              // [T*K]
   uint32_t* bm = reinterpret_cast<uint32_t*>(s_ids + T * K);     // [E][words]
-  int* s_p1 = reinterpret_cast<int*>(bm + E * words);            // [E+1]
-  int* s_p2 = s_p1 + (E + 1);
-  int* s_cnt = s_p2 + (E + 1);
-  int* s_off = s_cnt + (E + 1);
+  int* s_off = reinterpret_cast<int*>(bm + E * words);           // [E]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < E * words; i += blockDim.x) bm[i] = 0u;
   for (int t = warp; t < T; t += 32) {
@@ -820,9 +781,12 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
     for (int w = 0; w < words; ++w) cnt += __popc(bm[threadIdx.x * words + w]);
   int all = 0;
   const int off = block_excl_scan(threadIdx.x < E ? cnt : 0, &all);
-  if (threadIdx.x < E) offsets[threadIdx.x] = off;
+  if (threadIdx.x < E) {
+    offsets[threadIdx.x] = off;
+    s_off[threadIdx.x] = off;
+  }
   if (threadIdx.x == 0) offsets[E] = all;
-  build_tile_lists(cnt, off, ta, s_p1, s_p2, s_cnt, s_off);  // also fills s_off
+  build_tile_lists(cnt, ta);
   __syncthreads();
   for (int q = threadIdx.x; q < T * K; q += blockDim.x) {
     const int e = s_ids[q];
@@ -872,7 +836,6 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
                                                          int nchunks, int32_t* __restrict__ base,
                                                          int32_t* __restrict__ offsets,
                                                          TileArgs ta) {
-  __shared__ int s_p1[1025], s_p2[1025], s_cnt[1025], s_off[1025];
   const int e = threadIdx.x, E = ta.E;
   int tot = 0;
   if (e < E) {
@@ -888,7 +851,7 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
     for (int c = 0; c < nchunks; ++c) base[static_cast<size_t>(c) * E + e] += off;
   }
   if (e == 0) offsets[E] = all;
-  build_tile_lists(tot, off, ta, s_p1, s_p2, s_cnt, s_off);
+  build_tile_lists(tot, ta);
 }
 
 __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __restrict__ ids,
@@ -1107,9 +1070,9 @@ static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T, int
   ta.nk2s = p.SI > 0 ? (p.SI + kBK - 1) / kBK : ta.nk2;
   ta.num_sms = p.num_sms;
   ta.max_split_tiles = L.max_split_tiles;
-  ta.tiles1 = reinterpret_cast<Tile*>(ws + L.tiles1);
-  ta.tiles2 = reinterpret_cast<Tile*>(ws + L.tiles2);
-  ta.tile_count = reinterpret_cast<int32_t*>(ws + L.tile_count);
+  ta.pre1 = reinterpret_cast<int32_t*>(ws + L.tile_pre);
+  ta.pre2 = ta.pre1 + (groups + 1);
+  ta.info = reinterpret_cast<int32_t*>(ws + L.tile_info);
   ta.kcount1 = reinterpret_cast<int*>(ws + L.kcount1);
   ta.kcount2 = reinterpret_cast<int*>(ws + L.kcount2);
   ta.err = p.d_err;
@@ -1147,7 +1110,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   if (route_uses_tail(p, T)) {
     const int words = (T + 31) / 32;
     const size_t smem = (static_cast<size_t>(T) * K + static_cast<size_t>(E) * words +
-                         4 * static_cast<size_t>(E + 1)) * sizeof(int);
+                         static_cast<size_t>(E)) * sizeof(int);
 #define MOE_TAIL_CASE(V)                                                                        \
   do {                                                                                          \
     static bool done[64] = {};                                                                  \
