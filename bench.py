@@ -29,6 +29,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import sys
 import threading
 import time
@@ -47,6 +48,25 @@ GLM = dict(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536)
 
 
 FALLBACK_BF16_TFLOPS = 1590.0
+
+
+PROFILE_GEMM = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                            "moe_gemm_glm47_decode_T64.md")
+
+
+def _traffic_ratio(kernel: str) -> float | None:
+    """DRAM bytes / algorithmic bytes of a grouped GEMM launch, from the committed
+    ncu summary (a 32-expert capture of the same kernel; traffic scales with the
+    weights streamed, which the algorithmic count tracks)."""
+    try:
+        with open(PROFILE_GEMM) as f:
+            for line in f:
+                m = re.match(rf"traffic_ratio_{kernel}\s*=\s*([0-9.]+)", line.strip())
+                if m:
+                    return float(m.group(1))
+    except OSError:
+        return None
+    return None
 
 
 def _peaks() -> tuple[float, str]:
@@ -506,10 +526,16 @@ def run_ours(args) -> None:  # noqa: ANN001
             "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel gate/up (swap-AB tcgen05)",
                          "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
                          "frac": gate_gbs / hbm, "peak_source": peak_kind,
-                         "traffic": None,
+                         "traffic": (_traffic_ratio("gateup") * ab["gateup"]
+                                     if _traffic_ratio("gateup") else None),
+                         "traffic_source": "profiles/moe_gemm_glm47_decode_T64.md: "
+                                           "dram bytes / algorithmic bytes of an ncu capture "
+                                           "(32 experts), times this launch's algorithmic bytes",
                          "algorithmic_bytes_per_launch": ab["gateup"],
                          "launch_ms": stage[1]},
             "roofline_down": {"achieved": down_gbs, "frac": down_gbs / hbm,
+                              "traffic": (_traffic_ratio("down") * ab["down"]
+                                          if _traffic_ratio("down") else None),
                               "algorithmic_bytes_per_launch": ab["down"], "launch_ms": stage[2]},
             "roofline_layer": {"achieved": layer_gbs, "frac": layer_gbs / hbm,
                                "algorithmic_bytes_per_step": ab["layer"],
@@ -521,9 +547,10 @@ def run_ours(args) -> None:  # noqa: ANN001
                     "d2h_bytes_per_step": T_main * GLM["hidden"] * 4,
                     "ms_per_step": e2e_s * 1e3},
             "cpu_baseline": cpu,
-            # our kernels per forward: router, decode tail (T <= 256; else top-k,
-            # histogram, scan, scatter), dispatch, two grouped GEMMs, combine
-            "gpu_launches": (6 if T_main <= 256 else 9) * args.steps,
+            # our kernels per forward: router, decode tail, dispatch, two grouped
+            # GEMMs, combine (T <= 256); prefill: prep, router GEMM, selection,
+            # histogram, scan, scatter, gather, two grouped GEMMs, combine
+            "gpu_launches": (6 if T_main <= 256 else 10) * args.steps,
             "clocks": clocks,
             "sub": sub,
             "other_configs": other,
