@@ -190,7 +190,10 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
-MOE_DEV float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// SwiGLU's silu in the GEMM epilogue (its f16 output rounds far above the
+// intrinsics' error); the exponent is clamped so the fast divide never sees a
+// denominator beyond 2^126.
+MOE_DEV float silu_f(float g) { return __fdividef(g, 1.0f + __expf(fminf(-g, 80.f))); }
 MOE_DEV float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 }  // namespace moe

@@ -60,8 +60,9 @@ struct GemmArgs {
   int* err;
 };
 
-// Named barrier of the four epilogue warps (barrier 0 is __syncthreads).
-MOE_DEV void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the NT epilogue threads (barrier 0 is __syncthreads).
+template <int NT>
+MOE_DEV void epilogue_bar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
 template <int BN>
 struct TileCfg {
@@ -69,12 +70,29 @@ struct TileCfg {
   static constexpr int kStageA8 = kBM * kBK;         // int8 staging tile, 8 KiB
   static constexpr int kStageB = BN * kBK * 2;
   static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  // Epilogue warps: a 256-column accumulator takes 8 (each TMEM lane quarter
+  // twice, splitting the columns) so that draining a tile stays shorter than
+  // its MMAs; narrow decode tiles keep 4.
+  static constexpr int kEpiWarps = BN >= 128 ? 8 : 4;
 };
+
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2 .. 2+E-1 epilogue,
+// then 4 int8 -> f16 converter warps when the weights are INT8.
+template <int BN, bool INT8>
+__host__ __device__ constexpr int gemm_threads() {
+  return 32 * (2 + TileCfg<BN>::kEpiWarps + (INT8 ? 4 : 0));
+}
+
+// As many stages as fit under the 227 KiB opt-in shared memory per CTA (less the
+// alignment slack, barriers and a little static shared memory), up to 8: the
+// prefill GEMMs are bound by the bytes in flight between L2 and the SM (Little's
+// law over the ring), so a fourth INT8 stage at BN = 256 pays directly.
+constexpr int kGemmSmemBudget = 232448 - 1024 - 256 - 512;
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr int gemm_stages() {
   constexpr int per = TileCfg<BN>::kStageA + TileCfg<BN>::kStageB + (INT8 ? TileCfg<BN>::kStageA8 : 0);
-  constexpr int s = (200 * 1024) / per;
+  constexpr int s = kGemmSmemBudget / per;
   return s > 8 ? 8 : s;
 }
 
@@ -172,12 +190,13 @@ MOE_DEV Tile tile_at(const TileMap& m, int u, int tot, int splits) {
 }
 
 template <int BN, int MODE, bool INT8>
-__global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
+__global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
   constexpr bool DOWN = MODE == MODE_DOWN;
   constexpr int STAGES = gemm_stages<BN, INT8>();
   constexpr int SA = TileCfg<BN>::kStageA, SB = TileCfg<BN>::kStageB, SA8 = TileCfg<BN>::kStageA8;
-  constexpr uint32_t IDESC = idesc_f16_f32(kBM, BN);
+  // The MMA runs with N = nvalid rounded up to 16: a partial tile does not pay
+  // tensor time for the token columns it does not use.
   constexpr uint32_t TMEM_COLS = TileCfg<BN>::kTmemCols;
 
   extern __shared__ uint8_t smem_raw[];
@@ -194,7 +213,8 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
   uint64_t* mma_done = tempty + 2;       // final drain of in-flight MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  __shared__ int s_ready[2][4];   // epilogue warps' per-tile readiness votes
+  constexpr int EPI = TileCfg<BN>::kEpiWarps;
+  __shared__ int s_ready[2][EPI];  // epilogue warps' per-tile readiness votes
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -229,7 +249,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 32 * EPI);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
+        const uint32_t idesc = idesc_f16_f32(kBM, (t.nvalid + 15) & ~15);
         bool ok = true;
         for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -322,7 +343,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
           const uint32_t a0 = smem_u32(sA + s * SA), b0 = smem_u32(sB + s * SB);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            tc_mma_f16(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
+            tc_mma_f16(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
                        (kb > t.kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit(&empty[s]);
@@ -337,9 +358,11 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
         mbar_wait_drain(mma_done, 0);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + EPI) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;         // epilogue warp index
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int cfirst = (ew >> 2) * 16, cstep = 16 * (EPI / 4);  // its column chunks
     const int r = q * 32 + lane;
     int tl = 0;
     for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
@@ -347,13 +370,15 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       if (!tile_ok(t)) continue;
       const int buf = tl & 1;
       // every lane polls; the warp vote re-converges the warp before the
-      // .sync.aligned TMEM loads, and the four warps then agree through a
+      // .sync.aligned TMEM loads, and the epilogue warps then agree through a
       // double-buffered flag so that all of them take (or skip) the named
       // barriers below together
       const bool my_ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl >> 1) & 1, abort_flag));
-      if (lane == 0) s_ready[tl & 1][q] = my_ready ? 1 : 0;
-      epilogue_bar();
-      const bool ready = s_ready[tl & 1][0] && s_ready[tl & 1][1] && s_ready[tl & 1][2] && s_ready[tl & 1][3];
+      if (lane == 0) s_ready[tl & 1][ew] = my_ready ? 1 : 0;
+      epilogue_bar<32 * EPI>();
+      bool ready = true;
+#pragma unroll
+      for (int w = 0; w < EPI; ++w) ready = ready && s_ready[tl & 1][w];
       if (!ready) {
         *abort_flag = 1;
         record_error(args.err, DEV_TIMEOUT_TMEM_FULL);
@@ -371,7 +396,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       const int ncol = (t.nvalid + 15) & ~15;
-      for (int c0 = 0; c0 < ncol; c0 += 16) {
+      for (int c0 = cfirst; c0 < ncol; c0 += cstep) {
         float v[16];
         tmem_ld16(taddr + c0, v);
         if constexpr (BN == kSplitTileRows) {
@@ -384,9 +409,9 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) mine[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             __threadfence();
-            epilogue_bar();
+            epilogue_bar<32 * EPI>();
             if (threadIdx.x == 64) s_last = (atomicAdd(&args.kcount[t.tile_id], 1) == nsplit - 1) ? 1 : 0;
-            epilogue_bar();
+            epilogue_bar<32 * EPI>();
             if (!s_last) break;  // ncol == 16: this was the only chunk
             __threadfence();
 #pragma unroll
@@ -476,7 +501,7 @@ __global__ void __launch_bounds__(INT8 ? 320 : 192, 1)
     }
   } else if constexpr (INT8) {
     // ------------------------------------------------------------ int8 -> f16
-    const int r = (warp - 6) * 32 + lane;  // one A row per thread
+    const int r = (warp - 2 - EPI) * 32 + lane;  // one A row per thread
     int it = 0;
     for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
       const Tile t = fetch_tile(ti);
@@ -521,7 +546,7 @@ static cudaError_t run_gemm(const GemmArgs& a, int grid, cudaStream_t s) {
     if (st != cudaSuccess) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  moe_gemm_kernel<BN, MODE, INT8><<<grid, INT8 ? 320 : 192, smem, s>>>(a);
+  moe_gemm_kernel<BN, MODE, INT8><<<grid, gemm_threads<BN, INT8>(), smem, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -153,24 +153,43 @@ class MoeLayer:
         self.forward_ptr(x.data_ptr(), out.data_ptr(), t, ws.data_ptr(), ws.numel(), stream)
         return out
 
-    def forward_host(self, x: np.ndarray, stream: Any = None) -> np.ndarray:
-        """Host fp32 in, host fp32 out: pinned H2D, device forward, D2H (end-to-end path)."""
+    def forward_host(self, x: Any, stream: Any = None, out: Any = None) -> Any:
+        """Host fp32 in, host fp32 out: H2D, device forward, D2H (end-to-end path).
+
+        ``x`` is a numpy array (staged through the layer's pinned buffers and
+        answered with a new numpy array) or a pinned CPU torch tensor, which is
+        copied to the device directly; the result then goes to ``out`` (a pinned
+        CPU tensor of the same shape, allocated when omitted)."""
         torch = _torch()
-        x = np.ascontiguousarray(x, dtype=np.float32)
-        t, h = x.shape
+        pinned_in = isinstance(x, torch.Tensor)
+        if pinned_in:
+            if x.device.type != "cpu" or x.dtype != torch.float32 or not x.is_contiguous():
+                raise ValueError("x must be a contiguous fp32 CPU tensor")
+            t, h = x.shape
+        else:
+            x = np.ascontiguousarray(x, dtype=np.float32)
+            t, h = x.shape
         if h != self.cfg.hidden:
             raise ValueError(f"x must be [T, {self.cfg.hidden}]")
         if t == 0:
-            return x.copy()
+            return x.clone() if pinned_in else x.copy()
         pin_in, pin_out, dev_in, dev_out = self._staging(t)
-        np.copyto(pin_in[:t].numpy(), x)
+        if pinned_in:
+            src = x
+            dst = out if out is not None else torch.empty((t, h), dtype=torch.float32,
+                                                          pin_memory=True)
+            if dst.shape != (t, h) or dst.dtype != torch.float32 or dst.device.type != "cpu":
+                raise ValueError("out must be a [T, H] fp32 CPU tensor")
+        else:
+            np.copyto(pin_in[:t].numpy(), x)
+            src, dst = pin_in[:t], pin_out[:t]
         s = torch.cuda.current_stream(self.cfg.device) if stream is None else stream
-        dev_in[:t].copy_(pin_in[:t], non_blocking=True)
+        dev_in[:t].copy_(src, non_blocking=True)
         ws = self.workspace(t)
         self.forward_ptr(dev_in.data_ptr(), dev_out.data_ptr(), t, ws.data_ptr(), ws.numel(), s)
-        pin_out[:t].copy_(dev_out[:t], non_blocking=True)
+        dst.copy_(dev_out[:t], non_blocking=True)
         s.synchronize()
-        return pin_out[:t].numpy().copy()
+        return dst if pinned_in else dst.numpy().copy()
 
     def _staging(self, tokens: int) -> tuple[Any, Any, Any, Any]:
         torch = _torch()

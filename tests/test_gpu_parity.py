@@ -100,6 +100,16 @@ def test_host_buffers_end_to_end() -> None:
     out = ex._moe_mlp_block(x, t)  # same call the reference executor makes
     assert isinstance(out, np.ndarray) and out.shape == x.shape
     assert rel_l2(out, gout) <= TOL_16
+    # pinned host tensors in and out (no staging copies) give the same bits
+    blob, meta = pack_layer(t, expert_format="bfloat16")
+    ml = MoeLayer(_layer_cfg(spec, "f16", 8))
+    ml.bind_host(blob, meta)
+    x_pin = torch.from_numpy(x).pin_memory()
+    o_pin = torch.empty_like(x_pin).pin_memory()
+    assert ml.forward_host(x_pin, out=o_pin) is o_pin
+    np.testing.assert_array_equal(o_pin.numpy(), ml.forward_host(x))
+    assert rel_l2(o_pin.numpy(), gout) <= TOL_16
+    ml.close()
 
 
 def test_empty_batch_and_limits() -> None:
