@@ -128,6 +128,10 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
     L.ids = take(R * 4);
     L.wts = take(R * 4);
     L.sgate = take(static_cast<size_t>(T) * 4);
+    const bool prefill = !route_uses_tail(p, T);
+    L.cand = take(prefill ? static_cast<size_t>(T) * kCandMax * 4 : 0);
+    L.ncand = take(prefill ? static_cast<size_t>(T) * 4 : 0);
+    L.exact = take(prefill ? static_cast<size_t>(T) * (kCandMax + 1) * 4 : 0);
   }
   L.bm = take(static_cast<size_t>(L.nchunks) * E * 32 * 4);
   L.hist = take(static_cast<size_t>(L.nchunks) * E * 4);

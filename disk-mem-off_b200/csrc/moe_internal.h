@@ -21,6 +21,10 @@ constexpr int kMaxTopK = 32;
 constexpr float kRouterWeightScale = 1024.0f;
 // The prefill router GEMM splits K into at most this many partial logit planes.
 constexpr int kRouterMaxSplit = 4;
+// Prefill routing keeps the K + kRefineMargin best tensor-core candidates of a
+// token (kCandMax slots) for the fp32 re-decision.
+constexpr int kRefineMargin = 12;
+constexpr int kCandMax = kMaxTopK + kRefineMargin;
 
 // One unit of work for the grouped GEMM: weight rows [m0, m0+128) of group
 // `group` (local routed expert index, or n_local for the shared expert)
@@ -96,6 +100,7 @@ struct Plan {
 // Workspace carve-up for one forward of T tokens (offsets in bytes).
 struct WsLayout {
   size_t h16, xg, act, act_s, y, y_s, logits, part, ss_part, rms, counters, ids, wts, sgate;
+  size_t cand, ncand, exact;  // prefill router: candidate ids, rows to recompute, fp32 logits
   size_t bm, hist, base, offsets, perm, slot_row;
   size_t tile_pre;   // [2][groups + 1] routed tile prefix per GEMM (gate/up, down)
   size_t tile_info;  // [2][4]: routed tiles, K splits, units per GEMM

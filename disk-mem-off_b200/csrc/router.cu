@@ -288,328 +288,312 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
 
 // Prefill tensor-core router, selection stage.  The tensor-core logits use f16
 // operands (~2e-3 absolute error at most for GLM-4.7 shapes, 2.5e-4 typical),
-// so they only choose candidates: each warp sums its token's partial logit
-// planes and takes the C = K + 4 best keys.  The CTA then recomputes in fp32
-// on the CUDA cores (sum_k (w_k x_k) Wg_k / rms, in a fixed order), at one of
-// three levels per token:
-//   0: the K chosen experts, when the K-th and (K+1)-th keys are at least
-//      kRefineGap * max(1, |best key|) apart (the set is certain; the order
-//      and weights come from the fp32 logits);
-//   1: all C candidates, when that boundary gap is smaller;
-//   2: every expert, when even the K-th and C-th keys are that close (rare:
-//      eight ranks past the boundary).
-// kRefineGap is ~8x the largest f16 logit error seen, so the final selection,
-// tie rule and weights are those of the fp32 router.  The shared-expert gate
-// logit is always recomputed.
-//
-// The recomputation streams rows from L2 as jobs (token, group of up to
-// kSelRows rows, chunk of kSelChunk floats of H).  Thread t owns float4 slot t
-// of every row of a job: it stages its slots with cp.async into a
-// double-buffered shared-memory ring (job i+1 in flight while job i is used)
-// and reads back only its own slots, so jobs need no CTA barrier; the CTA
-// synchronises once per row group to add the 256 partial sums in a fixed order.
-constexpr int kRefineMargin = 8;
-constexpr float kRefineGap = 1.6e-2f;
-constexpr int kSelRows = 20;     // Wg rows per job (besides the x chunk)
-constexpr int kSelChunk = 1024;  // floats of H per job: one float4 per thread
-constexpr int kSelStages = 2;
-constexpr size_t kSelStageFloats = static_cast<size_t>(kSelRows + 1) * kSelChunk;
-constexpr size_t kSelSmemBytes = kSelStages * kSelStageFloats * sizeof(float);  // 168 KiB
+// so they only choose candidates; the decision is made on fp32 logits
+// recomputed on the CUDA cores (sum_k (w_k x_k) Wg_k / rms, in a fixed order),
+// in three launches:
+//   route_cand_kernel   warp per token: adds the logit planes (into plane 0),
+//                       takes the C = K + kRefineMargin best tensor-core keys
+//                       and names the rows to recompute: the K chosen experts
+//                       plus every candidate whose key is within kRefineGap *
+//                       max(1, |best key|) of the K-th key (usually none or
+//                       one); every expert when even the C-th key is that
+//                       close (ties across the whole window).
+//   route_exact_kernel  CTA per token, warp per row: fp32 dot products, with
+//                       loads unrolled across two rows so that many small CTAs
+//                       per SM keep L2 busy; writes the exact logits (plane 0's
+//                       row when every expert is recomputed) and the
+//                       shared-expert gate logit.
+//   route_final_kernel  warp per token: softmax over all experts with the
+//                       exact logits substituted, top-k among the recomputed
+//                       rows by exact keys and the lower-id tie rule, weights.
+// kRefineGap is ~4x the largest f16 logit error seen: an expert outside the
+// recomputed set is more than the gap below the K-th key, so the selection,
+// order and weights are those of the fp32 router.
+constexpr float kRefineGap = 8e-3f;
+static_assert(kCandMax <= 64, "route_final_kernel holds two candidate slots per lane");
 
 template <int VPL>
-__global__ void __launch_bounds__(256, 1) route_select_kernel(
-    float* __restrict__ logits, int nplanes, const float* __restrict__ x,
-    const float* __restrict__ wn, const float* __restrict__ wr, const float* __restrict__ rms,
-    const float* __restrict__ bias, int32_t* __restrict__ ids, float* __restrict__ wts,
-    float* __restrict__ sgate, int T, int E, int R, int H, int K, int score_func, int norm,
-    float scale, int* err) {
-  constexpr int CMAX = kMaxTopK + kRefineMargin;  // <= 64: two candidate slots per lane
-  extern __shared__ __align__(128) float sel_stage[];
-  __shared__ int s_cand[8][CMAX];
-  __shared__ float s_logit[8][CMAX];
-  __shared__ float s_part[8][kSelRows];
-  __shared__ float s_gate[8];
-  __shared__ int s_level[8];
-  __shared__ int s_jobbase[9];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int C = min(E, K + kRefineMargin);
-  const int nq = (H + kSelChunk - 1) / kSelChunk;
-  const bool gate = sgate != nullptr;
+__global__ void __launch_bounds__(256) route_cand_kernel(
+    float* __restrict__ logits, int nplanes, const float* __restrict__ bias,
+    int32_t* __restrict__ cand, int32_t* __restrict__ nrows, int T, int E, int R, int K,
+    int score_func, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
   const size_t plane = static_cast<size_t>(T) * R;
+  float* lrow = logits + static_cast<size_t>(t) * R;
+  const int C = min(E, K + kRefineMargin);
+  float key[VPL];
+  bool taken[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int e = j * 32 + lane;
+    key[j] = -FLT_MAX;
+    taken[j] = false;
+    if (e < E) {
+      float l = lrow[e];
+      for (int sp = 1; sp < nplanes; ++sp) l += lrow[sp * plane + e];
+      if (nplanes > 1) lrow[e] = l;  // plane 0 now holds the summed logits
+      key[j] = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bias[e] : l)
+                                                 : (bias ? sigmoid_f(l) + bias[e] : sigmoid_f(l));
+    }
+  }
+  if (nplanes > 1 && lane == 0 && E < R) {  // the shared-expert gate row
+    float l = lrow[E];
+    for (int sp = 1; sp < nplanes; ++sp) l += lrow[sp * plane + E];
+    lrow[E] = l;
+  }
+  float thr = 0.f, k_last = 0.f;
+  int n = K;
+  bool all_rows = false;
+  for (int r = 0; r < C; ++r) {
+    float bk = -FLT_MAX;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E && !taken[j] && (bid == 0x7fffffff || key[j] > bk || (key[j] == bk && e < bid))) {
+        bk = key[j];
+        bid = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+      if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
+        bk = ok;
+        bid = oid;
+      }
+    }
+    if (bid >= E) {  // a NaN key leaves no winner
+      record_error(err, DEV_BAD_ROUTE);
+      bid = 0;
+    }
+    if (r == 0) thr = kRefineGap * fmaxf(1.f, fabsf(bk));
+    if (r == K - 1) k_last = bk;
+    if (r >= K) {
+      if (k_last - bk < thr) {
+        n = r + 1;  // still inside the tie window
+        if (r == C - 1 && C < E) all_rows = true;
+      } else {
+        break;  // keys only fall from here on
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (j == (bid >> 5) && lane == (bid & 31)) taken[j] = true;
+    if (lane == 0) cand[static_cast<size_t>(t) * kCandMax + r] = bid;
+  }
+  if (lane == 0) nrows[t] = all_rows ? -1 : n;
+}
 
-  // rows of job (token j, group g): level 2 walks all R rows, else the
-  // candidates then the gate row E
-  auto row_count = [&](int lev) { return lev == 2 ? R : (lev == 0 ? K : C) + (gate ? 1 : 0); };
-  auto row_id = [&](int j, int lev, int idx) {
-    if (lev == 2) return idx;
-    return idx < (lev == 0 ? K : C) ? s_cand[j][idx] : E;
+// Rows of token t: its n candidates (then the gate row E when the layer has a
+// shared-expert gate), or all R router rows when n < 0.
+__global__ void __launch_bounds__(256) route_exact_kernel(
+    float* __restrict__ logits, const int32_t* __restrict__ cand, const int32_t* __restrict__ nrows,
+    const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ wr,
+    const float* __restrict__ rms, float* __restrict__ exact, int T, int E, int R, int H,
+    int has_gate) {
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = nrows[t];
+  const bool all_rows = n < 0;
+  const int rows = all_rows ? R : n + (has_gate ? 1 : 0);
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+  const float4* gr = reinterpret_cast<const float4*>(wn);
+  const int nv = H >> 2;
+  const float rt = rms[t];
+  auto row_of = [&](int r) {
+    if (all_rows) return r;
+    return r < n ? cand[static_cast<size_t>(t) * kCandMax + r] : E;
   };
-  for (int grp = blockIdx.x; grp * 8 < T; grp += gridDim.x) {
-    const int t = grp * 8 + warp;
-    const bool live = t < T;
-    const float* lrow = logits + static_cast<size_t>(live ? t : 0) * R;
-    float lg[VPL];  // tensor-core logits of this lane's experts
-    int cidx[VPL];  // candidate index of expert j*32+lane, or -1
-    // 1. candidates on the tensor-core keys (same keys and tie rule as warp_topk)
-    if (live) {
-      float key[VPL];
+  // two rows per pass, four float4 of each in flight per lane
+  for (int r0 = warp * 2; r0 < rows; r0 += 16) {
+    const int r1 = r0 + 1;
+    const bool has1 = r1 < rows;
+    const float4* w0 = reinterpret_cast<const float4*>(wr + static_cast<size_t>(row_of(r0)) * H);
+    const float4* w1 = reinterpret_cast<const float4*>(wr + static_cast<size_t>(row_of(has1 ? r1 : r0)) * H);
+    float a0 = 0.f, a1 = 0.f;
+    int k = lane;
+    for (; k + 96 < nv; k += 128) {
+      float4 xv[4], g[4], p[4], q[4];
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int e = j * 32 + lane;
-        key[j] = -FLT_MAX;
-        lg[j] = 0.f;
-        cidx[j] = -1;
-        if (e < E) {
-          float l = lrow[e];
-          for (int sp = 1; sp < nplanes; ++sp) l += lrow[sp * plane + e];
-          lg[j] = l;
-          key[j] = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bias[e] : l)
-                                                     : (bias ? sigmoid_f(l) + bias[e] : sigmoid_f(l));
-        }
+      for (int i = 0; i < 4; ++i) {
+        xv[i] = xr[k + 32 * i];
+        g[i] = __ldg(gr + k + 32 * i);
+        p[i] = __ldg(w0 + k + 32 * i);
+        q[i] = __ldg(w1 + k + 32 * i);
       }
-      float thr = 0.f, k_last = 0.f;
-      int level = 0;
-      for (int r = 0; r < C; ++r) {
-        float bk = -FLT_MAX;
-        int bid = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-          const int e = j * 32 + lane;
-          if (e < E && cidx[j] < 0 && (bid == 0x7fffffff || key[j] > bk || (key[j] == bk && e < bid))) {
-            bk = key[j];
-            bid = e;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-          if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
-            bk = ok;
-            bid = oid;
-          }
-        }
-        if (bid >= E) {  // a NaN key leaves no winner
-          record_error(err, DEV_BAD_ROUTE);
-          bid = 0;
-        }
-        if (r == 0) thr = kRefineGap * fmaxf(1.f, fabsf(bk));
-        if (r == K - 1) k_last = bk;
-        if (r == K && k_last - bk < thr) level = max(level, 1);
-        if (r == C - 1 && C < E && k_last - bk < thr) level = 2;
-        float mine = 0.f;
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-          if (j == (bid >> 5)) {
-            mine = lg[j];
-            if (lane == (bid & 31)) cidx[j] = r;
-          }
-        }
-        const float l = __shfl_sync(0xffffffffu, mine, bid & 31);
-        if (lane == 0) {
-          s_cand[warp][r] = bid;
-          s_logit[warp][r] = l;
-        }
-      }
-      if (lane == 0) s_level[warp] = level;
-    } else if (lane == 0) {
-      s_level[warp] = -1;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int b = 0;
-      for (int j = 0; j < 8; ++j) {
-        s_jobbase[j] = b;
-        if (s_level[j] >= 0) b += ((row_count(s_level[j]) + kSelRows - 1) / kSelRows) * nq;
-      }
-      s_jobbase[8] = b;
-    }
-    __syncthreads();
-    const int njobs = s_jobbase[8];
-    // job i -> (token j, row group g, chunk q)
-    auto decode = [&](int i, int& j, int& g, int& q) {
-      j = 0;
-      while (j < 7 && s_jobbase[j + 1] <= i) ++j;
-      const int rel = i - s_jobbase[j];
-      g = rel / nq;
-      q = rel % nq;
-    };
-    const int k4 = threadIdx.x * 4;
-    // this thread's slots of job i -> ring stage i % kSelStages (one commit group per job)
-    auto issue = [&](int i) {
-      int j, g, q;
-      decode(i, j, g, q);
-      const int lev = s_level[j];
-      const int rows = min(kSelRows, row_count(lev) - g * kSelRows);
-      const int len = min(kSelChunk, H - q * kSelChunk);
-      if (k4 < len) {
-        float* dst = sel_stage + (i % kSelStages) * kSelStageFloats + k4;
-        const size_t col = static_cast<size_t>(q) * kSelChunk + k4;
-        cp_async16(dst, x + static_cast<size_t>(grp * 8 + j) * H + col);
-        for (int r = 0; r < rows; ++r)
-          cp_async16(dst + (r + 1) * kSelChunk,
-                     wr + static_cast<size_t>(row_id(j, lev, g * kSelRows + r)) * H + col);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    // 2. fp32 logits, job by job
-    if (njobs > 0) issue(0);
-    float acc[kSelRows];
-    for (int i = 0; i < njobs; ++i) {
-      if (i + 1 < njobs) issue(i + 1);
-      else asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // job i's slots have landed
-      int j, g, q;
-      decode(i, j, g, q);
-      const int lev = s_level[j];
-      const int rows = min(kSelRows, row_count(lev) - g * kSelRows);
-      const int len = min(kSelChunk, H - q * kSelChunk);
-      if (q == 0) {
-#pragma unroll
-        for (int r = 0; r < kSelRows; ++r) acc[r] = 0.f;
-      }
-      const float* sx = sel_stage + (i % kSelStages) * kSelStageFloats;
-      if (k4 < len) {
-        const float4 xv = *reinterpret_cast<const float4*>(sx + k4);
-        const float4 gv = __ldg(reinterpret_cast<const float4*>(wn + q * kSelChunk + k4));
-        const float4 u = make_float4(gv.x * xv.x, gv.y * xv.y, gv.z * xv.z, gv.w * xv.w);
-#pragma unroll
-        for (int r = 0; r < kSelRows; ++r) {
-          if (r < rows) {
-            const float4 wv = *reinterpret_cast<const float4*>(sx + (r + 1) * kSelChunk + k4);
-            float a2 = acc[r];
-            a2 = fmaf(u.x, wv.x, a2);
-            a2 = fmaf(u.y, wv.y, a2);
-            a2 = fmaf(u.z, wv.z, a2);
-            a2 = fmaf(u.w, wv.w, a2);
-            acc[r] = a2;
-          }
-        }
-      }
-      if (q == nq - 1) {  // last chunk of this row group: reduce over the CTA in a fixed order
-#pragma unroll
-        for (int r = 0; r < kSelRows; ++r) {
-          if (r < rows) {
-            float v = acc[r];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) s_part[warp][r] = v;
-          }
-        }
-        __syncthreads();
-        if (warp == j && lane < rows) {
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) v += s_part[w][lane];
-          const int tj = grp * 8 + j;
-          v = v / rms[tj];
-          const int idx = g * kSelRows + lane;
-          if (lev == 2) {
-            logits[static_cast<size_t>(tj) * R + idx] = v;  // plane 0 row becomes exact
-            if (gate && idx == E) s_gate[j] = v;
-          } else if (idx < (lev == 0 ? K : C)) {
-            s_logit[j][idx] = v;
-          } else {
-            s_gate[j] = v;
-          }
-        }
-        __syncthreads();  // s_part is reusable
+      for (int i = 0; i < 4; ++i) {
+        const float4 u = make_float4(g[i].x * xv[i].x, g[i].y * xv[i].y, g[i].z * xv[i].z, g[i].w * xv[i].w);
+        a0 = fmaf(u.x, p[i].x, a0);
+        a0 = fmaf(u.y, p[i].y, a0);
+        a0 = fmaf(u.z, p[i].z, a0);
+        a0 = fmaf(u.w, p[i].w, a0);
+        a1 = fmaf(u.x, q[i].x, a1);
+        a1 = fmaf(u.y, q[i].y, a1);
+        a1 = fmaf(u.z, q[i].z, a1);
+        a1 = fmaf(u.w, q[i].w, a1);
       }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (!live) continue;
-    if (gate && lane == 0) sgate[t] = sigmoid_f(s_gate[warp]);
-    if (s_level[warp] == 2) {  // every logit of plane 0's row is exact now
-      warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, ids + static_cast<size_t>(t) * K,
-                     wts + static_cast<size_t>(t) * K, err);
-      continue;
-    }
-    // 3. softmax over all experts, candidates with their recomputed logits
-    float denom = 1.f, m = -FLT_MAX;
-    if (score_func == MOE_SCORE_SOFTMAX) {
-      float lv[VPL];
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int e = j * 32 + lane;
-        lv[j] = -FLT_MAX;
-        if (e < E) {
-          const float l = cidx[j] >= 0 ? s_logit[warp][cidx[j]] : lg[j];
-          lv[j] = bias ? l + bias[e] : l;
-          m = fmaxf(m, lv[j]);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float ssum = 0.f;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j)
-        if (j * 32 + lane < E) ssum += expf(lv[j] - m);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-      denom = ssum;
-    }
-    // 4. final top-k among the candidates: lane holds candidates lane and lane + 32
-    float ck[2], cv[2];
-    int ce[2], rank[2];
-#pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      const int c = lane + 32 * qq;
-      ce[qq] = 0x7fffffff;
-      ck[qq] = -FLT_MAX;
-      cv[qq] = 0.f;
-      rank[qq] = -1;
-      if (c < C) {
-        const int e = s_cand[warp][c];
-        const float l = s_logit[warp][c];
-        ce[qq] = e;
-        if (score_func == MOE_SCORE_SOFTMAX) {
-          ck[qq] = bias ? l + bias[e] : l;
-          cv[qq] = expf(ck[qq] - m) / denom;
-        } else {
-          cv[qq] = sigmoid_f(l);
-          ck[qq] = bias ? cv[qq] + bias[e] : cv[qq];
-        }
-      }
-    }
-    float sum = 0.f;
-    for (int r = 0; r < K; ++r) {
-      float bk = -FLT_MAX, bv = 0.f;
-      int bid = 0x7fffffff;
-#pragma unroll
-      for (int qq = 0; qq < 2; ++qq) {
-        if (ce[qq] != 0x7fffffff && rank[qq] < 0 &&
-            (bid == 0x7fffffff || ck[qq] > bk || (ck[qq] == bk && ce[qq] < bid))) {
-          bk = ck[qq];
-          bid = ce[qq];
-          bv = cv[qq];
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-        const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
-          bk = ok;
-          bid = oid;
-          bv = ov;
-        }
-      }
-#pragma unroll
-      for (int qq = 0; qq < 2; ++qq)
-        if (ce[qq] == bid) rank[qq] = r;
-      if (norm) sum += bv;  // rank order, like warp_topk
+    for (; k < nv; k += 32) {
+      const float4 xv = xr[k], g = __ldg(gr + k), p = __ldg(w0 + k), q = __ldg(w1 + k);
+      const float4 u = make_float4(g.x * xv.x, g.y * xv.y, g.z * xv.z, g.w * xv.w);
+      a0 = fmaf(u.x, p.x, a0);
+      a0 = fmaf(u.y, p.y, a0);
+      a0 = fmaf(u.z, p.z, a0);
+      a0 = fmaf(u.w, p.w, a0);
+      a1 = fmaf(u.x, q.x, a1);
+      a1 = fmaf(u.y, q.y, a1);
+      a1 = fmaf(u.z, q.z, a1);
+      a1 = fmaf(u.w, q.w, a1);
     }
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      if (rank[qq] >= 0) {
-        float wv = cv[qq];
-        if (norm) wv = wv / (sum + 1e-20f);
-        ids[static_cast<size_t>(t) * K + rank[qq]] = ce[qq];
-        wts[static_cast<size_t>(t) * K + rank[qq]] = wv * scale;
+    for (int o = 16; o > 0; o >>= 1) {
+      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    }
+    if (lane == 0) {
+      const float v0 = a0 / rt, v1 = a1 / rt;
+      if (all_rows) {
+        logits[static_cast<size_t>(t) * R + r0] = v0;  // plane 0's row becomes exact
+        if (has1) logits[static_cast<size_t>(t) * R + r1] = v1;
+      } else {
+        exact[static_cast<size_t>(t) * (kCandMax + 1) + r0] = v0;
+        if (has1) exact[static_cast<size_t>(t) * (kCandMax + 1) + r1] = v1;
       }
     }
   }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) route_final_kernel(
+    const float* __restrict__ logits, const int32_t* __restrict__ cand,
+    const int32_t* __restrict__ nrows, const float* __restrict__ exact,
+    const float* __restrict__ bias, int32_t* __restrict__ ids, float* __restrict__ wts,
+    float* __restrict__ sgate, int T, int E, int R, int K, int score_func, int norm, float scale,
+    int* err) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float* lrow = logits + static_cast<size_t>(t) * R;
+  const int n = nrows[t];
+  if (n < 0) {  // every expert recomputed: plane 0's row is exact
+    warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, ids + static_cast<size_t>(t) * K,
+                   wts + static_cast<size_t>(t) * K, err);
+    if (sgate && lane == 0) sgate[t] = sigmoid_f(lrow[E]);
+    return;
+  }
+  const int32_t* crow = cand + static_cast<size_t>(t) * kCandMax;
+  const float* xrow = exact + static_cast<size_t>(t) * (kCandMax + 1);
+  // this lane's recomputed candidates (slots lane, lane + 32)
+  float cl[2];
+  int ce[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int c = lane + 32 * q;
+    ce[q] = c < n ? crow[c] : 0x7fffffff;
+    cl[q] = c < n ? xrow[c] : 0.f;
+  }
+  float denom = 1.f, m = -FLT_MAX;
+  if (score_func == MOE_SCORE_SOFTMAX) {
+    float lv[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int e = j * 32 + lane;
+      lv[j] = -FLT_MAX;
+      if (e < E) lv[j] = lrow[e];
+    }
+    // substitute the exact logits of the recomputed candidates
+    for (int c = 0; c < n; ++c) {
+      const int e = __shfl_sync(0xffffffffu, c < 32 ? ce[0] : ce[1], c & 31);
+      const float l = __shfl_sync(0xffffffffu, c < 32 ? cl[0] : cl[1], c & 31);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        if (j == (e >> 5) && lane == (e & 31)) lv[j] = l;
+    }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E) {
+        if (bias) lv[j] = lv[j] + bias[e];
+        m = fmaxf(m, lv[j]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float ssum = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (j * 32 + lane < E) ssum += expf(lv[j] - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    denom = ssum;
+  }
+  float ck[2], cv[2];
+  int rank[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    ck[q] = -FLT_MAX;
+    cv[q] = 0.f;
+    rank[q] = -1;
+    if (ce[q] != 0x7fffffff) {
+      const int e = ce[q];
+      const float l = cl[q];
+      if (score_func == MOE_SCORE_SOFTMAX) {
+        ck[q] = bias ? l + bias[e] : l;
+        cv[q] = expf(ck[q] - m) / denom;
+      } else {
+        cv[q] = sigmoid_f(l);
+        ck[q] = bias ? cv[q] + bias[e] : cv[q];
+      }
+    }
+  }
+  float sum = 0.f;
+  for (int r = 0; r < K; ++r) {
+    float bk = -FLT_MAX, bv = 0.f;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (ce[q] != 0x7fffffff && rank[q] < 0 &&
+          (bid == 0x7fffffff || ck[q] > bk || (ck[q] == bk && ce[q] < bid))) {
+        bk = ck[q];
+        bid = ce[q];
+        bv = cv[q];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
+        bk = ok;
+        bid = oid;
+        bv = ov;
+      }
+    }
+    if (bid == 0x7fffffff) {  // fewer than K recomputed rows cannot happen (n >= K)
+      record_error(err, DEV_BAD_ROUTE);
+      bid = 0;
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+      if (ce[q] == bid) rank[q] = r;
+    if (norm) sum += bv;  // rank order, like warp_topk
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    if (rank[q] >= 0) {
+      float wv = cv[q];
+      if (norm) wv = wv / (sum + 1e-20f);
+      ids[static_cast<size_t>(t) * K + rank[q]] = ce[q];
+      wts[static_cast<size_t>(t) * K + rank[q]] = wv * scale;
+    }
+  }
+  if (sgate && lane == 0) sgate[t] = sigmoid_f(xrow[n]);
 }
 
 template <int VPL>
@@ -1133,14 +1117,18 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 #define MOE_TOPK_CASE(V)                                                                        \
   do {                                                                                          \
     if (tc) {                                                                                   \
-      static bool done[64] = {};                                                                \
-      st = set_smem_attr(reinterpret_cast<const void*>(route_select_kernel<V>),                 \
-                         static_cast<int>(kSelSmemBytes), done);                                \
-      if (st != cudaSuccess) return st;                                                         \
-      route_select_kernel<V><<<min(grid, p.num_sms), 256, kSelSmemBytes, s>>>(                  \
-          logits, router_tc_splits(p, T), x, p.w.norm_w, p.w.router_w,                          \
-          reinterpret_cast<const float*>(ws + L.rms), bias, ids, wts, sg, T, E, R, p.H, K,      \
-          p.cfg.score_func, p.cfg.norm_topk_prob, p.cfg.routed_scaling_factor, p.d_err);        \
+      int32_t* cand = reinterpret_cast<int32_t*>(ws + L.cand);                                  \
+      int32_t* nrows = reinterpret_cast<int32_t*>(ws + L.ncand);                                \
+      route_cand_kernel<V><<<grid, 256, 0, s>>>(logits, router_tc_splits(p, T), bias, cand,     \
+                                                nrows, T, E, R, K, p.cfg.score_func, p.d_err);  \
+      route_exact_kernel<<<T, 256, 0, s>>>(logits, cand, nrows, x, p.w.norm_w, p.w.router_w,    \
+                                           reinterpret_cast<const float*>(ws + L.rms),          \
+                                           reinterpret_cast<float*>(ws + L.exact), T, E, R, p.H, \
+                                           p.cfg.has_shared_gate);                              \
+      route_final_kernel<V><<<grid, 256, 0, s>>>(                                               \
+          logits, cand, nrows, reinterpret_cast<const float*>(ws + L.exact), bias, ids, wts, sg, \
+          T, E, R, K, p.cfg.score_func, p.cfg.norm_topk_prob, p.cfg.routed_scaling_factor,     \
+          p.d_err);                                                                             \
     } else                                                                                      \
       topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, R, K,               \
                                           p.cfg.score_func, p.cfg.norm_topk_prob,               \

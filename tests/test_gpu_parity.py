@@ -187,7 +187,7 @@ def test_full_shape_routing(glm_full, T: int) -> None:  # noqa: ANN001
 
 @pytest.mark.parametrize("score_func", ["softmax", "sigmoid"])
 def test_prefill_router_exact_ties(score_func: str) -> None:
-    """Prefill batches route on the tensor cores and re-decide in fp32.  Twelve
+    """Prefill batches route on the tensor cores and re-decide in fp32.  Sixteen
     identical router rows with equal bias make exact ties at the top-k boundary
     and whole runs of tied candidates past it, which is where the selection
     kernel widens its recomputation; ids must follow the oracle's lower-id rule."""
@@ -196,8 +196,8 @@ def test_prefill_router_exact_ties(score_func: str) -> None:
     t = {"post_attention_layernorm.weight": (1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
          "mlp.gate.weight": (rng.standard_normal((E, H)) * 0.02).astype(np.float32),
          "mlp.gate.e_score_correction_bias": (rng.standard_normal(E) * 0.01).astype(np.float32)}
-    t["mlp.gate.weight"][1:12] = t["mlp.gate.weight"][0]
-    t["mlp.gate.e_score_correction_bias"][:12] = 0.0
+    t["mlp.gate.weight"][1:16] = t["mlp.gate.weight"][0]
+    t["mlp.gate.e_score_correction_bias"][:16] = 0.0
     for e in range(E):
         t[f"mlp.experts.{e}.gate_proj.weight"] = (rng.standard_normal((64, H)) * 0.02).astype(np.float32)
         t[f"mlp.experts.{e}.up_proj.weight"] = (rng.standard_normal((64, H)) * 0.02).astype(np.float32)
@@ -218,12 +218,12 @@ def test_prefill_router_exact_ties(score_func: str) -> None:
     h = rms_norm(x, t["post_attention_layernorm.weight"], ocfg.eps)
     ids, w, logits = route(h, t["mlp.gate.weight"], t["mlp.gate.e_score_correction_bias"], ocfg)
     got = r["topk_ids"].cpu().numpy()
-    tied = np.isin(ids, np.arange(12)).sum(axis=1)
+    tied = np.isin(ids, np.arange(16)).sum(axis=1)
     assert np.count_nonzero((tied > 0) & (tied < K)) > 10  # the tie group straddles the boundary
     for row in np.nonzero((got != ids).any(axis=1))[0]:
         srt = np.sort(logits[row])[::-1]
         gap = np.min(np.abs(np.diff(srt[: K + 1]))) / max(abs(srt[K - 1]), 1e-30)
-        assert gap < 1e-6 and not np.all(logits[row, :12] == logits[row, 0]), \
+        assert gap < 1e-6 and not np.all(logits[row, :16] == logits[row, 0]), \
             f"token {row}: {got[row]} vs {ids[row]}"
     np.testing.assert_allclose(r["topk_w"].cpu().numpy()[got == ids], w[got == ids], rtol=1e-5)
     ml.close()
