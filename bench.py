@@ -551,9 +551,10 @@ def run_ours(args) -> None:  # noqa: ANN001
                     "ms_per_step": e2e_s * 1e3},
             "cpu_baseline": cpu,
             # our kernels per forward: router, decode tail, dispatch, two grouped
-            # GEMMs, combine (T <= 256); prefill: prep, router GEMM, selection,
-            # histogram, scan, scatter, gather, two grouped GEMMs, combine
-            "gpu_launches": (6 if T_main <= 256 else 10) * args.steps,
+            # GEMMs, combine (T <= 256); prefill: prep, router GEMM, candidates,
+            # fp32 recompute, final selection, histogram, scan, scatter, gather,
+            # two grouped GEMMs, combine
+            "gpu_launches": (6 if T_main <= 256 else 12) * args.steps,
             "clocks": clocks,
             "sub": sub,
             "other_configs": other,
