@@ -12,9 +12,10 @@ launching stream, barrier + synchronize on both sides, max over ranks.  The
 touched expert weights (>= 425 MB at T=1) are larger than the 126 MB L2, so no
 flush is needed between steps.
 
-e2e: the same metric through MoeLayer.forward_host (the call behind the
-executor's ``_moe_mlp_block``) with host fp32 activations: pinned H2D of x and
-D2H of the output inside the timed region.
+e2e: the same metric through MoeLayer.host_runner (the library's serving-loop
+call over fixed pinned host buffers; the step is replayed as one CUDA graph)
+with host fp32 activations: H2D of x, the layer, D2H of the output and a
+synchronise inside every timed step.
 
 --impl reference: the CPU oracle port of the reference executor
 (offload_runtime/executors/glm4_moe.py:176-240; same numpy expressions) on the
@@ -470,20 +471,23 @@ def run_ours(args) -> None:  # noqa: ANN001
     down_gbs = ab["down"] / (stage[2] * 1e-3) / 1e9
     layer_gbs = ab["layer"] / (ms * 1e-3) / 1e9
 
-    # end-to-end through the host-buffer call: pinned input -> H2D -> forward -> D2H
-    # -> synchronise, every step
+    # end-to-end through the serving-loop call: every step copies the pinned input
+    # to the device, runs the layer, copies the result back and synchronises
+    # (MoeLayer.host_runner: the step replayed as one CUDA graph)
     x_host = main["x"].cpu().numpy()
     e2e_s = float("nan")
     if not args.no_e2e:
         x_pin = torch.from_numpy(x_host).pin_memory()
         out_pin = torch.empty_like(x_pin).pin_memory()
+        runner = ml.host_runner(x_pin, out_pin)
         for _ in range(args.warmup):
-            ml.forward_host(x_pin, out=out_pin)
+            runner()
         _barrier(world)
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            ml.forward_host(x_pin, out=out_pin)
+            runner()
         e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+        del runner
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

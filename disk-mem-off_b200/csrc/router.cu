@@ -325,14 +325,25 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
   const int C = min(E, K + kRefineMargin);
   float key[VPL];
   bool taken[VPL];
+  // all plane loads are issued before any is added (the bound is a constant)
+  float pl[kRouterMaxSplit][VPL];
+#pragma unroll
+  for (int sp = 0; sp < kRouterMaxSplit; ++sp)
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int e = j * 32 + lane;
+      pl[sp][j] = (sp < nplanes && e < E) ? lrow[sp * plane + e] : 0.f;
+    }
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int e = j * 32 + lane;
     key[j] = -FLT_MAX;
     taken[j] = false;
     if (e < E) {
-      float l = lrow[e];
-      for (int sp = 1; sp < nplanes; ++sp) l += lrow[sp * plane + e];
+      float l = pl[0][j];
+#pragma unroll
+      for (int sp = 1; sp < kRouterMaxSplit; ++sp)
+        if (sp < nplanes) l += pl[sp][j];  // split order
       if (nplanes > 1) lrow[e] = l;  // plane 0 now holds the summed logits
       key[j] = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bias[e] : l)
                                                  : (bias ? sigmoid_f(l) + bias[e] : sigmoid_f(l));

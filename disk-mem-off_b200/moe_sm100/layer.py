@@ -191,6 +191,10 @@ class MoeLayer:
         s.synchronize()
         return dst if pinned_in else dst.numpy().copy()
 
+    def host_runner(self, x_pinned: Any, out_pinned: Any) -> "HostRunner":
+        """A reusable end-to-end step over fixed pinned host buffers (see HostRunner)."""
+        return HostRunner(self, x_pinned, out_pinned)
+
     def _staging(self, tokens: int) -> tuple[Any, Any, Any, Any]:
         torch = _torch()
         cap = self._pinned.get("cap", 0)
@@ -246,3 +250,57 @@ def layer_shapes(tensor_meta: Iterable[dict[str, Any]]) -> dict[str, Any]:
         elif n.endswith("mlp.shared_expert_gate.weight"):
             gate = True
     return {"inter": inter, "shared_inter": shared, "has_shared_gate": gate}
+
+
+class HostRunner:
+    """One layer step from pinned host memory, for serving loops with fixed buffers.
+
+    The step -- copy ``x_pinned`` to the device, ``moe_forward``, copy the result
+    into ``out_pinned`` -- is captured once as a CUDA graph and replayed by each
+    call, so a step costs one graph launch on the host instead of a dozen API
+    calls.  The caller refills ``x_pinned`` before a call and reads
+    ``out_pinned`` after it; the runner owns its device buffers and workspace.
+    Capture needs one uncaptured warm-up step, which the constructor runs.
+    """
+
+    def __init__(self, layer: MoeLayer, x_pinned: Any, out_pinned: Any) -> None:
+        torch = _torch()
+        for name, tnsr in (("x_pinned", x_pinned), ("out_pinned", out_pinned)):
+            if not (isinstance(tnsr, torch.Tensor) and tnsr.device.type == "cpu"
+                    and tnsr.dtype == torch.float32 and tnsr.is_contiguous() and tnsr.is_pinned()):
+                raise ValueError(f"{name} must be a contiguous pinned fp32 CPU tensor")
+        if x_pinned.dim() != 2 or x_pinned.shape[1] != layer.cfg.hidden:
+            raise ValueError(f"x_pinned must be [T, {layer.cfg.hidden}]")
+        if out_pinned.shape != x_pinned.shape:
+            raise ValueError("out_pinned must have the shape of x_pinned")
+        t = x_pinned.shape[0]
+        if not 0 < t <= layer.cfg.max_tokens:
+            raise ValueError("T outside (0, max_tokens]")
+        dev = torch.device(f"cuda:{layer.cfg.device}")
+        self.layer, self.x, self.out = layer, x_pinned, out_pinned
+        self._din = torch.empty_like(x_pinned, device=dev)
+        self._dout = torch.empty_like(x_pinned, device=dev)
+        self._ws = torch.empty(max(layer.workspace_bytes(t), 256), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            self._step()
+        stream.synchronize()
+        layer.status(stream)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph, stream=stream):
+            self._step()
+        torch.cuda.current_stream(dev).synchronize()
+
+    def _step(self) -> None:
+        t = self.x.shape[0]
+        self._din.copy_(self.x, non_blocking=True)
+        self.layer.forward_ptr(self._din.data_ptr(), self._dout.data_ptr(), t, self._ws.data_ptr(),
+                               self._ws.numel())
+        self.out.copy_(self._dout, non_blocking=True)
+
+    def __call__(self) -> Any:
+        """Run one step and wait for it; returns ``out_pinned``."""
+        torch = _torch()
+        self._graph.replay()
+        torch.cuda.current_stream(self._din.device).synchronize()
+        return self.out

@@ -109,6 +109,14 @@ def test_host_buffers_end_to_end() -> None:
     assert ml.forward_host(x_pin, out=o_pin) is o_pin
     np.testing.assert_array_equal(o_pin.numpy(), ml.forward_host(x))
     assert rel_l2(o_pin.numpy(), gout) <= TOL_16
+    # the replayed serving-loop step: same bits, and it follows refills of x_pin
+    r_out = torch.empty_like(x_pin).pin_memory()
+    runner = ml.host_runner(x_pin, r_out)
+    np.testing.assert_array_equal(runner().numpy(), o_pin.numpy())
+    x_pin.mul_(0.5)
+    np.testing.assert_array_equal(runner().numpy(), ml.forward_host(x_pin.numpy()))
+    ml.status()
+    del runner
     ml.close()
 
 
