@@ -63,15 +63,19 @@ class ExpertParallelMoe:
         mark("start")
         send_rows, send_experts, send_offsets = self.ops.dispatch(x)
         mark("dispatched")
-        offs = send_offsets.tolist()
-        if len(offs) != dist.get_world_size(g) + 1 or offs[0] != 0 or offs[-1] != send_rows.shape[0] \
-                or any(b < a for a, b in zip(offs, offs[1:])):
-            raise ValueError(f"malformed send offsets {offs} for {send_rows.shape[0]} rows")
-        send_counts = (send_offsets[1:] - send_offsets[:-1]).to(torch.int64)
+        # counts go through the exchange on the device; the host reads the send
+        # offsets and the received counts in one synchronisation
+        world = dist.get_world_size(g)
+        send_offsets = send_offsets.to(torch.int64)
+        send_counts = send_offsets[1:] - send_offsets[:-1]
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=g)
-        sc = send_counts.tolist()
-        rc = recv_counts.tolist()
+        both = torch.cat([send_offsets, recv_counts]).tolist()
+        offs, rc = both[:world + 1], both[world + 1:]
+        if len(offs) != world + 1 or offs[0] != 0 or offs[-1] != send_rows.shape[0] \
+                or any(b < a for a, b in zip(offs, offs[1:])):
+            raise ValueError(f"malformed send offsets {offs} for {send_rows.shape[0]} rows")
+        sc = [b - a for a, b in zip(offs, offs[1:])]
         n_recv = int(sum(rc))
         h = send_rows.shape[1]
         recv_rows = send_rows.new_empty((n_recv, h))
