@@ -6,7 +6,10 @@ own tokens.  One forward (weak scaling: T tokens per rank):
 
   1. dispatch   route the local tokens; normalised f16 rows grouped by owner rank
   2. counts     all_to_all of the per-rank row counts (the only host sync)
-  3. exchange   all_to_all of the rows and of their local expert ids
+  3. exchange   all_to_all of the rows and of their local expert ids; meanwhile
+                the shared expert runs on a side stream when the ops provide it
+                (``start_shared``).  (One batched group of point-to-point
+                transfers for both was measured slower than two all_to_alls.)
   4. experts    grouped GEMMs of the resident experts on the received rows
   5. return     all_to_all of the f16 expert outputs back to their source rank
   6. combine    x + sum_k w * y + shared expert
@@ -77,10 +80,13 @@ class ExpertParallelMoe:
             raise ValueError(f"malformed send offsets {offs} for {send_rows.shape[0]} rows")
         sc = [b - a for a, b in zip(offs, offs[1:])]
         n_recv = int(sum(rc))
+        start_shared = getattr(self.ops, "start_shared", None)
+        if start_shared is not None:
+            start_shared(x)
         h = send_rows.shape[1]
         recv_rows = send_rows.new_empty((n_recv, h))
-        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=g)
         recv_experts = send_experts.new_empty((n_recv,))
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=g)
         dist.all_to_all_single(recv_experts, send_experts, rc, sc, group=g)
         mark("exchanged")
         y = self.ops.experts(recv_rows, recv_experts)
@@ -117,6 +123,7 @@ class DeviceEPOps:
         self._ws = None
         self._ws_ep = None
         self._T = 0
+        self._shared_done: Any = None  # event of a shared-expert pass started early
 
     def bind_device(self, blob_ptr: int, blob_bytes: int, tensor_meta: list[dict[str, Any]],
                     stream: Any = None) -> None:
@@ -159,6 +166,23 @@ class DeviceEPOps:
                                    c_void_p(_stream_handle(None))))
         return y
 
+    def start_shared(self, x: Any) -> None:
+        """Run the shared expert of the dispatched tokens on a side stream, so that
+        it overlaps the row exchange; combine waits for it."""
+        torch = _torch()
+        t = x.shape[0]
+        if t == 0 or self.cfg.shared_inter == 0:
+            return
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=x.device)
+        main = torch.cuda.current_stream(x.device)
+        self._side.wait_stream(main)  # after dispatch (its workspace holds the rows)
+        ws = self._ws
+        check(lib().moe_ep_shared(self.layer._plan, t, c_void_p(ws.data_ptr()), ws.numel(),
+                                  c_void_p(self._side.cuda_stream)))
+        self._shared_done = torch.cuda.Event()
+        self._shared_done.record(self._side)
+
     def combine(self, x: Any, y_back: Any) -> Any:
         torch = _torch()
         out = torch.empty_like(x)
@@ -168,7 +192,11 @@ class DeviceEPOps:
         plan = self.layer._plan
         ws = self._ws
         s = c_void_p(_stream_handle(None))
-        check(lib().moe_ep_shared(plan, t, c_void_p(ws.data_ptr()), ws.numel(), s))
+        if self._shared_done is not None:
+            torch.cuda.current_stream(x.device).wait_event(self._shared_done)
+            self._shared_done = None
+        else:
+            check(lib().moe_ep_shared(plan, t, c_void_p(ws.data_ptr()), ws.numel(), s))
         check(lib().moe_ep_combine(plan, c_void_p(x.data_ptr()), t, c_void_p(y_back.data_ptr()),
                                    c_void_p(out.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(), s))
         return out
