@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const float* __restrict__ x, const YT* __restrict__ y, const float* __restrict__ y_s,
     const int32_t* __restrict__ slot_row, const float* __restrict__ wts,
     const float* __restrict__ sgate, float* __restrict__ out, int K, int H) {
+  pdl_enter();
   const int t = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
   if (v >= (H >> 2)) return;
@@ -67,7 +68,7 @@ cudaError_t launch_combine_half(const Plan& p, const float* x, const __half* y, 
                                 float* out, int T, cudaStream_t s) {
   const int nv = p.H >> 2;
   dim3 grid((nv + 255) / 256, T);
-  combine_kernel<__half><<<grid, 256, 0, s>>>(x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
+  MOE_PDL(combine_kernel<__half>, dim3(grid), dim3(256), 0, s, x, y, p.SI > 0 ? y_s : nullptr, slot_row, wts,
                                               p.cfg.has_shared_gate ? sgate : nullptr, out, p.K,
                                               p.H);
   return cudaGetLastError();
@@ -79,6 +80,7 @@ __global__ void ep_meta_kernel(const int32_t* __restrict__ perm, const int32_t* 
                                const int32_t* __restrict__ offsets, int n, int e_loc, int world,
                                int E, int32_t* __restrict__ send_experts,
                                int32_t* __restrict__ send_offsets) {
+  pdl_enter();
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x)
     send_experts[r] = ids[perm[r]] % e_loc;
   if (blockIdx.x == 0)
@@ -89,7 +91,7 @@ cudaError_t launch_ep_meta(const Plan& p, const int32_t* perm, const int32_t* id
                            const int32_t* offsets, int n, int32_t* send_experts,
                            int32_t* send_offsets, cudaStream_t s) {
   const int world = p.E / p.n_local;
-  ep_meta_kernel<<<max(1, min((n + 255) / 256, p.num_sms * 4)), 256, 0, s>>>(
+  MOE_PDL(ep_meta_kernel, dim3(max(1, min((n + 255) / 256, p.num_sms * 4))), dim3(256), 0, s, 
       perm, ids, offsets, n, p.n_local, world, p.E, send_experts, send_offsets);
   return cudaGetLastError();
 }

@@ -40,6 +40,20 @@ MOE_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- launch chaining
+// Every forward kernel is launched with programmatic stream serialisation, so
+// its launch and on-chip prologue overlap the tail of the kernel before it.
+// pdl_release lets the next kernel of the stream start launching; pdl_wait
+// blocks until the previous kernel has completed and its writes are visible.
+// Kernels call both before their first global-memory access (a no-op when the
+// launch did not ask for chaining).
+MOE_DEV void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+MOE_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MOE_DEV void pdl_enter() {
+  pdl_release();
+  pdl_wait();
+}
+
 // ---------------------------------------------------------------- mbarrier
 MOE_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

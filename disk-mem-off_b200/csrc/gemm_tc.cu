@@ -218,12 +218,11 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_release();
   // Grouped GEMMs read their unit count and K split from the tile map the
-  // routing kernels wrote; the router GEMM's units are a plain (m, n, K split)
-  // grid derived from the index.
-  const int map_tot = args.router_grid ? 0 : __ldg(args.map.info);
-  const int map_splits = args.router_grid ? 1 : __ldg(args.map.info + 1);
-  const int ntiles = args.router_grid ? args.max_tiles : min(__ldg(args.map.info + 2), args.max_tiles);
+  // routing kernels wrote (after pdl_wait below); the router GEMM's units are a
+  // plain (m, n, K split) grid derived from the index.
+  int map_tot = 0, map_splits = 1, ntiles = 0;
   auto fetch_tile = [&](int ti) {
     if (!args.router_grid) return tile_at(args.map, ti, map_tot, map_splits);
     Tile t;
@@ -266,6 +265,11 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the prologue above touches only on-chip state; global memory after this
+  pdl_wait();
+  map_tot = args.router_grid ? 0 : __ldg(args.map.info);
+  map_splits = args.router_grid ? 1 : __ldg(args.map.info + 1);
+  ntiles = args.router_grid ? args.max_tiles : min(__ldg(args.map.info + 2), args.max_tiles);
 
   auto tile_ok = [&](const Tile& t) {
     if (t.group < 0 || t.group > args.n_local || t.nvalid <= 0 || t.nvalid > BN) return false;
@@ -546,8 +550,8 @@ static cudaError_t run_gemm(const GemmArgs& a, int grid, cudaStream_t s) {
     if (st != cudaSuccess) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  moe_gemm_kernel<BN, MODE, INT8><<<grid, gemm_threads<BN, INT8>(), smem, s>>>(a);
-  return cudaGetLastError();
+  return pdl_launch(moe_gemm_kernel<BN, MODE, INT8>, dim3(grid), dim3(gemm_threads<BN, INT8>()),
+                    smem, s, a);
 }
 
 template <bool DOWN, bool INT8>

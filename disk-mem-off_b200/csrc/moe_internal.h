@@ -7,10 +7,37 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/moe_sm100.h"
 
 namespace moe {
+
+// Launches a forward kernel chained to the previous kernel of the stream
+// (programmatic stream serialisation; the kernel calls pdl_enter / pdl_wait
+// before it touches global memory).
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Statement form of pdl_launch for launchers that return cudaError_t.
+#define MOE_PDL(...)                                  \
+  do {                                                \
+    const cudaError_t pdl_st_ = pdl_launch(__VA_ARGS__); \
+    if (pdl_st_ != cudaSuccess) return pdl_st_;       \
+  } while (0)
 
 constexpr int kBM = 128;          // GEMM tile rows (weight rows, swap-AB)
 constexpr int kBK = 64;           // GEMM k-block (one 128-byte swizzle atom of f16)

@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(256) router_kernel(
     float* __restrict__ part, float* __restrict__ ss_part, float* __restrict__ logits,
     float* __restrict__ rms_out, int* __restrict__ counters, int T, int H, int R, int S,
     int k_per_split, float eps) {
+  pdl_enter();
   constexpr int EPT = (BT == 64) ? 4 : 2;     // router rows per thread
   constexpr int XT = kRouterRows / EPT;       // threads along rows
   constexpr int YT = 256 / XT;                // threads along tokens
@@ -317,6 +318,7 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
     float* __restrict__ logits, int nplanes, const float* __restrict__ bias,
     int32_t* __restrict__ cand, int32_t* __restrict__ nrows, int T, int E, int R, int K,
     int score_func, int* err) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -406,6 +408,7 @@ __global__ void __launch_bounds__(256) route_exact_kernel(
     const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ wr,
     const float* __restrict__ rms, float* __restrict__ exact, int T, int E, int R, int H,
     int has_gate) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = nrows[t];
@@ -486,6 +489,7 @@ __global__ void __launch_bounds__(256) route_final_kernel(
     const float* __restrict__ bias, int32_t* __restrict__ ids, float* __restrict__ wts,
     float* __restrict__ sgate, int T, int E, int R, int K, int score_func, int norm, float scale,
     int* err) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -614,6 +618,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
                                                    float* __restrict__ sgate, int T, int E, int R,
                                                    int K, int score_func, int norm, float scale,
                                                    int* err) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -750,6 +755,7 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
     int score_func, int norm, float scale, int32_t* __restrict__ ids, float* __restrict__ wts,
     float* __restrict__ sgate, int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
     int32_t* __restrict__ slot_row, TileArgs ta) {
+  pdl_enter();
   extern __shared__ int tsm[];
   const int words = (T + 31) >> 5;
   int* s_ids = tsm;                                              // [T*K]
@@ -801,6 +807,7 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
 __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restrict__ ids, int T,
                                                          int K, int E, uint32_t* __restrict__ bmg,
                                                          int32_t* __restrict__ hist, int* err) {
+  pdl_enter();
   extern __shared__ uint32_t bm[];  // [E][32]
   const int c = blockIdx.x;
   const int tbeg = c * kPermChunk;
@@ -831,6 +838,7 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
                                                          int nchunks, int32_t* __restrict__ base,
                                                          int32_t* __restrict__ offsets,
                                                          TileArgs ta) {
+  pdl_enter();
   const int e = threadIdx.x, E = ta.E;
   int tot = 0;
   if (e < E) {
@@ -855,6 +863,7 @@ __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __rest
                                                            int T, int K, int E,
                                                            int32_t* __restrict__ perm,
                                                            int32_t* __restrict__ slot_row) {
+  pdl_enter();
   for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < T * K; q += gridDim.x * blockDim.x) {
     const int t = q / K;
     const int e = ids[q];
@@ -873,6 +882,7 @@ __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __rest
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ src,
                                                           const int32_t* __restrict__ perm, int n,
                                                           int H, int div, __half* __restrict__ dst) {
+  pdl_enter();
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
     const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r] / div) * H);
     uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * H);
@@ -888,6 +898,7 @@ __global__ void __launch_bounds__(256) router_prep_kernel(const float* __restric
                                                           const float* __restrict__ wn, int H,
                                                           float eps, float* __restrict__ rms_out,
                                                           __half* __restrict__ h16, int* err) {
+  pdl_enter();
   const int t = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
   const float4* wr = reinterpret_cast<const float4*>(wn);
@@ -965,6 +976,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__
                                                        int K, int H, int with_shared,
                                                        __half* __restrict__ xg,
                                                        __half* __restrict__ h16) {
+  pdl_enter();
   const int rows = T * K + (with_shared ? T : 0);
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     int t;
@@ -1038,7 +1050,7 @@ static cudaError_t run_router(const Plan& p, const WsLayout& L, char* ws, const 
     if (a != cudaSuccess) return a;
   }
   dim3 grid(g.rx, g.splits, g.tz);
-  router_kernel<BT><<<grid, 256, smem, s>>>(
+  MOE_PDL(router_kernel<BT>, dim3(grid), dim3(256), smem, s, 
       x, p.w.norm_w, p.w.router_w, reinterpret_cast<float*>(ws + L.part),
       reinterpret_cast<float*>(ws + L.ss_part), reinterpret_cast<float*>(ws + L.logits),
       reinterpret_cast<float*>(ws + L.rms), counters, T, p.H, p.router_rows, g.splits,
@@ -1081,7 +1093,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
   const bool tc = route_uses_tc_router(p, T);
   cudaError_t st;
   if (tc) {
-    router_prep_kernel<<<T, 256, 0, s>>>(x, p.w.norm_w, p.H, p.cfg.rms_norm_eps,
+    MOE_PDL(router_prep_kernel, dim3(T), dim3(256), 0, s, x, p.w.norm_w, p.H, p.cfg.rms_norm_eps,
                                          reinterpret_cast<float*>(ws + L.rms),
                                          reinterpret_cast<__half*>(ws + L.h16), p.d_err);
     st = cudaGetLastError();
@@ -1111,7 +1123,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
     static bool done[64] = {};                                                                  \
     st = set_smem_attr(reinterpret_cast<const void*>(route_tail_kernel<V>), 160 * 1024, done);  \
     if (st != cudaSuccess) return st;                                                           \
-    route_tail_kernel<V><<<1, 1024, smem, s>>>(logits, bias, T, E, R, K, p.cfg.score_func,      \
+    MOE_PDL(route_tail_kernel<V>, dim3(1), dim3(1024), smem, s, logits, bias, T, E, R, K, p.cfg.score_func,      \
                                                p.cfg.norm_topk_prob,                            \
                                                p.cfg.routed_scaling_factor, ids, wts, sg,       \
                                                offsets, perm, slot_row, ta);                    \
@@ -1130,18 +1142,18 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
     if (tc) {                                                                                   \
       int32_t* cand = reinterpret_cast<int32_t*>(ws + L.cand);                                  \
       int32_t* nrows = reinterpret_cast<int32_t*>(ws + L.ncand);                                \
-      route_cand_kernel<V><<<grid, 256, 0, s>>>(logits, router_tc_splits(p, T), bias, cand,     \
+      MOE_PDL(route_cand_kernel<V>, dim3(grid), dim3(256), 0, s, logits, router_tc_splits(p, T), bias, cand,     \
                                                 nrows, T, E, R, K, p.cfg.score_func, p.d_err);  \
-      route_exact_kernel<<<T, 256, 0, s>>>(logits, cand, nrows, x, p.w.norm_w, p.w.router_w,    \
+      MOE_PDL(route_exact_kernel, dim3(T), dim3(256), 0, s, logits, cand, nrows, x, p.w.norm_w, p.w.router_w,    \
                                            reinterpret_cast<const float*>(ws + L.rms),          \
                                            reinterpret_cast<float*>(ws + L.exact), T, E, R, p.H, \
                                            p.cfg.has_shared_gate);                              \
-      route_final_kernel<V><<<grid, 256, 0, s>>>(                                               \
+      MOE_PDL(route_final_kernel<V>, dim3(grid), dim3(256), 0, s,                                                \
           logits, cand, nrows, reinterpret_cast<const float*>(ws + L.exact), bias, ids, wts, sg, \
           T, E, R, K, p.cfg.score_func, p.cfg.norm_topk_prob, p.cfg.routed_scaling_factor,     \
           p.d_err);                                                                             \
     } else                                                                                      \
-      topk_kernel<V><<<grid, 256, 0, s>>>(logits, bias, ids, wts, sg, T, E, R, K,               \
+      MOE_PDL(topk_kernel<V>, dim3(grid), dim3(256), 0, s, logits, bias, ids, wts, sg, T, E, R, K,               \
                                           p.cfg.score_func, p.cfg.norm_topk_prob,               \
                                           p.cfg.routed_scaling_factor, p.d_err);                \
   } while (0)
@@ -1161,27 +1173,27 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
     st = set_smem_attr(reinterpret_cast<const void*>(perm_hist_kernel), 1024 * 32 * sizeof(uint32_t),
                        done_hist);
     if (st != cudaSuccess) return st;
-    perm_hist_kernel<<<L.nchunks, 1024, static_cast<size_t>(E) * 32 * sizeof(uint32_t), s>>>(
+    MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
         ids, T, K, E, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    perm_scan_kernel<<<1, 1024, 0, s>>>(hist, L.nchunks, base, offsets, ta);
+    MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, hist, L.nchunks, base, offsets, ta);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     const int entries = T * K;
-    perm_scatter_kernel<<<min((entries + 255) / 256, p.num_sms * 8), 256, 0, s>>>(
+    MOE_PDL(perm_scatter_kernel, dim3(min((entries + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, 
         ids, bmg, base, T, K, E, perm, slot_row);
   }
   st = cudaGetLastError();
   if (st != cudaSuccess || !dispatch) return st;
   if (tc) {  // h16 already holds the normalised rows: gather them per slot
-    gather_rows_kernel<<<min(T * K, p.num_sms * 16), 256, 0, s>>>(
+    MOE_PDL(gather_rows_kernel, dim3(min(T * K, p.num_sms * 16)), dim3(256), 0, s, 
         reinterpret_cast<const __half*>(ws + L.h16), perm, T * K, p.H, K,
         xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg));
     return cudaGetLastError();
   }
   const int rows = T * K + (p.SI > 0 ? T : 0);
-  dispatch_kernel<<<min(rows, p.num_sms * 8), 256, 0, s>>>(
+  MOE_PDL(dispatch_kernel, dim3(min(rows, p.num_sms * 8)), dim3(256), 0, s, 
       x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms), perm, T, K, p.H, p.SI > 0,
       xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
   return cudaGetLastError();
@@ -1203,26 +1215,26 @@ cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const 
                                  1024 * 32 * sizeof(uint32_t), done_hist);
   if (st != cudaSuccess) return st;
   if (n > 0) {
-    perm_hist_kernel<<<L.nchunks, 1024, static_cast<size_t>(E) * 32 * sizeof(uint32_t), s>>>(
+    MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
         keys, n, 1, E, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
   }
-  perm_scan_kernel<<<1, 1024, 0, s>>>(hist, L.nchunks, base, offsets, ta);
+  MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, hist, L.nchunks, base, offsets, ta);
   st = cudaGetLastError();
   if (st != cudaSuccess || n == 0) return st;
-  perm_scatter_kernel<<<min((n + 255) / 256, p.num_sms * 8), 256, 0, s>>>(keys, bmg, base, n, 1, E,
+  MOE_PDL(perm_scatter_kernel, dim3(min((n + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, keys, bmg, base, n, 1, E,
                                                                          perm, slot_row);
   st = cudaGetLastError();
   if (st != cudaSuccess) return st;
-  gather_rows_kernel<<<min(n, p.num_sms * 8), 256, 0, s>>>(rows, perm, n, p.H, 1,
+  MOE_PDL(gather_rows_kernel, dim3(min(n, p.num_sms * 8)), dim3(256), 0, s, rows, perm, n, p.H, 1,
                                                           reinterpret_cast<__half*>(ws + L.xg));
   return cudaGetLastError();
 }
 
 cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s) {
   const TileArgs ta = tile_args(p, L, ws, T, 0, true);
-  perm_scan_kernel<<<1, 1024, 0, s>>>(nullptr, 0, nullptr, reinterpret_cast<int32_t*>(ws + L.offsets),
+  MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, nullptr, 0, nullptr, reinterpret_cast<int32_t*>(ws + L.offsets),
                                       ta);
   return cudaGetLastError();
 }
