@@ -218,7 +218,6 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_release();
   // Grouped GEMMs read their unit count and K split from the tile map the
   // routing kernels wrote (after pdl_wait below); the router GEMM's units are a
   // plain (m, n, K split) grid derived from the index.
@@ -528,6 +527,10 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     }
   }
 
+  // the next kernel may launch now (released after the tile loop rather than at
+  // entry, so that its waiting CTAs never sit beside this kernel's tiles; the two
+  // placements measured the same)
+  pdl_release();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
