@@ -132,6 +132,8 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
     L.cand = take(prefill ? static_cast<size_t>(T) * kCandMax * 4 : 0);
     L.ncand = take(prefill ? static_cast<size_t>(T) * 4 : 0);
     L.exact = take(prefill ? static_cast<size_t>(T) * (kCandMax + 1) * 4 : 0);
+  } else if (p.E == 0) {
+    L.rms = take(static_cast<size_t>(T) * 4);  // dense MLP: per-token rms of the prologue
   }
   L.bm = take(static_cast<size_t>(L.nchunks) * E * 32 * 4);
   L.hist = take(static_cast<size_t>(L.nchunks) * E * 4);
@@ -152,6 +154,8 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
 }
 
 WsLayout ws_layout(const Plan& p, int T) {
+  if (p.E == 0)  // dense MLP: normalised rows and the shared-expert GEMMs only
+    return ws_layout_general(p, T, 0, 0, T, pick_bn(T), false);
   return ws_layout_general(p, T, p.K, p.E, p.SI > 0 ? T : 0, pick_bn(T), true);
 }
 
@@ -163,7 +167,7 @@ WsLayout ws_layout_ep_experts(const Plan& p, int R) {
 }
 
 // ------------------------------------------------------------ name parsing
-enum Kind { K_NONE, K_NORM, K_ROUTER, K_BIAS, K_SHARED_GATE, K_EXPERT, K_SHARED };
+enum Kind { K_NONE, K_NORM, K_ROUTER, K_BIAS, K_SHARED_GATE, K_EXPERT, K_SHARED, K_DENSE };
 enum Proj { P_GATE = 0, P_UP = 1, P_DOWN = 2 };
 
 struct Parsed {
@@ -208,6 +212,7 @@ static Parsed parse_name(const char* cname) {
   if (s == "mlp.gate.weight") p.kind = K_ROUTER;
   else if (s == "mlp.gate.e_score_correction_bias") p.kind = K_BIAS;
   else if (s == "mlp.shared_expert_gate.weight") p.kind = K_SHARED_GATE;
+  else if (parse_proj(s.substr(4), &p)) p.kind = K_DENSE;  // mlp.{gate,up,down}_proj (dense layers)
   else if (starts_with(s, "mlp.shared_experts.") || starts_with(s, "mlp.shared_expert.")) {
     const std::string rest = s.substr(s.find('.', 4) + 1);
     if (parse_proj(rest, &p)) p.kind = K_SHARED;
@@ -256,13 +261,23 @@ int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan) {
   const MoeConfig& c = *cfg;
   if (c.hidden <= 0 || c.hidden % 16 != 0)
     return fail(MOE_ERR_UNSUPPORTED, "hidden must be a positive multiple of 16");
-  if (c.inter <= 0 || c.inter % 16 != 0)
+  // n_experts == 0: the dense MLP of a first_k_dense_replace layer
+  // (glm4_moe.py:166-172), computed as a shared expert of shared_inter columns
+  const bool dense = c.n_experts == 0;
+  if (dense) {
+    if (c.top_k != 0 || c.use_bias || c.has_shared_gate || c.expert_begin || c.expert_end)
+      return fail(MOE_ERR_INVALID,
+                  "a dense MLP plan (n_experts = 0) takes top_k = 0, no bias, gate or expert range");
+    if (c.shared_inter <= 0)
+      return fail(MOE_ERR_INVALID, "a dense MLP plan needs shared_inter = intermediate_size");
+  }
+  if (c.inter < 0 || c.inter % 16 != 0 || (!dense && c.inter == 0))
     return fail(MOE_ERR_UNSUPPORTED, "moe_intermediate_size must be a positive multiple of 16");
   if (c.shared_inter < 0 || c.shared_inter % 16 != 0)
     return fail(MOE_ERR_UNSUPPORTED, "shared intermediate size must be a multiple of 16");
-  if (c.n_experts <= 0 || c.n_experts > 1024)
-    return fail(MOE_ERR_UNSUPPORTED, "n_experts must be in [1, 1024]");
-  if (c.top_k <= 0 || c.top_k > kMaxTopK || c.top_k > c.n_experts)
+  if (c.n_experts < 0 || c.n_experts > 1024)
+    return fail(MOE_ERR_UNSUPPORTED, "n_experts must be in [0, 1024]");
+  if (!dense && (c.top_k <= 0 || c.top_k > kMaxTopK || c.top_k > c.n_experts))
     return fail(MOE_ERR_INVALID, "top_k must be in [1, min(32, n_experts)]");
   if (c.score_func != MOE_SCORE_SOFTMAX && c.score_func != MOE_SCORE_SIGMOID)
     return fail(MOE_ERR_INVALID, "unknown score_func");
@@ -273,8 +288,8 @@ int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan) {
     return fail(MOE_ERR_INVALID, "shared gate requires a shared expert");
   int eb = c.expert_begin, ee = c.expert_end;
   if (eb == 0 && ee == 0) ee = c.n_experts;
-  if (eb < 0 || ee > c.n_experts || eb >= ee) return fail(MOE_ERR_INVALID, "bad expert range");
-  if (c.n_experts % (ee - eb) != 0 || eb % (ee - eb) != 0)
+  if (!dense && (eb < 0 || ee > c.n_experts || eb >= ee)) return fail(MOE_ERR_INVALID, "bad expert range");
+  if (!dense && (c.n_experts % (ee - eb) != 0 || eb % (ee - eb) != 0))
     return fail(MOE_ERR_INVALID,
                 "expert share must be one of n_experts / share equal contiguous ranges");
 
@@ -289,7 +304,7 @@ int moe_plan_create(const MoeConfig* cfg, MoePlan** out_plan) {
   p.E = c.n_experts;
   p.K = c.top_k;
   p.H = c.hidden;
-  p.I = c.inter;
+  p.I = c.inter > 0 ? c.inter : c.shared_inter;  // a dense plan has no routed I
   p.SI = c.shared_inter;
   p.e_begin = eb;
   p.e_end = ee;
@@ -385,7 +400,11 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
         }
         break;
       }
+      case K_DENSE:
       case K_SHARED: {
+        // a dense MLP plan packs mlp.*_proj into the shared-expert slots; a MoE
+        // plan packs the shared expert and ignores dense-layer names
+        if ((pn.kind == K_DENSE) != (E == 0)) break;
         const int64_t rows = pn.proj == P_DOWN ? H : SI, cols = pn.proj == P_DOWN ? SI : H;
         if (SI == 0) break;
         if (pn.scale) {
@@ -402,7 +421,7 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
     }
   }
   if (!norm.ptr) return fail(MOE_ERR_MISSING_TENSOR, "post_attention_layernorm.weight");
-  if (!router.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.gate.weight");
+  if (E > 0 && !router.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.gate.weight");
   if (p.cfg.has_shared_gate && !sgate.ptr) return fail(MOE_ERR_MISSING_TENSOR, "mlp.shared_expert_gate.weight");
   static const char* pname[3] = {"gate_proj", "up_proj", "down_proj"};
   for (int le = 0; le < NL; ++le)
@@ -415,7 +434,9 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
         return fail(MOE_ERR_UNSUPPORTED, "int8 expert weights need weight_format = MOE_WEIGHTS_INT8_PC");
     }
   for (int j = 0; j < 3 && SI > 0; ++j) {
-    if (!sh[j].ptr) return fail(MOE_ERR_MISSING_TENSOR, std::string("shared expert ") + pname[j]);
+    if (!sh[j].ptr)
+      return fail(MOE_ERR_MISSING_TENSOR, E == 0 ? std::string("mlp.") + pname[j] + ".weight"
+                                                 : std::string("shared expert ") + pname[j]);
     if (sh[j].dtype == SRC_I8 && !shs[j].ptr) return fail(MOE_ERR_MISSING_TENSOR, std::string("shared expert scale ") + pname[j]);
     if (sh[j].dtype == SRC_I8 && !p.int8)
       return fail(MOE_ERR_UNSUPPORTED, "int8 shared weights need weight_format = MOE_WEIGHTS_INT8_PC");
@@ -461,11 +482,12 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
 
   // ---- pack
   MOE_CUDA(launch_to_f32(norm.ptr, norm.dtype, p.w.norm_w, H, s));
-  MOE_CUDA(launch_to_f32(router.ptr, router.dtype, p.w.router_w, static_cast<int64_t>(E) * H, s));
+  if (E > 0) MOE_CUDA(launch_to_f32(router.ptr, router.dtype, p.w.router_w, static_cast<int64_t>(E) * H, s));
   if (sgate.ptr)
     MOE_CUDA(launch_to_f32(sgate.ptr, sgate.dtype, p.w.router_w + static_cast<size_t>(E) * H, H, s));
   if (p.w.bias) MOE_CUDA(launch_to_f32(bias.ptr, bias.dtype, p.w.bias, E, s));
-  MOE_CUDA(launch_scale_router_weights(p.w.router_w, p.w.rw16, p.router_rows, H, rw16_err, s));
+  if (p.router_rows > 0)
+    MOE_CUDA(launch_scale_router_weights(p.w.router_w, p.w.rw16, p.router_rows, H, rw16_err, s));
   for (int le = 0; le < NL; ++le) {
     const Src& g = ex[le * 3 + P_GATE];
     const Src& u = ex[le * 3 + P_UP];
@@ -563,6 +585,11 @@ static int check_call(const MoePlan* plan, int32_t T, const void* ws, uint64_t w
 
 static int route_impl(Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                       bool dispatch, cudaStream_t s) {
+  if (p.E == 0) {  // dense MLP: normalised f16 rows, then the shared-expert tile map
+    MOE_CUDA(launch_row_prep(p, L, ws, x, T, s));
+    MOE_CUDA(launch_shared_tiles(p, L, ws, T, s));
+    return MOE_OK;
+  }
   MOE_CUDA(launch_route(p, L, ws, x, T, dispatch, s));
   return MOE_OK;
 }
@@ -642,6 +669,7 @@ int moe_route(MoePlan* plan, const float* x_dev, int32_t T, int32_t* topk_ids, f
   if (!x_dev) return fail(MOE_ERR_INVALID, "null x");
   if (misaligned16(x_dev)) return fail(MOE_ERR_INVALID, "x must be 16-byte aligned");
   Plan& p = plan->p;
+  if (p.E == 0) return fail(MOE_ERR_UNSUPPORTED, "a dense MLP plan has no routing");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const WsLayout L = ws_layout(p, T);
   char* ws = static_cast<char*>(workspace);
@@ -675,6 +703,7 @@ int moe_status(MoePlan* plan, void* stream) {
 static int check_ep(const MoePlan* plan, int32_t n, const void* ws, uint64_t ws_bytes,
                     uint64_t need) {
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  if (plan->p.E == 0) return fail(MOE_ERR_UNSUPPORTED, "a dense MLP plan has no experts to exchange");
   if (!plan->p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
   if (n < 0) return fail(MOE_ERR_INVALID, "negative row count");
   if (n == 0) return MOE_OK;

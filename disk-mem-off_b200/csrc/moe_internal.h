@@ -160,6 +160,8 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
                               const __half* rows, int n, cudaStream_t s);
 cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
+cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                            cudaStream_t s);
 cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
 bool route_uses_tc_router(const Plan& p, int T);
 int router_tc_splits(const Plan& p, int T);

@@ -69,6 +69,8 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
   Plan& p = plan->p;
   if (!p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
+  if (p.E == 0)
+    return fail(MOE_ERR_UNSUPPORTED, "a dense MLP plan runs through moe_forward");
   if (p.n_local != p.E)
     return fail(MOE_ERR_UNSUPPORTED,
                 "this plan holds a share of the experts: use the moe_ep_* entry points");

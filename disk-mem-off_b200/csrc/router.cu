@@ -955,6 +955,14 @@ __global__ void __launch_bounds__(256) scale_router_kernel(const float* __restri
   if (bad) atomicExch(err, 1);
 }
 
+// Dense MLP prologue: rms and the normalised f16 rows (h16) of T tokens.
+cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                            cudaStream_t s) {
+  MOE_PDL(router_prep_kernel, dim3(T), dim3(256), 0, s, x, p.w.norm_w, p.H, p.cfg.rms_norm_eps,
+          reinterpret_cast<float*>(ws + L.rms), reinterpret_cast<__half*>(ws + L.h16), p.d_err);
+  return cudaSuccess;
+}
+
 cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, int H, int* err,
                                         cudaStream_t s) {
   scale_router_kernel<<<rows, 256, 0, s>>>(w, rw16, H, err);

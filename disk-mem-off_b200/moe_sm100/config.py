@@ -67,6 +67,18 @@ class MoeLayerConfig:
         return cls(**kw)
 
     @classmethod
+    def dense_mlp(cls, config: dict[str, Any], **overrides: Any) -> "MoeLayerConfig":
+        """The dense MLP of GLM-4 first_k_dense_replace layers (glm4_moe.py:166-172):
+        a plan with no routed experts whose mlp.{gate,up,down}_proj run as the
+        shared-expert GEMMs (``intermediate_size`` columns)."""
+        kw = dict(hidden=config["hidden_size"], n_experts=0, top_k=0, inter=0,
+                  shared_inter=config["intermediate_size"], use_bias=False,
+                  has_shared_gate=False, routed_scaling_factor=1.0,
+                  rms_norm_eps=config.get("rms_norm_eps", 1e-5))
+        kw.update(overrides)
+        return cls(**kw)
+
+    @classmethod
     def qwen3_next(cls, config: dict[str, Any], **overrides: Any) -> "MoeLayerConfig":
         """qwen3_next.py:105-133 defaults (softmax top-k, no bias, no scale)."""
         inter = config.get("moe_intermediate_size", 512)

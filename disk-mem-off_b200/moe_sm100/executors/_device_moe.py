@@ -11,9 +11,12 @@ Drop-in for the reference executors' MoE block:
   straight from the device blob; only the non-MoE tensors (attention, input
   norm) are read back to the host for the attention delegate, instead of the
   whole blob (_common.py:20-33).
-* Attention and the dense MLP of ``first_k_dense_replace`` layers are not part
-  of this library: pass ``attention=`` / ``dense_mlp=`` callables (for example
-  the reference executor's own methods, see ``reference_delegates``).
+* ``_dense_mlp_block(x, t)`` (glm4_moe.py:166) runs the dense MLP of
+  ``first_k_dense_replace`` layers on the device too (a plan with no routed
+  experts); ``run_layer`` uses it for non-MoE layers unless a ``dense_mlp=``
+  callable is given.
+* Attention is not part of this library: pass an ``attention=`` callable (for
+  example the reference executor's own method, see ``reference_delegates``).
 """
 from __future__ import annotations
 
@@ -71,27 +74,41 @@ class DeviceMoeExecutor:
         return True
 
     # -- binding ---------------------------------------------------------------------
+    def _dense_config(self, tensor_meta: list[dict[str, Any]]) -> MoeLayerConfig:
+        inter = next((int(m["shape"][0]) for m in tensor_meta
+                      if str(m["name"]).endswith("mlp.gate_proj.weight")), 0)
+        if inter <= 0:
+            raise KeyError("mlp.gate_proj.weight")
+        c = self.moe_config
+        return MoeLayerConfig.dense_mlp({"hidden_size": c.hidden, "intermediate_size": inter},
+                                        rms_norm_eps=c.rms_norm_eps,
+                                        weight_format=c.weight_format, max_tokens=c.max_tokens,
+                                        device=c.device)
+
     def _layer_config(self, tensor_meta: list[dict[str, Any]]) -> MoeLayerConfig:
         shp = layer_shapes(tensor_meta)
         return self.moe_config.with_shapes(shp["inter"] or self.moe_config.inter,
                                            shp["shared_inter"], shp["has_shared_gate"])
 
     def bind_device_blob(self, key: Any, blob_ptr: int, blob_bytes: int,
-                         tensor_meta: list[dict[str, Any]], stream: Any = None) -> MoeLayer:
-        """Pack the MoE tensors of a device-resident layer blob (cached under ``key``)."""
+                         tensor_meta: list[dict[str, Any]], stream: Any = None,
+                         dense: bool = False) -> MoeLayer:
+        """Pack the MoE (or, with ``dense``, the dense-MLP) tensors of a
+        device-resident layer blob (cached under ``key``)."""
         if self.resident and key in self._bound:
             return self._bound[key]
-        ml = MoeLayer(self._layer_config(tensor_meta))
+        ml = MoeLayer(self._dense_config(tensor_meta) if dense else self._layer_config(tensor_meta))
         ml.bind_device(blob_ptr, blob_bytes, tensor_meta, stream)
         if self.resident:
             self._bound[key] = ml
         return ml
 
-    def bind_tensors(self, t: dict[str, Any], expert_format: str = "float32") -> MoeLayer:
+    def bind_tensors(self, t: dict[str, Any], expert_format: str = "float32",
+                     dense: bool = False) -> MoeLayer:
         """Pack a dict of host arrays (reference tensor names) and bind it."""
         moe_t = {k: np.asarray(v) for k, v in t.items() if is_moe_tensor(k)}
         blob, meta = pack_layer(moe_t, expert_format=expert_format)
-        ml = MoeLayer(self._layer_config(meta))
+        ml = MoeLayer(self._dense_config(meta) if dense else self._layer_config(meta))
         ml.bind_host(blob, meta)
         return ml
 
@@ -110,6 +127,21 @@ class DeviceMoeExecutor:
             ml = self._bound.get(key)
             if ml is None:
                 ml = self.bind_tensors(t)
+                self._bound[key] = ml
+        if isinstance(x, np.ndarray):
+            return ml.forward_host(x)
+        return ml.forward(x)
+
+    def _dense_mlp_block(self, x: Any, t: Any) -> Any:
+        """``x + down(silu(gate(h)) * up(h))``, ``h = rms_norm(x)``, on the device;
+        same contract as the reference (glm4_moe.py:166-172)."""
+        if isinstance(t, MoeLayer):
+            ml = t
+        else:
+            key = ("dense", id(t))
+            ml = self._bound.get(key)
+            if ml is None:
+                ml = self.bind_tensors(t, dense=True)
                 self._bound[key] = ml
         if isinstance(x, np.ndarray):
             return ml.forward_host(x)
@@ -137,11 +169,16 @@ class DeviceMoeExecutor:
                                        [dict(m, name=_short(m["name"], layer)) for m in meta],
                                        stream_handle)
             x = self._moe_mlp_block(x, ml)
-        else:
-            if self.dense_mlp is None:
-                raise NotImplementedError("dense layer: pass dense_mlp=<callable(x, t)>")
+        elif self.dense_mlp is not None:
             t_all = _read_ranges(backend, device_weights, meta, stream)
             x = self.dense_mlp(x, t_all)
+        else:  # the dense MLP on the device, packed straight from the blob
+            stream_handle = getattr(stream, "value", stream)
+            ml = self.bind_device_blob(("dense", layer.layer_id), int(device_weights.handle),
+                                       int(device_weights.nbytes),
+                                       [dict(m, name=_short(m["name"], layer)) for m in meta],
+                                       stream_handle, dense=True)
+            x = self._dense_mlp_block(x, ml)
         return x
 
 
@@ -163,9 +200,11 @@ def _read_ranges(backend: Any, buf: Any, metas: list[dict[str, Any]], stream: An
 
 
 def reference_delegates(ref_executor: Any) -> dict[str, Any]:
-    """``attention=`` / ``dense_mlp=`` callables built from a reference executor instance.
+    """The ``attention=`` callable built from a reference executor instance (dense
+    MLP layers run on the device; pass the reference's ``_dense_mlp_block`` as
+    ``dense_mlp=`` to keep them on the host instead).
 
-    GLM-4 MoE: ``_attention_block`` (glm4_moe.py:112) and ``_dense_mlp_block`` (:166).
+    GLM-4 MoE: ``_attention_block`` (glm4_moe.py:112).
     Qwen3-Next: ``_full_attn_block`` / ``_linear_attn_block`` by ``metadata["attn_type"]``
     (qwen3_next.py:149-154).
     """
@@ -180,5 +219,4 @@ def reference_delegates(ref_executor: Any) -> dict[str, Any]:
             if layer.metadata.get("attn_type", "linear") == "full":
                 return ref_executor._full_attn_block(x, _strip(layer, t))
             return ref_executor._linear_attn_block(x, _strip(layer, t))
-    dense = getattr(ref_executor, "_dense_mlp_block", None)
-    return {"attention": attention, "dense_mlp": dense}
+    return {"attention": attention}

@@ -1,9 +1,9 @@
 """GLM-4 MoE (Glm4MoeForCausalLM) executor with the MoE block on sm_100a.
 
 Constructor and attribute names follow offload_runtime/executors/glm4_moe.py:70-84;
-the MoE block (glm4_moe.py:176-240) runs through libmoe_sm100.  Dense layers
-(``metadata["is_moe"] == False``, glm4_moe.py:102-106) use the ``dense_mlp``
-delegate.
+the MoE block (glm4_moe.py:176-240) runs through libmoe_sm100, and so does the
+dense MLP of ``first_k_dense_replace`` layers (``metadata["is_moe"] == False``,
+glm4_moe.py:102-106, 166-172) unless a ``dense_mlp`` delegate is given.
 """
 from __future__ import annotations
 

@@ -16,7 +16,9 @@ from typing import Any
 
 import numpy as np
 
-EXPERT_WEIGHT = re.compile(r"(^|\.)mlp\.(experts\.\d+|shared_experts?)\.(gate|up|down)_proj\.weight$")
+# expert, shared-expert and dense-MLP (first_k_dense_replace layers) projections
+EXPERT_WEIGHT = re.compile(
+    r"(^|\.)mlp\.((experts\.\d+|shared_experts?)\.)?(gate|up|down)_proj\.weight$")
 
 
 def is_expert_weight(name: str) -> bool:

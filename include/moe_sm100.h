@@ -63,6 +63,12 @@ enum {
 
 typedef struct MoePlan MoePlan;
 
+/* n_experts = 0 (with top_k = 0, no bias / gate / expert range) makes a dense
+ * MLP plan: the MLP of GLM-4 first_k_dense_replace layers
+ * (offload_runtime/executors/glm4_moe.py:166-172, _dense_mlp_block), whose
+ * mlp.{gate,up,down}_proj weights bind as a shared expert of shared_inter
+ * (= intermediate_size) columns; moe_forward then returns x + MLP(rms_norm(x)).
+ * moe_route, moe_forward_static_scratch and moe_ep_* refuse dense plans. */
 typedef struct MoeConfig {
   int32_t hidden;                /* H  (hidden_size)                                  */
   int32_t n_experts;             /* E  (n_routed_experts / num_experts)               */

@@ -148,3 +148,32 @@ SIGMOID_SPECS: dict[str, CaseSpec] = {
     "glm_sigmoid": CaseSpec(hidden=1024, n_experts=16, top_k=4, inter=256, shared_inter=256,
                             tokens=64, seed=7, score_func="sigmoid", routed_scaling_factor=2.5),
 }
+
+
+# Dense MLP of GLM-4 first_k_dense_replace layers (glm4_moe.py:166-172): only
+# hidden, inter (the layer's intermediate_size), tokens, seed, eps and weights
+# matter; n_experts / top_k are 0.
+DENSE_SPECS: dict[str, CaseSpec] = {
+    "glm_dense": CaseSpec(hidden=1024, n_experts=0, top_k=0, inter=512, shared_inter=0,
+                          tokens=24, seed=31, weights="bf16", norm_w_std=0.1),
+    "glm_dense_t1": CaseSpec(hidden=512, n_experts=0, top_k=0, inter=384, shared_inter=0,
+                             tokens=1, seed=32, weights="f32", norm_w_std=0.1),
+}
+
+
+def make_dense_case(spec: CaseSpec) -> tuple[np.ndarray, dict[str, np.ndarray], dict[str, Any]]:
+    """``(x, tensors, quant)`` of a dense-MLP layer: post_attention_layernorm and
+    mlp.{gate,up,down}_proj (nn.Linear [out, in] layout)."""
+    rng = np.random.default_rng(spec.seed)
+    H, I = spec.hidden, spec.inter
+    x = rng.standard_normal((spec.tokens, H), dtype=np.float32)
+    t: dict[str, np.ndarray] = {}
+    quant: dict[str, Any] = {}
+    t["post_attention_layernorm.weight"] = (
+        1.0 + spec.norm_w_std * rng.standard_normal(H, dtype=np.float32)).astype(np.float32)
+    for nm, shp in (("gate_proj", (I, H)), ("up_proj", (I, H)), ("down_proj", (H, I))):
+        key = f"mlp.{nm}.weight"
+        t[key], qs = _weights(rng, shp, spec.weights)
+        if qs is not None:
+            quant[key] = qs
+    return x, t, quant

@@ -168,6 +168,14 @@ def _swiglu(xin: np.ndarray, wg: np.ndarray, wu: np.ndarray, wd: np.ndarray) -> 
     return (silu(xin @ wg.T) * (xin @ wu.T)) @ wd.T
 
 
+def dense_mlp_block(x: np.ndarray, t: dict[str, np.ndarray], eps: float) -> np.ndarray:
+    """glm4_moe.py:166-172 (``_dense_mlp_block`` of first_k_dense_replace layers):
+    ``x + (silu(h Wg^T) * (h Wu^T)) Wd^T`` with ``h = rms_norm(x)``."""
+    h = rms_norm(x, t["post_attention_layernorm.weight"], eps)
+    return x + _swiglu(h, t["mlp.gate_proj.weight"], t["mlp.up_proj.weight"],
+                       t["mlp.down_proj.weight"])
+
+
 def moe_block(x: np.ndarray, t: dict[str, np.ndarray], cfg: OracleConfig
               ) -> tuple[np.ndarray, dict[str, np.ndarray]]:
     """Full MoE block on fp32 numpy arrays; returns ``(x + moe(x), aux)``.

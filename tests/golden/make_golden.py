@@ -14,6 +14,11 @@ records the result of the ``take_along_axis`` call that reorders ``topk_indices`
 For ``oracle.cases.SIGMOID_SPECS`` (HF GLM-4.x sigmoid routing, which the reference
 does not implement) it records transformers' ``Glm4MoeMoE.route_tokens_to_experts``.
 
+For ``oracle.cases.DENSE_SPECS`` it runs the reference ``_dense_mlp_block`` (the MLP
+of GLM-4 first_k_dense_replace layers, glm4_moe.py:166-172) and stores its output.
+
+``--only NAME ...`` regenerates just those fixtures (the manifest keeps the others).
+
 Fixtures hold outputs and input checksums only; inputs are rebuilt from the seed.
 """
 from __future__ import annotations
@@ -28,7 +33,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
-from oracle.cases import GOLDEN_SPECS, SIGMOID_SPECS, input_checksum, make_case  # noqa: E402
+from oracle.cases import (DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS, input_checksum,  # noqa: E402
+                          make_case, make_dense_case)
 from oracle.moe_oracle import rms_norm  # noqa: E402
 
 
@@ -78,6 +84,15 @@ def run_reference(spec, x, t):  # noqa: ANN001, ANN201
     return np.asarray(out, dtype=np.float32), ids
 
 
+def run_reference_dense(spec, x, t):  # noqa: ANN001, ANN201
+    import offload_runtime.executors.glm4_moe as mod
+    ex = mod.GLM4MoeExecutor({
+        "hidden_size": spec.hidden, "num_attention_heads": 8, "intermediate_size": spec.inter,
+        "rms_norm_eps": spec.eps,
+    })
+    return np.asarray(ex._dense_mlp_block(x, t), dtype=np.float32)
+
+
 def run_hf_sigmoid(spec, x, t):  # noqa: ANN001, ANN201
     import torch
     from transformers.models.glm4_moe.configuration_glm4_moe import Glm4MoeConfig
@@ -102,11 +117,16 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the disk-mem-off checkout")
     ap.add_argument("--out", default=str(Path(__file__).resolve().parent))
+    ap.add_argument("--only", nargs="*", default=None, help="fixture names to regenerate")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     out_dir = Path(args.out)
-    manifest = {}
+    mpath = out_dir / "manifest.json"
+    manifest = json.loads(mpath.read_text()) if args.only and mpath.exists() else {}
+    want = (lambda n: True) if not args.only else (lambda n: n in args.only)
     for name, spec in GOLDEN_SPECS.items():
+        if not want(name):
+            continue
         x, t, _quant, _cfg = make_case(spec)
         out, ids = run_reference(spec, x, t)
         np.savez_compressed(out_dir / f"{name}.npz", out=out, topk_ids=ids,
@@ -114,6 +134,8 @@ def main() -> None:
         manifest[name] = {"spec": spec.to_dict(), "source": "reference _moe_mlp_block"}
         print(name, out.shape, ids.shape)
     for name, spec in SIGMOID_SPECS.items():
+        if not want(name):
+            continue
         x, t, _quant, _cfg = make_case(spec)
         ids, w = run_hf_sigmoid(spec, x, t)
         np.savez_compressed(out_dir / f"{name}.npz", topk_ids=ids, topk_w=w,
@@ -121,7 +143,15 @@ def main() -> None:
         manifest[name] = {"spec": spec.to_dict(),
                           "source": "transformers Glm4MoeMoE.route_tokens_to_experts"}
         print(name, ids.shape)
-    (out_dir / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True))
+    for name, spec in DENSE_SPECS.items():
+        if not want(name):
+            continue
+        x, t, _quant = make_dense_case(spec)
+        out = run_reference_dense(spec, x, t)
+        np.savez_compressed(out_dir / f"{name}.npz", out=out, checksum=input_checksum(x, t))
+        manifest[name] = {"spec": spec.to_dict(), "source": "reference _dense_mlp_block"}
+        print(name, out.shape)
+    mpath.write_text(json.dumps(manifest, indent=1, sort_keys=True))
 
 
 if __name__ == "__main__":

@@ -57,6 +57,12 @@ def _cfg(**kw: int) -> _lib.MoeConfigC:
     (dict(max_tokens=0), _lib.MOE_ERR_INVALID),
     (dict(shared_inter=0, has_shared_gate=1), _lib.MOE_ERR_INVALID),
     (dict(n_experts=2000), _lib.MOE_ERR_UNSUPPORTED),
+    (dict(n_experts=-1), _lib.MOE_ERR_UNSUPPORTED),
+    # dense MLP plans (n_experts = 0): no routing, no bias, a shared width
+    (dict(n_experts=0, top_k=2), _lib.MOE_ERR_INVALID),
+    (dict(n_experts=0, top_k=0, use_bias=1), _lib.MOE_ERR_INVALID),
+    (dict(n_experts=0, top_k=0, use_bias=0, shared_inter=0), _lib.MOE_ERR_INVALID),
+    (dict(n_experts=0, top_k=0, use_bias=0, has_shared_gate=1), _lib.MOE_ERR_INVALID),
 ])
 def test_plan_create_validates_before_touching_cuda(built_lib: str, bad: dict, code: int) -> None:
     lib = _lib.lib()

@@ -9,7 +9,8 @@
   oracle at T = 1, 8, 64 and 4096 (a flip is tolerated only at an oracle score gap
   below 1e-6 relative, and is counted), output parity at T = 1 and 4 on the
   experts the tokens touch, size-independent properties at T = 64 / 4096;
-* prefill routing (tensor-core candidates, fp32 decision) on exact ties.
+* prefill routing (tensor-core candidates, fp32 decision) on exact ties;
+* the dense MLP of first_k_dense_replace layers against the reference's output.
 """
 from __future__ import annotations
 
@@ -26,8 +27,9 @@ pytestmark = [pytest.mark.gpu,
 from moe_sm100 import MoeLayer, MoeLayerConfig  # noqa: E402
 from moe_sm100.packing import pack_layer  # noqa: E402
 from moe_sm100.synthetic import GLM47, LazyHostTensors, SyntheticSpec, build_device_layer  # noqa: E402
-from oracle.cases import GOLDEN_SPECS, make_case  # noqa: E402
-from oracle.moe_oracle import OracleConfig, moe_block, permutation, rms_norm, route  # noqa: E402
+from oracle.cases import DENSE_SPECS, GOLDEN_SPECS, make_case, make_dense_case  # noqa: E402
+from oracle.moe_oracle import (OracleConfig, dense_mlp_block, int8_pc_dequantize,  # noqa: E402
+                               int8_pc_quantize, moe_block, permutation, rms_norm, route)
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 TOL_16 = 2e-3
@@ -135,6 +137,55 @@ def test_empty_batch_and_limits() -> None:
     with pytest.raises(KeyError):
         bad = [m for m in meta if m["name"] != "mlp.experts.3.up_proj.weight"]
         MoeLayer(_layer_cfg(spec, "f16", 4)).bind_host(blob, bad)
+
+
+# ------------------------------------------------------------------ dense MLP layers
+@pytest.mark.parametrize("name,fmt", [("glm_dense", "bfloat16"), ("glm_dense", "float32"),
+                                      ("glm_dense_t1", "float32"), ("glm_dense", "int8")])
+def test_dense_mlp_parity(name: str, fmt: str) -> None:
+    """first_k_dense_replace layers (glm4_moe.py:166-172) as a plan with no routed
+    experts: against the reference's own output (16-bit weights) or the oracle on
+    the dequantized per-channel INT8 weights."""
+    spec = DENSE_SPECS[name]
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        gout = z["out"]
+    x, t, _q = make_dense_case(spec)
+    blob, meta = pack_layer(t, expert_format=fmt)
+    cfg = MoeLayerConfig.dense_mlp({"hidden_size": spec.hidden, "intermediate_size": spec.inter},
+                                   rms_norm_eps=spec.eps, max_tokens=spec.tokens,
+                                   weight_format="int8" if fmt == "int8" else "f16")
+    ml = MoeLayer(cfg)
+    ml.bind_host(blob, meta)
+    out = ml.forward(torch.from_numpy(x).cuda())
+    ml.status()
+    if fmt == "int8":
+        tq = dict(t)
+        for k in ("mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"):
+            tq[k] = int8_pc_dequantize(*int8_pc_quantize(t[k]))
+        ref, tol = dense_mlp_block(x, tq, spec.eps), TOL_I8
+    else:
+        ref, tol = gout, TOL_16
+    err = rel_l2(out.cpu().numpy(), ref)
+    assert err <= tol, f"rel-L2 {err:.3e}"
+    assert torch.equal(out, ml.forward(torch.from_numpy(x).cuda()))  # deterministic
+    with pytest.raises(RuntimeError, match="no routing"):  # no routing to report
+        ml.route(torch.from_numpy(x).cuda())
+    ml.close()
+
+
+def test_dense_layer_through_executor() -> None:
+    """GLM4MoeExecutor._dense_mlp_block keeps the reference signature and runs on the device."""
+    spec = DENSE_SPECS["glm_dense"]
+    with np.load(os.path.join(GOLDEN, "glm_dense.npz")) as z:
+        gout = z["out"]
+    x, t, _q = make_dense_case(spec)
+    from moe_sm100.executors import GLM4MoeExecutor
+    ex = GLM4MoeExecutor({"hidden_size": spec.hidden, "intermediate_size": spec.inter,
+                          "moe_intermediate_size": 64, "n_routed_experts": 8,
+                          "num_experts_per_tok": 2, "rms_norm_eps": spec.eps}, max_tokens=32)
+    out = ex._dense_mlp_block(x, t)
+    assert isinstance(out, np.ndarray) and out.shape == x.shape
+    assert rel_l2(out, gout) <= TOL_16
 
 
 # ------------------------------------------------------------------ full GLM-4.7 shape

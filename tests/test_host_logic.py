@@ -53,6 +53,10 @@ def test_expert_weight_names() -> None:
     assert not is_expert_weight("mlp.gate.weight")
     assert not is_expert_weight("mlp.shared_expert_gate.weight")
     assert not is_expert_weight("self_attn.q_proj.weight")
+    # dense MLP of first_k_dense_replace layers: packed like expert weights
+    assert is_expert_weight("mlp.gate_proj.weight")
+    assert is_expert_weight("model.layers.0.mlp.down_proj.weight")
+    assert not is_expert_weight("mlp.gate_proj.bias")
 
 
 @pytest.mark.parametrize("fmt", ["float32", "bfloat16", "int8"])
@@ -92,6 +96,15 @@ def test_glm_config_defaults_follow_reference() -> None:
     assert s.score_func == "sigmoid"
     cc = c.to_c()
     assert cc.hidden == 5120 and cc.n_experts == 160 and abs(cc.routed_scaling_factor - 2.5) < 1e-7
+
+
+def test_dense_mlp_config() -> None:
+    c = MoeLayerConfig.dense_mlp({"hidden_size": 5120, "intermediate_size": 12288,
+                                  "rms_norm_eps": 1e-5})
+    assert (c.n_experts, c.top_k, c.shared_inter, c.inter) == (0, 0, 12288, 0)
+    assert not c.use_bias and not c.has_shared_gate and c.rms_norm_eps == 1e-5
+    cc = c.to_c()
+    assert cc.n_experts == 0 and cc.shared_inter == 12288
 
 
 def test_qwen3_config_defaults_follow_reference() -> None:

@@ -11,9 +11,10 @@ import os
 import numpy as np
 import pytest
 
-from oracle.cases import GOLDEN_SPECS, SIGMOID_SPECS, CaseSpec, input_checksum, make_case
-from oracle.moe_oracle import (int8_pc_dequantize, int8_pc_quantize, moe_block, permutation,
-                               rms_norm, route, select_topk)
+from oracle.cases import (DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS, CaseSpec, input_checksum,
+                          make_case, make_dense_case)
+from oracle.moe_oracle import (dense_mlp_block, int8_pc_dequantize, int8_pc_quantize, moe_block,
+                               permutation, rms_norm, route, select_topk)
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -33,6 +34,17 @@ def test_oracle_reproduces_reference(name: str) -> None:
     out, aux = moe_block(x, t, cfg)
     np.testing.assert_array_equal(aux["topk_ids"], g["topk_ids"])
     np.testing.assert_array_equal(out, g["out"])  # bit-exact
+
+
+@pytest.mark.parametrize("name", sorted(DENSE_SPECS))
+def test_dense_oracle_reproduces_reference(name: str) -> None:
+    """The dense MLP of first_k_dense_replace layers, against the reference's own
+    ``_dense_mlp_block`` output (glm4_moe.py:166-172), bit for bit."""
+    spec = DENSE_SPECS[name]
+    g = _load(name)
+    x, t, _q = make_dense_case(spec)
+    np.testing.assert_array_equal(input_checksum(x, t), g["checksum"])
+    np.testing.assert_array_equal(dense_mlp_block(x, t, spec.eps), g["out"])
 
 
 @pytest.mark.parametrize("name", sorted(SIGMOID_SPECS))
