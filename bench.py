@@ -334,6 +334,48 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
 
 
 # ------------------------------------------------------------------ expert parallel (N > 1)
+def run_ep_qwen3(args, world: int, rank: int, local: int, tflops: float) -> dict:  # noqa: ANN001
+    """BASELINE config 3 across the ranks: Qwen3-Next shape, 512/N experts per rank,
+    1-token decode and 8192-token prefill per rank (weak scaling)."""
+    import torch
+    from moe_sm100 import MoeLayerConfig
+    from moe_sm100.ep import DeviceEPOps, ExpertParallelMoe
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer
+    spec = SyntheticSpec(**QWEN3, family="qwen3", expert_dtype="bfloat16", seed=5678)
+    blob, meta = build_device_layer(spec, device=f"cuda:{local}")
+    cfg = MoeLayerConfig(**QWEN3, use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
+                         rms_norm_eps=1e-6, max_tokens=8192, device=local)
+    ops = DeviceEPOps(cfg, rank, world)
+    ops.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    del blob
+    torch.cuda.empty_cache()
+    ep = ExpertParallelMoe(ops)
+    gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    res = {}
+    for T in (1, 8192):
+        x = torch.randn((T, QWEN3["hidden"]), generator=gen, device="cuda")
+        steps = max(3, min(args.steps, 10 if T > 1024 else args.steps))
+        ms = _time_steps(lambda: ep.forward(x), steps, args.warmup, world)
+        tim = []
+        for _ in range(3):
+            ep.forward(x, timed=True)
+            tim.append(ep.last_timing)
+        a2a = float(np.median([t["a2a_ms"] for t in tim]))
+        tot = float(np.median([t["total_ms"] for t in tim]))
+        entry = {"tokens_per_s": world * T / (ms * 1e-3), "ms_per_step": ms,
+                 "tokens_per_rank": T, "experts_per_rank": QWEN3["n_experts"] // world,
+                 "a2a_frac_of_layer": _max_over_ranks(a2a / tot, world)}
+        if T >= 1024:
+            fg, fd = _gemm_flops(T, QWEN3["top_k"], QWEN3["hidden"], QWEN3["inter"],
+                                 QWEN3["shared_inter"])
+            entry["tc_frac_layer_per_gpu"] = (fg + fd) / (ms * 1e-3) / 1e12 / tflops
+        res[f"cfg3_qwen3_next_ep{world}_T{T}"] = entry
+    ops.status()
+    ops.close()
+    return res
+
+
 def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     """N GPUs: experts sharded 160/N per rank, T tokens per rank, NCCL all-to-all."""
     import torch
@@ -386,6 +428,12 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     for _ in range(args.steps):
         e2e_step()
     e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    other = {}
+    if not args.no_other:
+        ops.close()
+        del ep, ops
+        torch.cuda.empty_cache()
+        other = run_ep_qwen3(args, world, rank, local, _tc_peak())
     # expert weight bytes this rank streams per step (its touched local experts + shared)
     e_loc = GLM["n_experts"] // world
     layer_bytes = (min(e_loc, recv) + 1) * 3 * GLM["hidden"] * GLM["inter"] * 2
@@ -414,8 +462,10 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             # gather, two GEMMs (experts); scan, two GEMMs (shared); combine
             "gpu_launches": 14 * args.steps,
             "clocks": clocks,
+            "other_configs": other,
         }))
-    ops.close()
+    if args.no_other:
+        ops.close()
     dist.barrier()
     dist.destroy_process_group()
 
