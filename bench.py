@@ -24,6 +24,11 @@ box's host cores, all BLAS threads, same config, metric and unit.
 N > 1 (torchrun): expert parallel -- rank r holds routed experts
 [r*160/N, (r+1)*160/N), router and shared expert replicated, 64 tokens per rank
 (weak scaling); dispatch and combine are NCCL all-to-all exchanges of f16 rows.
+
+--stack (torchrun, N = 2, 4 or 8): BASELINE config 4 -- 89 GLM-4.7-shape INT8 layers
+(seed + layer each, Zipf-skewed routing) resident expert parallel, 160/N experts of
+every layer per GPU; a 256-token decode batch and a 16384-token prefill batch split
+evenly over the ranks (strong scaling); one JSON line with both workloads.
 """
 from __future__ import annotations
 
@@ -287,7 +292,8 @@ def _measure(ml, T: int, H: int, steps: int, warmup: int, world: int, gen) -> di
 
 
 def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -> dict:  # noqa: ANN001
-    """BASELINE config 2 (GLM-4.7 INT8, 4096-token prefill, Zipf routing) and
+    """BASELINE config 2 (GLM-4.7 INT8, 4096-token prefill, Zipf routing; the same
+    layer also at 32 and 128 tokens, the per-rank decode batches of config 4) and
     config 3 (Qwen3-Coder-Next shape, 1-token decode and 8192-token prefill)."""
     import torch
     from moe_sm100 import MoeLayer, MoeLayerConfig
@@ -297,7 +303,8 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
     runs = [
         ("cfg2_glm47_int8_prefill", dict(GLM, family="glm", expert_dtype="int8", seed=4321,
                                          zipf_s=1.1, zipf_amp=1.0),
-         dict(weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5), [4096]),
+         dict(weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5),
+         [32, 128, 4096]),
         ("cfg3_qwen3_next", dict(QWEN3, family="qwen3", expert_dtype="bfloat16", seed=5678),
          dict(use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
               rms_norm_eps=1e-6), [1, 8192]),
@@ -327,7 +334,8 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
             else:  # decode: weight streaming
                 wb = (m["unique"] + 1) * 3 * H * I * wbytes
                 entry["layer_hbm_frac"] = wb / (m["ms"] * 1e-3) / 1e9 / hbm
-            res[f"{name}_T{T}"] = entry
+            # the INT8 layer at decode sizes (the per-rank batches of BASELINE config 4)
+            res[f"{name if T >= 1024 else name.replace('_prefill', '_decode')}_T{T}"] = entry
         ml.close()
         torch.cuda.empty_cache()
     return res
@@ -470,11 +478,164 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ 89-layer stack (N > 1)
+def _sum_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def _stack_resident_bytes(e_loc: int, layers: int) -> int:
+    """Device bytes one rank keeps resident for the INT8 stack (packed weights,
+    fp32 per-row scales, shared expert, norm, fp32 + f16 router, bias)."""
+    H, I, SI, E = GLM["hidden"], GLM["inter"], GLM["shared_inter"], GLM["n_experts"]
+    per_layer = (e_loc * (3 * H * I + (2 * I + H) * 4) + 3 * SI * H + (2 * SI + H) * 4
+                 + H * 4 + E * H * 6 + E * 4)
+    return layers * per_layer
+
+
+def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
+    """a stack of GLM-4.7-shape INT8 MoE layers (seed + layer per
+    layer, Zipf-skewed routing), resident expert parallel over the ranks (160/N
+    experts of every layer per GPU), NCCL all-to-all dispatch and return.  The
+    global batch is fixed (256-token decode, 16384-token prefill) and split evenly
+    over the ranks: strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from moe_sm100 import MoeLayerConfig
+    from moe_sm100.ep import DeviceEPOps, ExpertParallelMoe
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer
+    hbm, peak_kind = _peaks()
+    tflops = _tc_peak()
+    L = args.stack_layers
+    H, E, K, I, SI = (GLM[k] for k in ("hidden", "n_experts", "top_k", "inter", "shared_inter"))
+    batches = {"decode": args.stack_decode, "prefill": args.stack_prefill}
+    head = {"metric": f"{L}-layer MoE stack tokens/s (GLM-4.7 shape, INT8 experts, expert parallel)",
+            "unit": "tokens/s", "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "config": {"workload": "BASELINE config 4", "layers": L, "global_tokens": batches,
+                       "experts_per_rank": E // world if world else None,
+                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/return)"}}
+    if world < 2 or E % world or any(t % world for t in batches.values()):
+        if rank == 0:
+            print(json.dumps({**head, "unavailable":
+                              "the stack runs expert parallel on 2, 4 or 8 GPUs (160 experts and "
+                              "the batches split evenly over the ranks)"}))
+        return
+    e_loc = E // world
+    t_dec, t_pre = batches["decode"] // world, batches["prefill"] // world
+    resident = _stack_resident_bytes(e_loc, L)
+    # transient: dispatch and expert workspaces, exchanged rows and outputs of the
+    # prefill batch (the hottest rank can receive about twice its share)
+    transient = 16 * t_pre * K * H * 2 + (4 << 30)
+    free, _total = torch.cuda.mem_get_info()
+    fits = torch.tensor([1 if resident + transient <= free else 0], device="cuda")
+    dist.all_reduce(fits, op=dist.ReduceOp.MIN)
+    if int(fits.item()) == 0:
+        if rank == 0:
+            print(json.dumps({**head, "unavailable":
+                              f"resident stack needs {resident / 2**30:.1f} GiB + "
+                              f"{transient / 2**30:.1f} GiB transient per GPU; "
+                              f"{free / 2**30:.1f} GiB free"}))
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+
+    lo, hi = rank * e_loc, (rank + 1) * e_loc
+    pool: dict = {}
+    layers = []
+    t0 = time.perf_counter()
+    for layer in range(L):
+        spec = SyntheticSpec(**GLM, family="glm", expert_dtype="int8", seed=args.stack_seed + layer,
+                             zipf_s=1.1, zipf_amp=1.0, experts=(lo, hi))
+        blob, meta = build_device_layer(spec, device=f"cuda:{local}")
+        cfg = MoeLayerConfig(**GLM, weight_format="int8", routed_scaling_factor=2.5,
+                             rms_norm_eps=1e-5, max_tokens=t_pre, device=local)
+        ops = DeviceEPOps(cfg, rank, world, pool=pool)
+        ops.bind_device(blob.data_ptr(), blob.numel(), meta)
+        torch.cuda.synchronize()
+        del blob
+        layers.append((ops, ExpertParallelMoe(ops)))
+    torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t0
+
+    def stack(x):  # noqa: ANN001, ANN202
+        for _ops, ep in layers:
+            x = ep.forward(x)
+        return x
+
+    gen = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    results = {}
+    clocks = None
+    for name, t in (("decode", t_dec), ("prefill", t_pre)):
+        x = torch.randn((t, H), generator=gen, device="cuda")
+        steps = max(3, min(args.steps, 10))
+        with ClockSampler(local) as clk:
+            ms = _time_steps(lambda: stack(x), steps, args.warmup, world)
+        if name == "decode":
+            clocks = clk.summary()
+        for ops, _ep in layers:
+            ops.status()
+        # one instrumented pass: exchange share and the experts each rank touched
+        a2a = tot = 0.0
+        touched = 0
+        h = x
+        for _ops, ep in layers:
+            h = ep.forward(h, timed=True)
+            a2a += ep.last_timing["a2a_ms"]
+            tot += ep.last_timing["total_ms"]
+            touched += ep.last_timing["recv_experts"]
+        g_tokens = t * world
+        entry = {"tokens_per_s": g_tokens / (ms * 1e-3), "ms_per_step": ms,
+                 "ms_per_layer": ms / L, "tokens_per_rank": t, "steps": steps,
+                 "a2a_frac_of_layer": _max_over_ranks(a2a / tot, world)}
+        if name == "decode":
+            # INT8 weights (+ fp32 row scales) of the touched local experts and the
+            # shared expert, streamed once per layer; mean over the GPUs
+            wb = 3 * H * I + (2 * I + H) * 4
+            rank_bytes = (touched + L) * wb
+            achieved = _sum_over_ranks(rank_bytes, world) / world / (ms * 1e-3) / 1e9
+            entry["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": hbm,
+                                 "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
+                                 "per": "GPU (mean), expert weights of the stack"}
+            entry["touched_local_experts_per_layer_rank0"] = touched / L
+        else:
+            fg, fd = _gemm_flops(g_tokens, K, H, I, SI)
+            achieved = (fg + fd) * L / world / (ms * 1e-3) / 1e12
+            entry["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": tflops,
+                                 "unit": "TFLOP/s", "frac": achieved / tflops,
+                                 "peak_source": "MEASURED_PEAKS.json bf16 burst",
+                                 "per": "GPU (mean), expert + shared GEMMs of the stack"}
+        results[f"{name}_T{g_tokens}"] = entry
+    if rank == 0:
+        print(json.dumps({**head, "value": results[f"decode_T{batches['decode']}"]["tokens_per_s"],
+                          "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": results[f"decode_T{batches['decode']}"]["ms_per_step"],
+                          "dtype": "INT8 weights widened to f16 in shared memory, f16 MMA / fp32 "
+                                   "accumulate; fp32 routing; f16 exchange",
+                          "data": "synthetic (seeded N(0,1) tokens; per-layer seeded N(0,0.02) "
+                                  "weights quantised per row; Zipf(1.1) router bias)",
+                          "resident_gib_per_gpu": resident / 2**30, "build_s": build_s,
+                          "workloads": results, "clocks": clocks,
+                          "gpu_launches_per_layer": 14}))
+    for ops, _ep in layers:
+        ops.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ arms
 def run_ours(args) -> None:  # noqa: ANN001
     import torch
     world, rank, local = _dist_init()
     torch.cuda.set_device(local)
+    if args.stack:
+        run_stack(args, world, rank, local)
+        return
     if world > 1:
         run_ep(args, world, rank, local)
         return
@@ -684,6 +845,12 @@ def main() -> None:
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
+    ap.add_argument("--stack", action="store_true",
+                    help="BASELINE config 4: resident INT8 layer stack, expert parallel (N >= 2)")
+    ap.add_argument("--stack-layers", type=int, default=89)
+    ap.add_argument("--stack-seed", type=int, default=7000)
+    ap.add_argument("--stack-decode", type=int, default=256, help="global decode batch")
+    ap.add_argument("--stack-prefill", type=int, default=16384, help="global prefill batch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -106,35 +106,48 @@ class ExpertParallelMoe:
                 "combine_ms": t("returned", "end"),
                 "total_ms": t("start", "end"),
                 "recv_rows": n_recv,
+                "recv_experts": int(torch.unique(recv_experts).numel()) if n_recv else 0,
             }
         return out
 
 
 class DeviceEPOps:
-    """EPOps over libmoe_sm100 for this rank's expert share (CUDA tensors)."""
+    """EPOps over libmoe_sm100 for this rank's expert share (CUDA tensors).
 
-    def __init__(self, cfg: MoeLayerConfig, rank: int, world: int) -> None:
+    ``pool``: a dict shared by the layers of a stack that run one after another on
+    the same stream.  Their workspaces and the shared-expert side stream then live
+    in it once instead of once per layer (a forward's workspace is free again when
+    its combine has been issued, and the next layer's dispatch is ordered after it).
+    """
+
+    def __init__(self, cfg: MoeLayerConfig, rank: int, world: int,
+                 pool: dict[str, Any] | None = None) -> None:
         if cfg.n_experts % world:
             raise ValueError("n_experts must be divisible by the number of ranks")
         e_loc = cfg.n_experts // world
         self.cfg = replace(cfg, expert_begin=rank * e_loc, expert_end=(rank + 1) * e_loc)
         self.layer = MoeLayer(self.cfg)
         self.world = world
-        self._ws = None
-        self._ws_ep = None
+        self._pool: dict[str, Any] = pool if pool is not None else {}
         self._T = 0
         self._shared_done: Any = None  # event of a shared-expert pass started early
+
+    @property
+    def _ws(self) -> Any:
+        return self._pool.get("ws")
 
     def bind_device(self, blob_ptr: int, blob_bytes: int, tensor_meta: list[dict[str, Any]],
                     stream: Any = None) -> None:
         self.layer.bind_device(blob_ptr, blob_bytes, tensor_meta, stream)
 
-    def _buf(self, attr: str, nbytes: int) -> Any:
+    def _buf(self, key: str, nbytes: int) -> Any:
         torch = _torch()
-        cur = getattr(self, attr)
+        cur = self._pool.get(key)
         if cur is None or cur.numel() < nbytes:
+            cur = None  # drop the smaller buffer before allocating its successor
+            self._pool.pop(key, None)
             cur = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=f"cuda:{self.cfg.device}")
-            setattr(self, attr, cur)
+            self._pool[key] = cur
         return cur
 
     def dispatch(self, x: Any) -> tuple[Any, Any, Any]:
@@ -142,7 +155,7 @@ class DeviceEPOps:
         t = x.shape[0]
         k, h = self.cfg.top_k, self.cfg.hidden
         plan = self.layer._plan
-        ws = self._buf("_ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
+        ws = self._buf("ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
         rows = torch.empty((t * k, h), dtype=torch.float16, device=x.device)
         experts = torch.empty((t * k,), dtype=torch.int32, device=x.device)
         offsets = torch.empty((self.world + 1,), dtype=torch.int32, device=x.device)
@@ -160,7 +173,7 @@ class DeviceEPOps:
         if r == 0:
             return y
         plan = self.layer._plan
-        ws = self._buf("_ws_ep", int(lib().moe_ep_workspace_bytes(plan, r)))
+        ws = self._buf("ws_ep", int(lib().moe_ep_workspace_bytes(plan, r)))
         check(lib().moe_ep_experts(plan, c_void_p(rows.data_ptr()), c_void_p(expert_ids.data_ptr()),
                                    r, c_void_p(y.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(),
                                    c_void_p(_stream_handle(None))))
@@ -173,15 +186,16 @@ class DeviceEPOps:
         t = x.shape[0]
         if t == 0 or self.cfg.shared_inter == 0:
             return
-        if getattr(self, "_side", None) is None:
-            self._side = torch.cuda.Stream(device=x.device)
+        side = self._pool.get("side")
+        if side is None:
+            side = self._pool["side"] = torch.cuda.Stream(device=x.device)
         main = torch.cuda.current_stream(x.device)
-        self._side.wait_stream(main)  # after dispatch (its workspace holds the rows)
+        side.wait_stream(main)  # after dispatch (its workspace holds the rows)
         ws = self._ws
         check(lib().moe_ep_shared(self.layer._plan, t, c_void_p(ws.data_ptr()), ws.numel(),
-                                  c_void_p(self._side.cuda_stream)))
+                                  c_void_p(side.cuda_stream)))
         self._shared_done = torch.cuda.Event()
-        self._shared_done.record(self._side)
+        self._shared_done.record(side)
 
     def combine(self, x: Any, y_back: Any) -> Any:
         torch = _torch()

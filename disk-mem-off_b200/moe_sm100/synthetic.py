@@ -9,6 +9,12 @@ bias ~ N(0,0.01) plus an optional Zipf(s)-ranked skew.
 
 ``expert_dtype``: "bfloat16" (bf16-rounded N(0,0.02)) or "int8" (per-row
 quantised from an fp32 N(0,0.02) source, fp16 scales = max|w|/127).
+
+``experts = (lo, hi)`` materialises only routed experts [lo, hi) (the share of one
+expert-parallel rank).  The router, bias, norm and shared expert are still built, the
+router and bias from the same generator stream as a full layer; each routed expert and
+the shared expert then come from their own generator (seeded from ``seed`` and the
+expert id), so an expert's weights do not depend on which rank builds it.
 """
 from __future__ import annotations
 
@@ -36,6 +42,7 @@ class SyntheticSpec:
     bias_std: float = 0.01
     zipf_s: float = 0.0
     zipf_amp: float = 1.0
+    experts: tuple[int, int] | None = None   # routed experts to materialise (None: all)
 
 
 GLM47 = dict(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536, family="glm")
@@ -59,7 +66,8 @@ def _tensor_list(spec: SyntheticSpec) -> list[tuple[str, list[int], str]]:
             if ed == "int8":
                 out.append((f"{prefix}{nm}.weight_scale", [shp[0]], "float16"))
 
-    for e in range(E):
+    lo, hi = spec.experts if spec.experts is not None else (0, E)
+    for e in range(lo, hi):
         proj(f"mlp.experts.{e}.", I)
     if SI > 0:
         proj("mlp.shared_experts." if spec.family == "glm" else "mlp.shared_expert.", SI)
@@ -107,10 +115,28 @@ def build_device_layer(spec: SyntheticSpec, device: Any = "cuda") -> tuple[Any, 
     if spec.family == "qwen3" and spec.shared_inter > 0:
         view("mlp.shared_expert_gate.weight", torch.float32).copy_(
             torch.randn((1, H), generator=gen, device=device) * 0.02)
+    subset = spec.experts is not None
+    if subset:
+        lo, hi = spec.experts
+        if not 0 <= lo < hi <= E:
+            raise ValueError(f"expert range {spec.experts} outside [0, {E}]")
+    gens: dict[int, Any] = {}
+
+    def gen_for(name: str) -> Any:
+        # full layers draw everything from one stream; subsets one stream per expert
+        if not subset:
+            return gen
+        key = int(name.split(".")[2]) if name.startswith("mlp.experts.") else E
+        if key not in gens:
+            g = torch.Generator(device=device)
+            g.manual_seed(spec.seed * 1_000_003 + 7919 * (key + 1))
+            gens[key] = g
+        return gens[key]
+
     for name, shape, dt in items:
         if dt not in ("bfloat16", "int8"):
             continue
-        w = torch.randn(shape, generator=gen, device=device) * 0.02
+        w = torch.randn(shape, generator=gen_for(name), device=device) * 0.02
         if dt == "bfloat16":
             view(name, torch.bfloat16).copy_(w.to(torch.bfloat16))
         else:

@@ -222,3 +222,21 @@ def test_executor_rejects_non_cuda_backend() -> None:
 
     with pytest.raises(ValueError):
         ex.run_layer(layer, np.zeros((1, 256), np.float32), DeviceBuffer(0, 0, "null"), _Null(), None)
+
+
+def test_synthetic_expert_subsets_agree_across_ranks() -> None:
+    """An expert-parallel rank builds only its experts; the router, bias and shared
+    expert, and every expert two ranks both hold, come out the same."""
+    from moe_sm100.synthetic import SyntheticSpec, build_device_layer, host_tensor
+    kw = dict(hidden=64, n_experts=8, top_k=2, inter=32, shared_inter=32, family="glm",
+              expert_dtype="int8", seed=5, zipf_s=1.1)
+    b1, m1 = build_device_layer(SyntheticSpec(**kw, experts=(0, 4)), device="cpu")
+    b2, m2 = build_device_layer(SyntheticSpec(**kw, experts=(2, 6)), device="cpu")
+    experts1 = {m["name"].split(".")[2] for m in m1 if m["name"].startswith("mlp.experts.")}
+    assert experts1 == {"0", "1", "2", "3"}
+    for name in ("mlp.gate.weight", "mlp.gate.e_score_correction_bias",
+                 "mlp.experts.2.up_proj.weight", "mlp.experts.3.down_proj.weight_scale",
+                 "mlp.shared_experts.gate_proj.weight"):
+        np.testing.assert_array_equal(host_tensor(b1, m1, name), host_tensor(b2, m2, name))
+    with pytest.raises(ValueError, match="outside"):
+        build_device_layer(SyntheticSpec(**kw, experts=(4, 9)), device="cpu")
