@@ -23,7 +23,9 @@ box's host cores, all BLAS threads, same config, metric and unit.
 
 N > 1 (torchrun): expert parallel -- rank r holds routed experts
 [r*160/N, (r+1)*160/N), router and shared expert replicated, 64 tokens per rank
-(weak scaling); dispatch and combine are NCCL all-to-all exchanges of f16 rows.
+(weak scaling); dispatch and combine are NCCL all-to-all exchanges of f16 rows,
+by default the fixed-capacity exchange (equal row blocks, no host synchronisation;
+--ep-exchange exact: counts first, then exactly the routed rows).
 
 --stack (torchrun, N = 2, 4 or 8): BASELINE config 4 -- 89 GLM-4.7-shape INT8 layers
 (seed + layer each, Zipf-skewed routing) resident expert parallel, 160/N experts of
@@ -358,7 +360,8 @@ def run_ep_qwen3(args, world: int, rank: int, local: int, tflops: float) -> dict
     torch.cuda.synchronize()
     del blob
     torch.cuda.empty_cache()
-    ep = ExpertParallelMoe(ops)
+    # the 1-token decode uses the fixed-capacity exchange, the prefill the exact one
+    ep = ExpertParallelMoe(ops, padded_tokens=1 if args.ep_exchange == "padded" else 0)
     gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
     res = {}
     for T in (1, 8192):
@@ -402,7 +405,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     torch.cuda.synchronize()
     del blob
     torch.cuda.empty_cache()
-    ep = ExpertParallelMoe(ops)
+    ep = ExpertParallelMoe(ops, padded_tokens=T if args.ep_exchange == "padded" else 0)
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
     x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
 
@@ -457,6 +460,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "config": {"workload": "BASELINE config 1 shape, expert parallel",
                        "tokens_per_rank": T, "experts_per_rank": e_loc,
                        "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)",
+                       "exchange": _exchange_name(args.ep_exchange),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (rank 0)",
                          "achieved": layer_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
@@ -466,9 +470,10 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
                     "h2d_bytes_per_step": T * GLM["hidden"] * 4,
                     "d2h_bytes_per_step": T * GLM["hidden"] * 4, "ms_per_step": e2e_s * 1e3},
             "cpu_baseline": None,
-            # per forward: router, tail, dispatch, send metadata; hist, scan, scatter,
-            # gather, two GEMMs (experts); scan, two GEMMs (shared); combine
-            "gpu_launches": 14 * args.steps,
+            # per forward: router, tail, dispatch (+ send metadata on the exact
+            # exchange); hist, scan, scatter, gather, two GEMMs (experts); scan, two
+            # GEMMs (shared); combine
+            "gpu_launches": (13 if args.ep_exchange == "padded" else 14) * args.steps,
             "clocks": clocks,
             "other_configs": other,
         }))
@@ -476,6 +481,11 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
         ops.close()
     dist.barrier()
     dist.destroy_process_group()
+
+
+def _exchange_name(kind: str) -> str:
+    return ("fixed-capacity (one all-to-all of equal row blocks each way, no host sync)"
+            if kind == "padded" else "exact (counts, then rows and ids; one host sync)")
 
 
 # ------------------------------------------------------------------ 89-layer stack (N > 1)
@@ -519,7 +529,8 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "vs_baseline": None,
             "config": {"workload": "BASELINE config 4", "layers": L, "global_tokens": batches,
                        "experts_per_rank": E // world if world else None,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/return)"}}
+                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/return)",
+                       "exchange": {"decode": _exchange_name(args.ep_exchange), "prefill": "exact"}}}
     if world < 2 or E % world or any(t % world for t in batches.values()):
         if rank == 0:
             print(json.dumps({**head, "unavailable":
@@ -559,7 +570,9 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
         ops.bind_device(blob.data_ptr(), blob.numel(), meta)
         torch.cuda.synchronize()
         del blob
-        layers.append((ops, ExpertParallelMoe(ops)))
+        # decode batches take the fixed-capacity exchange, prefill the exact one
+        layers.append((ops, ExpertParallelMoe(
+            ops, padded_tokens=t_dec if args.ep_exchange == "padded" else 0)))
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
 
@@ -621,7 +634,9 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
                                   "weights quantised per row; Zipf(1.1) router bias)",
                           "resident_gib_per_gpu": resident / 2**30, "build_s": build_s,
                           "workloads": results, "clocks": clocks,
-                          "gpu_launches_per_layer": 14}))
+                          "gpu_launches_per_layer": {
+                              "decode": 13 if args.ep_exchange == "padded" else 14,
+                              "prefill": 20}}))
     for ops, _ep in layers:
         ops.close()
     dist.barrier()
@@ -845,6 +860,8 @@ def main() -> None:
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
+    ap.add_argument("--ep-exchange", choices=["padded", "exact"], default="padded",
+                    help="N > 1 decode batches: fixed-capacity or exact all-to-all")
     ap.add_argument("--stack", action="store_true",
                     help="BASELINE config 4: resident INT8 layer stack, expert parallel (N >= 2)")
     ap.add_argument("--stack-layers", type=int, default=89)

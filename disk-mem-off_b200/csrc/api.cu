@@ -1,6 +1,8 @@
 // C ABI of libmoe_sm100 (declarations and reference citations: include/moe_sm100.h).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -160,9 +162,12 @@ WsLayout ws_layout(const Plan& p, int T) {
 }
 
 // Expert side of the expert-parallel path: R received rows grouped by the
-// n_local resident experts, no router, no shared expert.
-WsLayout ws_layout_ep_experts(const Plan& p, int R) {
-  const int per_expert = (2 * R + p.n_local - 1) / (p.n_local > 0 ? p.n_local : 1);
+// n_local resident experts, no router, no shared expert.  The token tile width
+// follows the rows expected to be valid (`expect`: all R for the exact
+// exchange, one rank's capacity for the fixed-capacity one), the buffers the
+// worst case of R.
+WsLayout ws_layout_ep_experts(const Plan& p, int R, int expect) {
+  const int per_expert = (2 * expect + p.n_local - 1) / (p.n_local > 0 ? p.n_local : 1);
   return ws_layout_general(p, R, 1, p.n_local, 0, pick_bn(per_expert > 0 ? per_expert : 1), false);
 }
 
@@ -741,7 +746,7 @@ int moe_ep_dispatch(MoePlan* plan, const float* x_dev, int32_t T, void* send_row
 
 uint64_t moe_ep_workspace_bytes(const MoePlan* plan, int32_t R) {
   if (!plan || R <= 0) return 0;
-  return ws_layout_ep_experts(plan->p, R).total;
+  return ws_layout_ep_experts(plan->p, R, R).total;
 }
 
 int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_experts, int32_t R,
@@ -749,13 +754,83 @@ int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_exp
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
   Plan& p = plan->p;
   int rc = check_ep(plan, R, workspace, workspace_bytes,
-                    R > 0 ? ws_layout_ep_experts(p, R).total : 0);
+                    R > 0 ? ws_layout_ep_experts(p, R, R).total : 0);
   if (rc != MOE_OK || R == 0) return rc;
   if (!recv_rows || !recv_experts || !y_out) return fail(MOE_ERR_INVALID, "null argument");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const WsLayout L = ws_layout_ep_experts(p, R);
+  const WsLayout L = ws_layout_ep_experts(p, R, R);
   char* ws = static_cast<char*>(workspace);
-  MOE_CUDA(launch_group_rows(p, L, ws, recv_experts, static_cast<const __half*>(recv_rows), R, s));
+  MOE_CUDA(launch_group_rows(p, L, ws, recv_experts, 1, false, static_cast<const __half*>(recv_rows),
+                             p.H, R, s));
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr, p.n_local}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true,
+                       GemmIO{R, 0, static_cast<__half*>(y_out),
+                              reinterpret_cast<const int32_t*>(ws + L.perm), p.n_local},
+                       s));
+  return MOE_OK;
+}
+
+int32_t moe_ep_capacity(const MoePlan* plan, int32_t T) {
+  if (!plan || T <= 0 || plan->p.E == 0) return 0;
+  const int64_t c = static_cast<int64_t>(T) * std::min(plan->p.K, plan->p.n_local);
+  return c > INT32_MAX ? 0 : static_cast<int32_t>(c);
+}
+
+// Rows a fixed-capacity exchange moves per rank: world * cap, or 0 if that
+// overflows an int32 row count.
+static int64_t padded_rows(const Plan& p, int32_t cap) {
+  return static_cast<int64_t>(p.E / std::max(p.n_local, 1)) * cap;
+}
+
+int moe_ep_dispatch_padded(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap,
+                           void* send_rows, void* workspace, uint64_t workspace_bytes,
+                           void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T above max_tokens");
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK) return rc;
+  if (cap <= 0 || cap < moe_ep_capacity(plan, T) || padded_rows(p, cap) > INT32_MAX)
+    return fail(MOE_ERR_INVALID, "cap below moe_ep_capacity(plan, T) or too large");
+  if (!send_rows || (T > 0 && !x_dev)) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(send_rows) || (T > 0 && misaligned16(x_dev)))
+    return fail(MOE_ERR_INVALID, "x and send_rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  WsLayout L{};
+  if (T > 0) {
+    L = ws_layout(p, T);
+    MOE_CUDA(launch_route(p, L, ws, x_dev, T, false, s, nullptr));
+  }
+  MOE_CUDA(launch_ep_pack(p, L, ws, x_dev, T, cap, static_cast<__half*>(send_rows), s));
+  return MOE_OK;
+}
+
+uint64_t moe_ep_padded_workspace_bytes(const MoePlan* plan, int32_t cap) {
+  if (!plan || cap <= 0 || plan->p.E == 0) return 0;
+  const int64_t R = padded_rows(plan->p, cap);
+  if (R > INT32_MAX) return 0;
+  return ws_layout_ep_experts(plan->p, static_cast<int>(R), cap).total;
+}
+
+int moe_ep_experts_padded(MoePlan* plan, const void* recv_rows, int32_t cap, void* y_out,
+                          void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (cap < 0 || padded_rows(p, cap) > INT32_MAX) return fail(MOE_ERR_INVALID, "bad cap");
+  const int R = static_cast<int>(padded_rows(p, cap));
+  int rc = check_ep(plan, R, workspace, workspace_bytes,
+                    R > 0 ? ws_layout_ep_experts(p, R, cap).total : 0);
+  if (rc != MOE_OK || R == 0) return rc;
+  if (!recv_rows || !y_out) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(recv_rows)) return fail(MOE_ERR_INVALID, "recv_rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout_ep_experts(p, R, cap);
+  char* ws = static_cast<char*>(workspace);
+  const __half* rows = static_cast<const __half*>(recv_rows);
+  // the local expert id is the first int32 of each row's 16-byte tail
+  const int32_t* keys = reinterpret_cast<const int32_t*>(rows + p.H);
+  MOE_CUDA(launch_group_rows(p, L, ws, keys, (p.H + 8) / 2, true, rows, p.H + 8, R, s));
   MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr, p.n_local}, s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
                        GemmIO{R, 0, static_cast<__half*>(y_out),

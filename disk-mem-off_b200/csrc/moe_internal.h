@@ -138,7 +138,7 @@ struct WsLayout {
 };
 
 WsLayout ws_layout(const Plan& p, int T);
-WsLayout ws_layout_ep_experts(const Plan& p, int R);
+WsLayout ws_layout_ep_experts(const Plan& p, int R, int expect);
 
 // Router launch geometry: rx router-row tiles x splits K-splits x tz token tiles.
 struct RouterGeom {
@@ -158,7 +158,12 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 // (stable: receive order inside an expert), gather them into L.xg and build the
 // tile lists; and the tile lists of the shared expert alone for T local tokens.
 cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
-                              const __half* rows, int n, cudaStream_t s);
+                              int key_stride, bool padded, const __half* rows, int row_ld, int n,
+                              cudaStream_t s);
+// Fixed-capacity send rows of the expert-parallel exchange (after launch_route
+// without dispatch): [world * cap] rows of H + 8 f16, tails carrying local ids.
+cudaError_t launch_ep_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                           int cap, __half* send, cudaStream_t s);
 cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
 cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                             cudaStream_t s);

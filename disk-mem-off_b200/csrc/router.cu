@@ -804,8 +804,11 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
 // ------------------------------------------------------------------ prefill permutation
 // Per chunk of 1024 tokens: a bitmask per expert, written to global with its
 // popcount histogram; a single-CTA scan; then one thread per (token, slot).
+// Key q sits at ids[q * key_stride]; with allow_pad a negative key marks an
+// unused row (fixed-capacity exchange) and is skipped.
 __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restrict__ ids, int T,
-                                                         int K, int E, uint32_t* __restrict__ bmg,
+                                                         int K, int E, int key_stride, int allow_pad,
+                                                         uint32_t* __restrict__ bmg,
                                                          int32_t* __restrict__ hist, int* err) {
   pdl_enter();
   extern __shared__ uint32_t bm[];  // [E][32]
@@ -816,7 +819,8 @@ __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restri
   __syncthreads();
   for (int q = threadIdx.x; q < tcnt * K; q += blockDim.x) {
     const int tl = q / K;
-    const int e = ids[static_cast<size_t>(tbeg) * K + q];
+    const int e = ids[(static_cast<size_t>(tbeg) * K + q) * key_stride];
+    if (e < 0 && allow_pad) continue;
     if (e < 0 || e >= E) {
       record_error(err, DEV_BAD_ROUTE);
       continue;
@@ -860,13 +864,13 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
 __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __restrict__ ids,
                                                            const uint32_t* __restrict__ bmg,
                                                            const int32_t* __restrict__ base,
-                                                           int T, int K, int E,
+                                                           int T, int K, int E, int key_stride,
                                                            int32_t* __restrict__ perm,
                                                            int32_t* __restrict__ slot_row) {
   pdl_enter();
   for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < T * K; q += gridDim.x * blockDim.x) {
     const int t = q / K;
-    const int e = ids[q];
+    const int e = ids[static_cast<size_t>(q) * key_stride];
     if (e < 0 || e >= E) continue;  // reported by perm_hist_kernel
     const int c = t / kPermChunk, tl = t % kPermChunk;
     const uint32_t* row = bmg + (static_cast<size_t>(c) * E + e) * 32;
@@ -878,13 +882,18 @@ __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __rest
   }
 }
 
-// dst[r] = src[perm[r] / div] for f16 rows of H elements (one CTA per row).
+// dst[r] = src[perm[r] / div] for f16 rows of H elements, source rows src_ld
+// elements apart (one CTA per row); rows from *nvalid on are left alone when
+// nvalid is given (only that many perm entries exist).
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ src,
                                                           const int32_t* __restrict__ perm, int n,
-                                                          int H, int div, __half* __restrict__ dst) {
+                                                          int H, int src_ld, int div,
+                                                          const int32_t* __restrict__ nvalid,
+                                                          __half* __restrict__ dst) {
   pdl_enter();
+  if (nvalid) n = min(n, *nvalid);
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
-    const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r] / div) * H);
+    const uint4* in = reinterpret_cast<const uint4*>(src + static_cast<size_t>(perm[r] / div) * src_ld);
     uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * H);
     for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
   }
@@ -974,9 +983,28 @@ cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, 
 bool route_uses_tc_router(const Plan& p, int T) { return p.router_tc && !route_uses_tail(p, T); }
 
 // ------------------------------------------------------------------ dispatch
+// dst = f16(w * (x_row / rms)) over H elements, spread over the CTA's threads, 8
+// elements per thread per step (the same roundings wherever a row is built).
+MOE_DEV void norm_row_f16(const float* __restrict__ x_row, const float* __restrict__ wn, float rms,
+                          int H, __half* __restrict__ dst) {
+  const float inv = 1.0f / rms;
+  const float4* xr = reinterpret_cast<const float4*>(x_row);
+  const float4* wr = reinterpret_cast<const float4*>(wn);
+  for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) {
+    const float4 a0 = xr[2 * v], a1 = xr[2 * v + 1];
+    const float4 g0 = wr[2 * v], g1 = wr[2 * v + 1];
+    __half2 o[4];
+    o[0] = __floats2half2_rn(g0.x * (a0.x * inv), g0.y * (a0.y * inv));
+    o[1] = __floats2half2_rn(g0.z * (a0.z * inv), g0.w * (a0.w * inv));
+    o[2] = __floats2half2_rn(g1.x * (a1.x * inv), g1.y * (a1.y * inv));
+    o[3] = __floats2half2_rn(g1.z * (a1.z * inv), g1.w * (a1.w * inv));
+    reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<uint4*>(o);
+  }
+}
+
 // Rows [0, T*K): xg[r] = f16(w * (x[token(r)] / rms)); rows [T*K, T*K+T): h16[t]
 // for the shared expert.  One CTA per row (decode batches have few rows, so
-// the row itself is spread over 256 threads), 8 elements per thread per step.
+// the row itself is spread over 256 threads).
 __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__ x,
                                                        const float* __restrict__ wn,
                                                        const float* __restrict__ rms,
@@ -996,18 +1024,54 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const float* __restrict__
       t = r - T * K;
       dst = h16 + static_cast<size_t>(t) * H;
     }
-    const float inv = 1.0f / rms[t];
-    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
-    const float4* wr = reinterpret_cast<const float4*>(wn);
-    for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) {
-      const float4 a0 = xr[2 * v], a1 = xr[2 * v + 1];
-      const float4 g0 = wr[2 * v], g1 = wr[2 * v + 1];
-      __half2 o[4];
-      o[0] = __floats2half2_rn(g0.x * (a0.x * inv), g0.y * (a0.y * inv));
-      o[1] = __floats2half2_rn(g0.z * (a0.z * inv), g0.w * (a0.w * inv));
-      o[2] = __floats2half2_rn(g1.x * (a1.x * inv), g1.y * (a1.y * inv));
-      o[3] = __floats2half2_rn(g1.z * (a1.z * inv), g1.w * (a1.w * inv));
-      reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<uint4*>(o);
+    norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H, dst);
+  }
+}
+
+// Fixed-capacity send buffer of the expert-parallel exchange: destination rank d
+// owns rows [d*cap, (d+1)*cap), each H f16 values and a 16-byte tail whose first
+// int32 is the expert id local to d, or -1 for an unused row.  The j-th routed row
+// for d (expert-major order, as dispatch_kernel would write it) lands at d*cap + j
+// and slot_row records that position for combine.  Rows from world*cap on build
+// h16 (shared expert) when with_shared.  Source: x normalised here, or the f16
+// rows h16src (prefill routing already built them).
+__global__ void __launch_bounds__(256) ep_pack_kernel(
+    const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ rms,
+    const __half* __restrict__ h16src, const int32_t* __restrict__ perm,
+    const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets, int T, int K, int H,
+    int e_loc, int world, int cap, int with_shared, __half* __restrict__ send,
+    int32_t* __restrict__ slot_row, __half* __restrict__ h16, int* err) {
+  pdl_enter();
+  const size_t ld = static_cast<size_t>(H) + 8;
+  const int padded_rows = world * cap;
+  const int rows = padded_rows + (with_shared ? T : 0);
+  for (int pr = blockIdx.x; pr < rows; pr += gridDim.x) {
+    if (pr >= padded_rows) {
+      const int t = pr - padded_rows;
+      norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H, h16 + static_cast<size_t>(t) * H);
+      continue;
+    }
+    const int d = pr / cap, j = pr - d * cap;
+    const int beg = T > 0 ? offsets[d * e_loc] : 0;
+    const int cnt = T > 0 ? offsets[(d + 1) * e_loc] - beg : 0;  // <= cap (host check)
+    if (j == 0 && cnt > cap && threadIdx.x == 0) record_error(err, DEV_BAD_TILE);
+    __half* row = send + static_cast<size_t>(pr) * ld;
+    if (j >= cnt) {
+      if (threadIdx.x == 0) *reinterpret_cast<int4*>(row + H) = make_int4(-1, 0, 0, 0);
+      continue;
+    }
+    const int q = perm[beg + j];
+    const int t = q / K;
+    if (threadIdx.x == 0) {
+      *reinterpret_cast<int4*>(row + H) = make_int4(ids[q] - d * e_loc, 0, 0, 0);
+      slot_row[q] = pr;
+    }
+    if (h16src) {
+      const uint4* in = reinterpret_cast<const uint4*>(h16src + static_cast<size_t>(t) * H);
+      uint4* out = reinterpret_cast<uint4*>(row);
+      for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
+    } else {
+      norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H, row);
     }
   }
 }
@@ -1182,7 +1246,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
                        done_hist);
     if (st != cudaSuccess) return st;
     MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
-        ids, T, K, E, bmg, hist, p.d_err);
+        ids, T, K, E, 1, 0, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, hist, L.nchunks, base, offsets, ta);
@@ -1190,13 +1254,13 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
     if (st != cudaSuccess) return st;
     const int entries = T * K;
     MOE_PDL(perm_scatter_kernel, dim3(min((entries + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, 
-        ids, bmg, base, T, K, E, perm, slot_row);
+        ids, bmg, base, T, K, E, 1, perm, slot_row);
   }
   st = cudaGetLastError();
   if (st != cudaSuccess || !dispatch) return st;
   if (tc) {  // h16 already holds the normalised rows: gather them per slot
     MOE_PDL(gather_rows_kernel, dim3(min(T * K, p.num_sms * 16)), dim3(256), 0, s, 
-        reinterpret_cast<const __half*>(ws + L.h16), perm, T * K, p.H, K,
+        reinterpret_cast<const __half*>(ws + L.h16), perm, T * K, p.H, p.H, K, nullptr,
         xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg));
     return cudaGetLastError();
   }
@@ -1209,7 +1273,8 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 
 // ------------------------------------------------------------------ expert-parallel helpers
 cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
-                              const __half* rows, int n, cudaStream_t s) {
+                              int key_stride, bool padded, const __half* rows, int row_ld, int n,
+                              cudaStream_t s) {
   const int E = p.n_local;
   uint32_t* bmg = reinterpret_cast<uint32_t*>(ws + L.bm);
   int32_t* hist = reinterpret_cast<int32_t*>(ws + L.hist);
@@ -1224,7 +1289,7 @@ cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const 
   if (st != cudaSuccess) return st;
   if (n > 0) {
     MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
-        keys, n, 1, E, bmg, hist, p.d_err);
+        keys, n, 1, E, key_stride, padded ? 1 : 0, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
   }
@@ -1232,11 +1297,29 @@ cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const 
   st = cudaGetLastError();
   if (st != cudaSuccess || n == 0) return st;
   MOE_PDL(perm_scatter_kernel, dim3(min((n + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, keys, bmg, base, n, 1, E,
-                                                                         perm, slot_row);
+                                                                         key_stride, perm, slot_row);
   st = cudaGetLastError();
   if (st != cudaSuccess) return st;
-  MOE_PDL(gather_rows_kernel, dim3(min(n, p.num_sms * 8)), dim3(256), 0, s, rows, perm, n, p.H, 1,
-                                                          reinterpret_cast<__half*>(ws + L.xg));
+  MOE_PDL(gather_rows_kernel, dim3(min(n, p.num_sms * 8)), dim3(256), 0, s, rows, perm, n, p.H,
+          row_ld, 1, padded ? offsets + E : nullptr, reinterpret_cast<__half*>(ws + L.xg));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                           int cap, __half* send, cudaStream_t s) {
+  // T == 0: every row is unused (the kernel reads nothing of the workspace)
+  const bool tc = T > 0 && route_uses_tc_router(p, T);
+  const int world = p.E / p.n_local;
+  const int with_shared = (T > 0 && !tc && p.SI > 0) ? 1 : 0;
+  const int rows = world * cap + (with_shared ? T : 0);
+  auto at = [&](size_t off) { return T > 0 ? ws + off : nullptr; };
+  MOE_PDL(ep_pack_kernel, dim3(min(rows, p.num_sms * 8)), dim3(256), 0, s, x, p.w.norm_w,
+          reinterpret_cast<const float*>(at(L.rms)),
+          tc ? reinterpret_cast<const __half*>(at(L.h16)) : nullptr,
+          reinterpret_cast<const int32_t*>(at(L.perm)), reinterpret_cast<const int32_t*>(at(L.ids)),
+          reinterpret_cast<const int32_t*>(at(L.offsets)), T, p.K, p.H, p.n_local, world, cap,
+          with_shared, send, reinterpret_cast<int32_t*>(at(L.slot_row)),
+          reinterpret_cast<__half*>(at(L.h16)), p.d_err);
   return cudaGetLastError();
 }
 

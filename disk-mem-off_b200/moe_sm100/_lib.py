@@ -85,6 +85,12 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_ep_shared": (c_int32, [c_void_p, c_int32, c_void_p, c_uint64, c_void_p]),
     "moe_ep_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p,
                                  c_uint64, c_void_p]),
+    "moe_ep_capacity": (c_int32, [c_void_p, c_int32]),
+    "moe_ep_dispatch_padded": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                                         c_uint64, c_void_p]),
+    "moe_ep_padded_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
+    "moe_ep_experts_padded": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_uint64,
+                                        c_void_p]),
     "moe_status": (c_int32, [c_void_p, c_void_p]),
     "moe_last_error": (c_char_p, []),
     "moe_version": (c_char_p, []),

@@ -14,6 +14,13 @@ own tokens.  One forward (weak scaling: T tokens per rank):
   5. return     all_to_all of the f16 expert outputs back to their source rank
   6. combine    x + sum_k w * y + shared expert
 
+Small batches can instead use the fixed-capacity exchange (``padded_tokens``): every
+rank sends every rank exactly ``cap`` rows (cap = the most rows one batch of
+``padded_tokens`` tokens can route to one rank), the local expert id travels in
+each row's tail (-1 marks an unused row), and steps 2-3 become one all_to_all of
+equal splits.  No counts cross and the host never waits, so the CPU runs ahead of
+the device across layers; the price is moving cap rows per rank pair.
+
 The exchanges are torch.distributed collectives (NCCL over NVLink on B200; gloo
 on CPU in the tests).  The device work is libmoe_sm100's moe_ep_* entry points.
 """
@@ -44,17 +51,26 @@ class EPOps(Protocol):
 
 
 class ExpertParallelMoe:
-    """Runs the dispatch / expert / combine protocol of one rank."""
+    """Runs the dispatch / expert / combine protocol of one rank.
 
-    def __init__(self, ops: EPOps, group: Any = None) -> None:
+    ``padded_tokens`` > 0 switches batches of at most that many tokens to the
+    fixed-capacity exchange (ops must provide ``capacity``, ``dispatch_padded`` and
+    ``experts_padded``).  Every rank must take the same branch in the same forward:
+    give all ranks the same ``padded_tokens`` and batches on the same side of it
+    (decode steps below, prefill above).
+    """
+
+    def __init__(self, ops: EPOps, group: Any = None, padded_tokens: int = 0) -> None:
         self.ops = ops
         self.group = group
         self.last_timing: dict[str, float] = {}
+        self.padded_tokens = int(padded_tokens)
+        self.cap = int(ops.capacity(self.padded_tokens)) if self.padded_tokens > 0 else 0
+        if self.padded_tokens > 0 and self.cap <= 0:
+            raise ValueError("no fixed capacity for padded_tokens")
 
     def forward(self, x: Any, timed: bool = False) -> Any:
         torch = _torch()
-        import torch.distributed as dist
-        g = self.group
         ev = {}
 
         def mark(name: str) -> None:
@@ -63,6 +79,56 @@ class ExpertParallelMoe:
                 e.record()
                 ev[name] = e
 
+        if 0 < self.padded_tokens and x.shape[0] <= self.padded_tokens:
+            out, n_recv = self._forward_padded(x, mark)
+        else:
+            out, n_recv = self._forward_exact(x, mark)
+        if timed and x.is_cuda:
+            torch.cuda.synchronize()
+            t = lambda a, b: ev[a].elapsed_time(ev[b])  # noqa: E731
+            self.last_timing = {
+                "dispatch_ms": t("start", "dispatched"),
+                "a2a_ms": t("dispatched", "exchanged") + t("computed", "returned"),
+                "experts_ms": t("exchanged", "computed"),
+                "combine_ms": t("returned", "end"),
+                "total_ms": t("start", "end"),
+            }
+            self.last_timing.update(n_recv())
+        return out
+
+    def _forward_padded(self, x: Any, mark: Any) -> tuple[Any, Any]:
+        torch = _torch()
+        import torch.distributed as dist
+        g, cap = self.group, self.cap
+        mark("start")
+        send = self.ops.dispatch_padded(x, cap)
+        mark("dispatched")
+        start_shared = getattr(self.ops, "start_shared", None)
+        if start_shared is not None:
+            start_shared(x)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=g)
+        mark("exchanged")
+        y = self.ops.experts_padded(recv, cap)
+        mark("computed")
+        y_back = torch.empty_like(y)
+        dist.all_to_all_single(y_back, y, group=g)
+        mark("returned")
+        out = self.ops.combine(x, y_back)
+        mark("end")
+
+        def counts() -> dict[str, float]:
+            ids = self.ops.padded_ids(recv)
+            valid = ids[ids >= 0]
+            return {"recv_rows": int(valid.numel()),
+                    "recv_experts": int(torch.unique(valid).numel()) if valid.numel() else 0,
+                    "exchanged_rows": int(recv.shape[0])}
+        return out, counts
+
+    def _forward_exact(self, x: Any, mark: Any) -> tuple[Any, Any]:
+        torch = _torch()
+        import torch.distributed as dist
+        g = self.group
         mark("start")
         send_rows, send_experts, send_offsets = self.ops.dispatch(x)
         mark("dispatched")
@@ -96,19 +162,12 @@ class ExpertParallelMoe:
         mark("returned")
         out = self.ops.combine(x, y_back)
         mark("end")
-        if timed and x.is_cuda:
-            torch.cuda.synchronize()
-            t = lambda a, b: ev[a].elapsed_time(ev[b])  # noqa: E731
-            self.last_timing = {
-                "dispatch_ms": t("start", "dispatched"),
-                "a2a_ms": t("dispatched", "exchanged") + t("computed", "returned"),
-                "experts_ms": t("exchanged", "computed"),
-                "combine_ms": t("returned", "end"),
-                "total_ms": t("start", "end"),
-                "recv_rows": n_recv,
-                "recv_experts": int(torch.unique(recv_experts).numel()) if n_recv else 0,
-            }
-        return out
+
+        def counts() -> dict[str, float]:
+            return {"recv_rows": n_recv,
+                    "recv_experts": int(torch.unique(recv_experts).numel()) if n_recv else 0,
+                    "exchanged_rows": n_recv}
+        return out, counts
 
 
 class DeviceEPOps:
@@ -165,6 +224,38 @@ class DeviceEPOps:
                                     c_void_p(_stream_handle(None))))
         self._T = t
         return rows, experts, offsets
+
+    def capacity(self, tokens: int) -> int:
+        """Rows one rank may have to send one destination for `tokens` tokens."""
+        return int(lib().moe_ep_capacity(self.layer._plan, int(tokens)))
+
+    def dispatch_padded(self, x: Any, cap: int) -> Any:
+        torch = _torch()
+        t = x.shape[0]
+        plan = self.layer._plan
+        ws = self._buf("ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
+        send = torch.empty((self.world * cap, self.cfg.hidden + 8), dtype=torch.float16,
+                           device=x.device)
+        check(lib().moe_ep_dispatch_padded(plan, c_void_p(x.data_ptr()), t, cap,
+                                           c_void_p(send.data_ptr()), c_void_p(ws.data_ptr()),
+                                           ws.numel(), c_void_p(_stream_handle(None))))
+        self._T = t
+        return send
+
+    def experts_padded(self, recv: Any, cap: int) -> Any:
+        torch = _torch()
+        plan = self.layer._plan
+        y = torch.empty((recv.shape[0], self.cfg.hidden), dtype=torch.float16, device=recv.device)
+        ws = self._buf("ws_ep", int(lib().moe_ep_padded_workspace_bytes(plan, cap)))
+        check(lib().moe_ep_experts_padded(plan, c_void_p(recv.data_ptr()), cap, c_void_p(y.data_ptr()),
+                                          c_void_p(ws.data_ptr()), ws.numel(),
+                                          c_void_p(_stream_handle(None))))
+        return y
+
+    def padded_ids(self, recv: Any) -> Any:
+        """Local expert id of every received row (-1: unused), from the row tails."""
+        h = self.cfg.hidden
+        return recv[:, h:h + 8].contiguous().view(_torch().int32)[:, 0]
 
     def experts(self, rows: Any, expert_ids: Any) -> Any:
         torch = _torch()

@@ -191,6 +191,31 @@ int moe_ep_shared(MoePlan* plan, int32_t T, void* workspace, uint64_t workspace_
 int moe_ep_combine(MoePlan* plan, const float* x_dev, int32_t T, const void* y_back,
                    float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Fixed-capacity exchange (no host synchronisation; for small batches).  Every
+ * rank sends every other rank exactly `cap` rows, so the exchange sizes are known
+ * in advance and no counts cross first: one all-to-all of equal splits each way,
+ * which a caller may also capture in a CUDA graph.  All ranks use the same cap,
+ * at least moe_ep_capacity(plan, T) of their largest T (T * min(top_k, experts
+ * per rank): no rank can then overflow a destination's share).
+ *   1. moe_ep_dispatch_padded: route; send_rows [world*cap, H + 8] f16, rows
+ *      [d*cap, (d+1)*cap) for rank d: H normalised values, then a 16-byte tail
+ *      whose first int32 is the expert id local to d, or -1 for an unused row.
+ *      Writes every row's tail (T = 0 included: all unused).  Workspace as for
+ *      moe_ep_dispatch.
+ *   2. caller: all-to-all of send_rows in equal splits of cap rows.
+ *   3. moe_ep_experts_padded: the resident experts on the world*cap received rows
+ *      (unused rows skipped); y_out [world*cap, H] f16 answers row r in place
+ *      (unused rows untouched).  Workspace moe_ep_padded_workspace_bytes(plan, cap).
+ *   4. caller: all-to-all of y_out back, equal splits of cap rows.
+ *   5. moe_ep_shared and moe_ep_combine as above, y_back [world*cap, H]. */
+int32_t moe_ep_capacity(const MoePlan* plan, int32_t T);
+int moe_ep_dispatch_padded(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap,
+                           void* send_rows, void* workspace, uint64_t workspace_bytes,
+                           void* stream);
+uint64_t moe_ep_padded_workspace_bytes(const MoePlan* plan, int32_t cap);
+int moe_ep_experts_padded(MoePlan* plan, const void* recv_rows, int32_t cap, void* y_out,
+                          void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Synchronise `stream`, then read and clear the device error word of the plan.
  * Returns MOE_OK, MOE_ERR_TIMEOUT or MOE_ERR_DEVICE. */
 int moe_status(MoePlan* plan, void* stream);

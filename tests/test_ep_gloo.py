@@ -1,7 +1,8 @@
 """Expert-parallel protocol on CPU ranks (gloo, world size 2).
 
 moe_sm100.ep.ExpertParallelMoe is the product code that exchanges row counts,
-rows, local expert ids and expert outputs between ranks.  Here each rank plugs
+rows, local expert ids and expert outputs between ranks (exact exchange), or
+fixed-capacity row blocks with the ids in their tails (padded exchange).  Here each rank plugs
 in oracle-based stand-ins for the device ops, so the test checks the protocol
 itself (splits, ordering, reverse exchange, combine indexing) against the
 single-process oracle, and that malformed dispatch output fails on the host
@@ -40,14 +41,20 @@ class OracleEPOps:
         return (silu(x @ t[prefix + "gate_proj.weight"].T) * (x @ t[prefix + "up_proj.weight"].T)) @ \
             t[prefix + "down_proj.weight"].T
 
-    def dispatch(self, x: torch.Tensor):  # noqa: ANN201
+    def _route(self, x: torch.Tensor):  # noqa: ANN202
         cfg, t = self.cfg, self.t
-        xn = x.numpy()
-        h = rms_norm(xn, t["post_attention_layernorm.weight"], cfg.eps)
+        h = rms_norm(x.numpy(), t["post_attention_layernorm.weight"], cfg.eps)
         bias = t.get("mlp.gate.e_score_correction_bias") if cfg.use_bias else None
         ids, w, _ = route(h, t["mlp.gate.weight"], bias, cfg)
         offsets, perm = permutation(ids, cfg.n_experts)
-        self.state = (h, w, perm)
+        return h, w, ids, offsets, perm
+
+    def dispatch(self, x: torch.Tensor):  # noqa: ANN201
+        cfg = self.cfg
+        h, w, ids, offsets, perm = self._route(x)
+        slot_row = np.empty_like(perm)
+        slot_row[perm] = np.arange(perm.size)
+        self.state = (h, w, slot_row)
         rows = h[perm // cfg.top_k].astype(np.float32)
         experts = (ids.reshape(-1)[perm] % self.e_loc).astype(np.int32)
         d = np.minimum(np.arange(self.world + 1) * self.e_loc, cfg.n_experts)
@@ -55,6 +62,44 @@ class OracleEPOps:
         if self.corrupt:
             send_offsets[-1] += 1
         return torch.from_numpy(rows), torch.from_numpy(experts), torch.from_numpy(send_offsets)
+
+    # fixed-capacity exchange: rows [world*cap, H + 1], the last column the local
+    # expert id (-1 unused) standing in for the device format's f16 row + tail
+    def capacity(self, tokens: int) -> int:
+        return tokens * min(self.cfg.top_k, self.e_loc)
+
+    def dispatch_padded(self, x: torch.Tensor, cap: int) -> torch.Tensor:
+        cfg = self.cfg
+        hdim = x.shape[1]
+        send = np.zeros((self.world * cap, hdim + 1), dtype=np.float32)
+        send[:, hdim] = -1
+        if x.shape[0] == 0:
+            self.state = (np.zeros((0, hdim), np.float32), np.zeros((0, cfg.top_k), np.float32),
+                          np.zeros(0, np.int64))
+            return torch.from_numpy(send)
+        h, w, ids, offsets, perm = self._route(x)
+        slot_row = np.empty_like(perm)
+        flat = ids.reshape(-1)
+        for d in range(self.world):
+            beg, end = offsets[d * self.e_loc], offsets[(d + 1) * self.e_loc]
+            assert end - beg <= cap
+            for j, r in enumerate(range(beg, end)):
+                q = perm[r]
+                send[d * cap + j, :hdim] = h[q // cfg.top_k]
+                send[d * cap + j, hdim] = flat[q] - d * self.e_loc
+                slot_row[q] = d * cap + j
+        self.state = (h, w, slot_row)
+        return torch.from_numpy(send)
+
+    def experts_padded(self, recv: torch.Tensor, cap: int) -> torch.Tensor:
+        r = recv.numpy()
+        hdim = r.shape[1] - 1
+        ids = r[:, hdim].astype(np.int64)
+        y = np.zeros((r.shape[0], hdim), dtype=np.float32)
+        for le in np.unique(ids[ids >= 0]):
+            sel = ids == le
+            y[sel] = self._swiglu(r[sel, :hdim], f"mlp.experts.{self.rank * self.e_loc + int(le)}.")
+        return torch.from_numpy(y)
 
     def experts(self, rows: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         r, e = rows.numpy(), ids.numpy()
@@ -66,10 +111,10 @@ class OracleEPOps:
         return torch.from_numpy(y)
 
     def combine(self, x: torch.Tensor, y_back: torch.Tensor) -> torch.Tensor:
-        h, w, perm = self.state
+        h, w, slot_row = self.state
         k = self.cfg.top_k
-        slot_row = np.empty_like(perm)
-        slot_row[perm] = np.arange(perm.size)
+        if h.shape[0] == 0:
+            return x.clone()
         yb = y_back.numpy()
         acc = np.zeros_like(h)
         for j in range(k):
@@ -83,7 +128,8 @@ class OracleEPOps:
         return torch.from_numpy(x.numpy() + acc)
 
 
-def _worker(rank: int, world: int, port: int, spec: CaseSpec, corrupt: bool, q) -> None:  # noqa: ANN001
+def _worker(rank: int, world: int, port: int, spec: CaseSpec, corrupt: bool, q,  # noqa: ANN001
+            padded_tokens: int = 0) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -94,11 +140,15 @@ def _worker(rank: int, world: int, port: int, spec: CaseSpec, corrupt: bool, q) 
         # weak scaling: each rank routes its own half of the tokens
         mine = np.array_split(np.arange(spec.tokens), world)[rank]
         xr = x[mine]
-        ep = ExpertParallelMoe(OracleEPOps(t, cfg, rank, world, corrupt=corrupt and rank == 0))
+        ep = ExpertParallelMoe(OracleEPOps(t, cfg, rank, world, corrupt=corrupt and rank == 0),
+                               padded_tokens=padded_tokens)
         try:
             out = ep.forward(torch.from_numpy(xr)).numpy()
         except ValueError as err:
             q.put((rank, "ValueError", str(err)))
+            return
+        if xr.shape[0] == 0:
+            q.put((rank, "ok", 0.0 if out.shape == xr.shape else 1.0))
             return
         ref, _ = moe_block(xr, t, cfg)
         err = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
@@ -113,11 +163,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(spec: CaseSpec, corrupt: bool = False) -> list:
+def _run(spec: CaseSpec, corrupt: bool = False, padded_tokens: int = 0) -> list:
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, spec, corrupt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, spec, corrupt, q, padded_tokens))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -141,3 +192,23 @@ def test_malformed_dispatch_fails_on_host_before_exchange() -> None:
     # rank 0 detects its own bad offsets and raises; rank 1 then finds its
     # count exchange partner gone and errors (or both raise) -- nobody hangs
     assert any(r[0] == 0 and r[1] == "ValueError" for r in res), res
+
+
+@pytest.mark.parametrize("spec", [SPEC, SPEC_QWEN], ids=["glm", "qwen3"])
+def test_fixed_capacity_exchange_matches_oracle(spec: CaseSpec) -> None:
+    """Padded exchange: equal splits of cap rows, ids in the row tails, unused rows
+    skipped by the experts and never read by combine."""
+    res = _run(spec, padded_tokens=spec.tokens)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    for _rank, _status, err in res:
+        assert err < 1e-5
+
+
+def test_fixed_capacity_exchange_with_an_empty_rank() -> None:
+    """One token over two ranks: rank 1 has no tokens, sends only unused rows and
+    still serves rank 0's rows for its experts."""
+    from dataclasses import replace
+    res = _run(replace(SPEC, tokens=1), padded_tokens=4)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    for _rank, _status, err in res:
+        assert err < 1e-5

@@ -3,7 +3,9 @@
 Two processes, one per GPU, each holding half of the routed experts.  Each rank
 compares its expert-parallel output with a single-GPU plan holding all experts
 on the same tokens: the only arithmetic difference is that expert outputs cross
-the exchange as f16, so the bound is the 16-bit parity tolerance.
+the exchange as f16, so the bound is the 16-bit parity tolerance.  Both exchanges
+run: exact (counts, then rows and ids) and fixed-capacity (equal row blocks, ids
+in the row tails).
 """
 from __future__ import annotations
 
@@ -52,15 +54,28 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
             torch.cuda.synchronize()
             del blob
             ep = ExpertParallelMoe(ops)
+            epp = ExpertParallelMoe(ops, padded_tokens=64)
             gen = torch.Generator(device=f"cuda:{rank}").manual_seed(100 + rank)
             for T in (1, 37, 300):
                 x = torch.randn((T, 2048), generator=gen, device=f"cuda:{rank}")
-                out = ep.forward(x)
                 ref = full.forward(x)
-                ops.status()
+                for mode, e in (("exact", ep), ("padded", epp)):
+                    out = e.forward(x)  # T = 300 > 64 takes the exact path in both
+                    ops.status()
+                    err = float((out.double() - ref.double()).norm() / ref.double().norm())
+                    results.append((family, mode, T, err))
                 full.status()
-                err = float((out.double() - ref.double()).norm() / ref.double().norm())
-                results.append((family, T, err))
+            # a capacity below the batch's worst case is refused on the host
+            from ctypes import c_void_p
+            from moe_sm100._lib import lib
+            x = torch.randn((8, 2048), generator=gen, device=f"cuda:{rank}")
+            send = torch.empty((2 * 8, 2048 + 8), dtype=torch.float16, device=f"cuda:{rank}")
+            ws = torch.empty(int(lib().moe_workspace_bytes(ops.layer._plan, 8)), dtype=torch.uint8,
+                             device=f"cuda:{rank}")
+            rc = lib().moe_ep_dispatch_padded(ops.layer._plan, c_void_p(x.data_ptr()), 8, 8,
+                                              c_void_p(send.data_ptr()), c_void_p(ws.data_ptr()),
+                                              ws.numel(), c_void_p(0))
+            results.append((family, "small_cap_rc", 8, 0.0 if rc != 0 else 1.0))
             ops.close()
             full.close()
         q.put((rank, results))
@@ -84,5 +99,5 @@ def test_expert_parallel_two_gpus_matches_single_gpu() -> None:
         assert p.exitcode == 0
     res = [q.get(timeout=10) for _ in procs]
     for _rank, rows in res:
-        for family, T, err in rows:
-            assert err <= TOL, (family, T, err)
+        for family, mode, T, err in rows:
+            assert err <= TOL, (family, mode, T, err)
