@@ -448,13 +448,17 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   }
 
   // ---- allocate the resident layout (once per plan; reused by later binds)
-  const size_t wel = p.int8 ? 1 : 2;
   size_t o = 0;
   auto take = [&](size_t b) { size_t at = o; o = align256(o + b); return at; };
-  const size_t o_w13 = take(static_cast<size_t>(NL) * 2 * I * H * wel);
-  const size_t o_w2 = take(static_cast<size_t>(NL) * H * I * wel);
-  const size_t o_ws13 = take(static_cast<size_t>(2) * SI * H * wel);
-  const size_t o_ws2 = take(static_cast<size_t>(H) * SI * wel);
+  // one expert matrix: f16 row-major, or int8 tile-major with its padding
+  auto mat_bytes = [&](int m, int k) {
+    return p.int8 ? i8_pad_rows(m) * i8_pad_cols(k) : static_cast<size_t>(m) * k * 2;
+  };
+  const size_t b13 = mat_bytes(2 * I, H), b2 = mat_bytes(H, I);
+  const size_t o_w13 = take(static_cast<size_t>(NL) * b13);
+  const size_t o_w2 = take(static_cast<size_t>(NL) * b2);
+  const size_t o_ws13 = take(mat_bytes(2 * SI, H));
+  const size_t o_ws2 = take(mat_bytes(H, SI));
   const size_t o_s13 = take(p.int8 ? static_cast<size_t>(NL) * 2 * I * 4 : 0);
   const size_t o_s2 = take(p.int8 ? static_cast<size_t>(NL) * H * 4 : 0);
   const size_t o_ss13 = take(p.int8 ? static_cast<size_t>(2) * SI * 4 : 0);
@@ -484,6 +488,8 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   int* range_err = reinterpret_cast<int*>(wb + o_flag);
   int* rw16_err = range_err + 1;
   MOE_CUDA(cudaMemsetAsync(range_err, 0, 2 * sizeof(int), s));
+  // int8 tiles are padded: zero the expert matrices before the packers fill them
+  if (p.int8) MOE_CUDA(cudaMemsetAsync(wb + o_w13, 0, o_s13 - o_w13, s));
 
   // ---- pack
   MOE_CUDA(launch_to_f32(norm.ptr, norm.dtype, p.w.norm_w, H, s));
@@ -497,8 +503,8 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
     const Src& g = ex[le * 3 + P_GATE];
     const Src& u = ex[le * 3 + P_UP];
     const Src& dn = ex[le * 3 + P_DOWN];
-    char* d13 = static_cast<char*>(p.w.w13) + static_cast<size_t>(le) * 2 * I * H * wel;
-    char* d2 = static_cast<char*>(p.w.w2) + static_cast<size_t>(le) * H * I * wel;
+    char* d13 = static_cast<char*>(p.w.w13) + static_cast<size_t>(le) * b13;
+    char* d2 = static_cast<char*>(p.w.w2) + static_cast<size_t>(le) * b2;
     float* s13 = p.int8 ? p.w.s13 + static_cast<size_t>(le) * 2 * I : nullptr;
     float* s2 = p.int8 ? p.w.s2 + static_cast<size_t>(le) * H : nullptr;
     if (g.dtype == SRC_I8 || u.dtype == SRC_I8) {
@@ -549,21 +555,21 @@ int moe_bind_layer(MoePlan* plan, const void* blob_dev, uint64_t blob_bytes,
   p.router_tc = h_range[1] == 0 &&
                 !(p.cfg.score_func == MOE_SCORE_SOFTMAX && !p.cfg.norm_topk_prob);
 
-  // ---- tensor maps over the resident weights
+  // ---- tensor maps over the resident f16 weights (int8 tiles are fetched as
+  // contiguous blocks straight from their tile-major layout)
   std::string err;
-  const bool i8 = p.int8;
-  const bool sw = !i8;  // f16 tiles are swizzled for the MMA; int8 tiles are staged plain
-  if (!make_tmap_2d(&p.tm_w13, p.w.w13, i8, H, static_cast<uint64_t>(NL) * 2 * I, kBK, kBM, sw, &err) ||
-      !make_tmap_2d(&p.tm_w2, p.w.w2, i8, I, static_cast<uint64_t>(NL) * H, kBK, kBM, sw, &err))
-    return fail(MOE_ERR_CUDA, err);
+  if (!p.int8) {
+    if (!make_tmap_2d(&p.tm_w13, p.w.w13, false, H, static_cast<uint64_t>(NL) * 2 * I, kBK, kBM, true, &err) ||
+        !make_tmap_2d(&p.tm_w2, p.w.w2, false, I, static_cast<uint64_t>(NL) * H, kBK, kBM, true, &err))
+      return fail(MOE_ERR_CUDA, err);
+    if (SI > 0 &&
+        (!make_tmap_2d(&p.tm_ws13, p.w.ws13, false, H, 2 * SI, kBK, kBM, true, &err) ||
+         !make_tmap_2d(&p.tm_ws2, p.w.ws2, false, SI, H, kBK, kBM, true, &err)))
+      return fail(MOE_ERR_CUDA, err);
+  }
   if (!make_tmap_2d(&p.tm_rw16, p.w.rw16, false, static_cast<uint64_t>(H), p.router_rows,
                     kBK, kBM, true, &err))
     return fail(MOE_ERR_CUDA, err);
-  if (SI > 0) {
-    if (!make_tmap_2d(&p.tm_ws13, p.w.ws13, i8, H, 2 * SI, kBK, kBM, sw, &err) ||
-        !make_tmap_2d(&p.tm_ws2, p.w.ws2, i8, SI, H, kBK, kBM, sw, &err))
-      return fail(MOE_ERR_CUDA, err);
-  }
   p.bound = true;
   return MOE_OK;
 }

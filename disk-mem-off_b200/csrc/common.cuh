@@ -117,6 +117,16 @@ MOE_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Contiguous bulk load global -> shared (this CTA): both addresses 16-byte aligned,
+// bytes a multiple of 16; completion counted in bytes on bar.
+MOE_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2D tiled load global -> shared (this CTA), completion counted in bytes on bar.
 // c0 is the innermost (K) coordinate in elements, c1 the row coordinate.
 MOE_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t c0, int32_t c1,

@@ -28,8 +28,14 @@
 namespace moe {
 
 struct GemmArgs {
-  CUtensorMap a_routed;  // weights: f16 or int8 [groups * rows_a][K]
-  CUtensorMap a_shared;  // shared expert weights [m_limit_shared][K]
+  CUtensorMap a_routed;  // f16 weights [groups * rows_a][K]
+  CUtensorMap a_shared;  // f16 shared expert weights [m_limit_shared][K]
+  // int8 weights, tile-major (i8_tile_off): a group's matrix a8_group_bytes long,
+  // a8_nkb_* 64-column tiles per 128-row tile
+  const int8_t* a8_routed;
+  const int8_t* a8_shared;
+  size_t a8_group_bytes;
+  int a8_nkb_routed, a8_nkb_shared;
   CUtensorMap b_routed;  // activations f16 [rows][K]
   CUtensorMap b_shared;
   TileMap map;           // routed / shared unit list (grouped GEMMs)
@@ -105,16 +111,20 @@ __host__ __device__ constexpr size_t gemm_smem_bytes() {
          256 /*barriers*/;
 }
 
-// Widen one 128 x 64 int8 row-major tile to f16 in the 128-byte-swizzled
+// Widen one 128 x 64 int8 tile (as stored: 64-byte rows, 16-byte chunk v of row
+// r at chunk v ^ ((r >> 1) & 3), i8_tile_off) to f16 in the 128-byte-swizzled
 // K-major layout the MMA descriptor expects (16-byte chunk c of row r lands at
-// chunk c ^ (r & 7)).  int8 -> f16 exactly: bias the byte to u = q + 128, place
-// it in the mantissa of 1024.0 (0x6400 | u = 1024 + u), subtract 1152.
+// chunk c ^ (r & 7)).  The stored chunk order makes eight neighbouring rows' reads
+// of one chunk hit eight different bank groups.  int8 -> f16 exactly: bias the
+// byte to u = q + 128, place it in the mantissa of 1024.0 (0x6400 | u = 1024 + u),
+// subtract 1152.
 MOE_DEV void convert_row_i8_f16(const int8_t* src_row, uint8_t* dst_tile, int r) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src_row);
   const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  const int rot = (r >> 1) & 3;
 #pragma unroll
   for (int v = 0; v < 4; ++v) {  // 4 x 16 int8 = 64 elements
-    const uint4 q = s4[v];
+    const uint4 q = s4[v ^ rot];
     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
     uint32_t out[8];
 #pragma unroll
@@ -258,7 +268,7 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&args.a_routed);
+    if (!INT8) tma_prefetch_desc(&args.a_routed);
     tma_prefetch_desc(&args.b_routed);
   }
   __syncthreads();
@@ -295,6 +305,12 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
         const CUtensorMap* ma = sh ? &args.a_shared : &args.a_routed;
         const CUtensorMap* mb = sh ? &args.b_shared : &args.b_routed;
         const int arow = sh ? t.m0 : t.group * args.rows_a_routed + t.m0;
+        // int8: this row tile's k-blocks are consecutive 8 KiB blocks
+        const int8_t* a8 = nullptr;
+        if constexpr (INT8) {
+          a8 = (sh ? args.a8_shared : args.a8_routed + static_cast<size_t>(t.group) * args.a8_group_bytes) +
+               static_cast<size_t>(t.m0 / kBM) * (sh ? args.a8_nkb_shared : args.a8_nkb_routed) * SA8;
+        }
         for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -304,7 +320,8 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], (INT8 ? SA8 : SA) + SB);
-          tma_load_2d(INT8 ? sA8 + s * SA8 : sA + s * SA, ma, kb * kBK, arow, &full[s]);
+          if constexpr (INT8) bulk_load(sA8 + s * SA8, a8 + static_cast<size_t>(kb) * SA8, SA8, &full[s]);
+          else tma_load_2d(sA + s * SA, ma, kb * kBK, arow, &full[s]);
           tma_load_2d(sB + s * SB, mb, kb * kBK, t.row0, &full[s]);
         }
       }
@@ -577,7 +594,7 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, i
 
 cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, const GemmIO& io,
                         cudaStream_t s) {
-  GemmArgs a;
+  GemmArgs a{};
   std::string err;
   const int rows = io.routed_rows;
   const int T = io.shared_rows;
@@ -602,6 +619,12 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, c
     a.k_shared = p.H;
     a.scale_routed = p.w.s13;
     a.scale_shared = p.w.ss13;
+    if (p.int8) {
+      a.a8_routed = static_cast<const int8_t*>(p.w.w13);
+      a.a8_shared = has_sh ? static_cast<const int8_t*>(p.w.ws13) : a.a8_routed;
+      a.a8_group_bytes = i8_pad_rows(2 * p.I) * i8_pad_cols(p.H);
+      a.a8_nkb_routed = a.a8_nkb_shared = static_cast<int>(i8_pad_cols(p.H) / kBK);
+    }
   } else {
     a.a_routed = p.tm_w2;
     a.a_shared = has_sh ? p.tm_ws2 : p.tm_w2;
@@ -618,6 +641,13 @@ cudaError_t launch_gemm(const Plan& p, const WsLayout& L, char* ws, bool down, c
     a.k_shared = has_sh ? p.SI : p.I;
     a.scale_routed = p.w.s2;
     a.scale_shared = p.w.ss2;
+    if (p.int8) {
+      a.a8_routed = static_cast<const int8_t*>(p.w.w2);
+      a.a8_shared = has_sh ? static_cast<const int8_t*>(p.w.ws2) : a.a8_routed;
+      a.a8_group_bytes = i8_pad_rows(p.H) * i8_pad_cols(p.I);
+      a.a8_nkb_routed = static_cast<int>(i8_pad_cols(p.I) / kBK);
+      a.a8_nkb_shared = static_cast<int>(i8_pad_cols(has_sh ? p.SI : p.I) / kBK);
+    }
   }
   const int32_t* pre = reinterpret_cast<const int32_t*>(ws + L.tile_pre);
   a.map.pre = down ? pre + (io.groups + 1) : pre;

@@ -88,10 +88,35 @@ struct TileMap {
 constexpr int kMaxKSplit = 4;       // K splits per tile for small decode batches
 constexpr int kSplitTileRows = 16;  // split-K only with 16-token tiles (BN = 16)
 
+// INT8 weights are stored tile-major: each 128-row x 64-column tile of a matrix
+// is one contiguous 8 KiB block (its rows 64 bytes apart), tiles ordered by row
+// tile, then column tile; rows are padded to 128 and columns to 64 with zeros.
+// Inside a row the four 16-byte chunks are permuted, chunk c at c ^ ((row >> 1) & 3),
+// so that the GEMM's converter threads (one row each, reading chunk c together)
+// meet no shared-memory bank conflicts.  One bulk copy fetches a whole k-block of
+// weights as a single contiguous transfer.
+constexpr int kI8TileRows = 128, kI8TileCols = 64;
+static_assert(kI8TileRows == kBM && kI8TileCols == kBK, "an int8 tile is one GEMM k-block of A");
+__host__ __device__ inline size_t i8_pad_rows(int m) {
+  return (static_cast<size_t>(m) + kI8TileRows - 1) / kI8TileRows * kI8TileRows;
+}
+__host__ __device__ inline size_t i8_pad_cols(int k) {
+  return (static_cast<size_t>(k) + kI8TileCols - 1) / kI8TileCols * kI8TileCols;
+}
+// byte offset of element (row, col) in a tile-major matrix of kpad padded columns
+__host__ __device__ inline size_t i8_tile_off(int row, int col, size_t kpad) {
+  const int rr = row % kI8TileRows, cc = col % kI8TileCols;
+  const int chunk = (cc >> 4) ^ ((rr >> 1) & 3);
+  return static_cast<size_t>(row / kI8TileRows) * kI8TileRows * kpad +
+         static_cast<size_t>(col / kI8TileCols) * (kI8TileRows * kI8TileCols) +
+         static_cast<size_t>(rr) * kI8TileCols + (chunk << 4) + (cc & 15);
+}
+
 struct DeviceWeights {
   // Packed, HBM-resident weights.  W13 rows are interleaved in groups of 32:
   // 16 gate_proj rows then the 16 matching up_proj rows, so one TMEM lane
-  // quarter holds both halves of 16 SwiGLU features.
+  // quarter holds both halves of 16 SwiGLU features.  f16 matrices are
+  // row-major; int8 ones tile-major (above), each expert padded on its own.
   void* w13 = nullptr;   // f16 or int8 [E_local][2I][H]
   void* w2 = nullptr;    // f16 or int8 [E_local][H][I]
   void* ws13 = nullptr;  // shared expert [2SI][H]

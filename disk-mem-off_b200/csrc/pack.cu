@@ -9,7 +9,9 @@
 //   * int8 mode from a float source: symmetric per-output-row quantisation,
 //     scale = fp16(max|w_row| / 127), q = clamp(rint(w / f32(scale)), -127, 127);
 //   * int8 mode from an int8 source: copied, fp16 row scales widened to fp32.
-// gate_proj / up_proj rows are interleaved in groups of 16 (see DeviceWeights).
+// gate_proj / up_proj rows are interleaved in groups of 16, and int8 matrices are
+// written tile-major (see DeviceWeights); the caller zeroes int8 matrices first so
+// that their padding stays zero.
 #include <float.h>
 
 #include "common.cuh"
@@ -47,9 +49,10 @@ __device__ float block_max(float v) {
   return out;
 }
 
-// One CTA per destination row.  src_row_of(dst_row) selects the source row.
+// One CTA per destination row.  f16 rows land at dst + dst_off; int8 rows at
+// their tile-major places in the matrix at dst (kpad padded columns).
 MOE_DEV void pack_one_row(const void* src, int dtype, size_t src_off, void* dst, size_t dst_off,
-                          bool to_int8, float* dst_scale, int dst_row, int cols,
+                          bool to_int8, float* dst_scale, int dst_row, int cols, size_t kpad,
                           int* range_err) {
   if (to_int8) {
     float amax = 0.f;
@@ -59,14 +62,14 @@ MOE_DEV void pack_one_row(const void* src, int dtype, size_t src_off, void* dst,
     const __half s16 = __float2half_rn(amax / 127.0f);
     const float s = __half2float(s16);
     if (!isfinite(s) && range_err && threadIdx.x == 0) atomicExch(range_err, 1);
-    int8_t* d = reinterpret_cast<int8_t*>(dst) + dst_off;
+    int8_t* d = reinterpret_cast<int8_t*>(dst);
     for (int c = threadIdx.x; c < cols; c += blockDim.x) {
       int q = 0;
       if (s > 0.f) {
         const float r = rintf(load_src(src, dtype, src_off + c) / s);
         q = static_cast<int>(fminf(fmaxf(r, -127.f), 127.f));
       }
-      d[c] = static_cast<int8_t>(q);
+      d[i8_tile_off(dst_row, c, kpad)] = static_cast<int8_t>(q);
     }
     if (threadIdx.x == 0) dst_scale[dst_row] = s;
   } else {
@@ -91,7 +94,8 @@ __global__ void __launch_bounds__(256) pack_w13_kernel(const void* gate, const v
   const int src_row = g * 16 + (w & 15);
   const void* src = (w < 16) ? gate : up;
   pack_one_row(src, dtype, static_cast<size_t>(src_row) * cols, dst,
-               static_cast<size_t>(pr) * cols, to_int8, dst_scale, pr, cols, range_err);
+               static_cast<size_t>(pr) * cols, to_int8, dst_scale, pr, cols, i8_pad_cols(cols),
+               range_err);
 }
 
 __global__ void __launch_bounds__(256) pack_rows_kernel(const void* src, int dtype, void* dst,
@@ -99,7 +103,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const void* src, int dty
                                                         int cols, int* range_err) {
   const int r = blockIdx.x;
   pack_one_row(src, dtype, static_cast<size_t>(r) * cols, dst, static_cast<size_t>(r) * cols,
-               to_int8, dst_scale, r, cols, range_err);
+               to_int8, dst_scale, r, cols, i8_pad_cols(cols), range_err);
 }
 
 __global__ void __launch_bounds__(256) copy_i8_w13_kernel(const int8_t* gate, const int8_t* up,
@@ -110,8 +114,8 @@ __global__ void __launch_bounds__(256) copy_i8_w13_kernel(const int8_t* gate, co
   const int g = pr >> 5, w = pr & 31;
   const int src_row = g * 16 + (w & 15);
   const int8_t* src = ((w < 16) ? gate : up) + static_cast<size_t>(src_row) * cols;
-  int8_t* d = dst + static_cast<size_t>(pr) * cols;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) d[c] = src[c];
+  const size_t kpad = i8_pad_cols(cols);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[i8_tile_off(pr, c, kpad)] = src[c];
   if (threadIdx.x == 0) dst_scale[pr] = __half2float(((w < 16) ? gs : us)[src_row]);
 }
 
@@ -119,8 +123,9 @@ __global__ void __launch_bounds__(256) copy_i8_rows_kernel(const int8_t* src, co
                                                            int8_t* dst, float* dst_scale,
                                                            int cols) {
   const int r = blockIdx.x;
+  const size_t kpad = i8_pad_cols(cols);
   for (int c = threadIdx.x; c < cols; c += blockDim.x)
-    dst[static_cast<size_t>(r) * cols + c] = src[static_cast<size_t>(r) * cols + c];
+    dst[i8_tile_off(r, c, kpad)] = src[static_cast<size_t>(r) * cols + c];
   if (threadIdx.x == 0) dst_scale[r] = __half2float(ss[r]);
 }
 

@@ -80,6 +80,10 @@ def test_null_arguments_are_errors_not_crashes(built_lib: str) -> None:
     assert lib.moe_forward(None, None, None, 1, None, 0, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_route(None, None, 1, None, None, None, None, None, 0, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_status(None, None) == _lib.MOE_ERR_INVALID
+    assert lib.moe_ep_capacity(None, 5) == 0
+    assert lib.moe_ep_padded_workspace_bytes(None, 5) == 0
+    assert lib.moe_ep_dispatch_padded(None, None, 1, 8, None, None, 0, None) == _lib.MOE_ERR_INVALID
+    assert lib.moe_ep_experts_padded(None, None, 8, None, None, 0, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_plan_destroy(None) == _lib.MOE_OK
     assert b"sm_100a" in lib.moe_version()
 

@@ -348,6 +348,28 @@ def test_int8_prefill_glm_dims() -> None:
                       T=1024, tol=TOL_I8, seed=31)
 
 
+@pytest.mark.parametrize("T", [3, 24, 64])
+def test_int8_decode_glm_dims(T: int) -> None:
+    """INT8 decode batches at GLM-4.7 dimensions (32 experts): 16-, 32- and 64-token
+    tiles, whose int8 staging ring is split from the f16 ring the MMA reads."""
+    _synthetic_parity(dict(hidden=5120, n_experts=32, top_k=8, inter=1536, shared_inter=1536,
+                           family="glm", expert_dtype="int8", seed=23, zipf_s=1.1),
+                      dict(hidden=5120, n_experts=32, top_k=8, inter=1536, shared_inter=1536,
+                           weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5),
+                      T=T, tol=TOL_I8, seed=50 + T)
+
+
+@pytest.mark.parametrize("T", [5, 300])
+def test_int8_padded_tiles(T: int) -> None:
+    """INT8 matrices whose rows are not a multiple of 128 and columns not of 64
+    (H 1040, I 208, shared 80): the zero padding of the tile-major layout."""
+    _synthetic_parity(dict(hidden=1040, n_experts=12, top_k=3, inter=208, shared_inter=80,
+                           family="glm", expert_dtype="int8", seed=24),
+                      dict(hidden=1040, n_experts=12, top_k=3, inter=208, shared_inter=80,
+                           weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5),
+                      T=T, tol=TOL_I8, seed=60 + T)
+
+
 @pytest.mark.parametrize("T", [1, 300])
 def test_qwen3_next_shape(T: int) -> None:
     """Qwen3-Coder-Next shape (H 2048, 512 experts, top-10, I 512, gated shared expert)."""
