@@ -41,7 +41,13 @@ def _torch():
 
 
 class EPOps(Protocol):
-    """Per-rank compute of the expert-parallel block (device or test stand-in)."""
+    """Per-rank compute of the expert-parallel block (device or test stand-in).
+
+    Optional: ``start_shared(x)`` (shared expert early, overlapping the exchange);
+    for the fixed-capacity exchange ``capacity(tokens)``, ``dispatch_padded(x, cap)``
+    (send rows [world*cap, ...] with the local expert id, -1 unused, in each row),
+    ``experts_padded(recv, cap)`` and, for timed forwards, ``padded_ids(recv)``.
+    """
 
     def dispatch(self, x: Any) -> tuple[Any, Any, Any]: ...      # rows, local expert ids, offsets
 
