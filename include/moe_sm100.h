@@ -68,7 +68,13 @@ typedef struct MoePlan MoePlan;
  * (offload_runtime/executors/glm4_moe.py:166-172, _dense_mlp_block), whose
  * mlp.{gate,up,down}_proj weights bind as a shared expert of shared_inter
  * (= intermediate_size) columns; moe_forward then returns x + MLP(rms_norm(x)).
- * moe_route, moe_forward_static_scratch and moe_ep_* refuse dense plans. */
+ * moe_route, moe_forward_static_scratch and moe_ep_* refuse dense plans.
+ *
+ * Shape limits (moe_plan_create refuses others with MOE_ERR_UNSUPPORTED /
+ * MOE_ERR_INVALID): hidden, inter and shared_inter multiples of 16 (16-byte
+ * rows for TMA and the vector loads; every released GLM-4 and Qwen3 MoE model
+ * qualifies, the reference's hidden-8 toy models in its integration tests do
+ * not); n_experts <= 1024; 1 <= top_k <= min(32, n_experts). */
 typedef struct MoeConfig {
   int32_t hidden;                /* H  (hidden_size)                                  */
   int32_t n_experts;             /* E  (n_routed_experts / num_experts)               */
