@@ -240,3 +240,31 @@ def test_synthetic_expert_subsets_agree_across_ranks() -> None:
         np.testing.assert_array_equal(host_tensor(b1, m1, name), host_tensor(b2, m2, name))
     with pytest.raises(ValueError, match="outside"):
         build_device_layer(SyntheticSpec(**kw, experts=(4, 9)), device="cpu")
+
+
+def test_stack_bench_memory_plan() -> None:
+    """The 89-layer INT8 stack's resident bytes per GPU (bench.py --stack decides
+    from this whether a world size fits before building anything)."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(os.path.dirname(__file__)), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    gib = [bench._stack_resident_bytes(160 // n, 89) / 2**30 for n in (2, 4, 8)]
+    # 160/N experts x 3 x 5120 x 1536 int8 + row scales + shared expert + router, per layer
+    assert 158 < gib[0] < 160 and 80 < gib[1] < 81.5 and 41 < gib[2] < 42
+    # the expert share halves with each doubling; router and shared expert stay
+    assert abs((gib[0] - gib[1]) - 2 * (gib[1] - gib[2])) < 0.01
+
+
+def test_fixed_capacity_needs_a_capacity() -> None:
+    from moe_sm100.ep import ExpertParallelMoe
+
+    class NoCapacity:
+        def capacity(self, tokens: int) -> int:
+            return 0
+
+    with pytest.raises(ValueError, match="capacity"):
+        ExpertParallelMoe(NoCapacity(), padded_tokens=8)
+    ExpertParallelMoe(NoCapacity(), padded_tokens=0)  # exact exchange only: no capacity asked
