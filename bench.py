@@ -295,8 +295,9 @@ def _measure(ml, T: int, H: int, steps: int, warmup: int, world: int, gen) -> di
 
 def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -> dict:  # noqa: ANN001
     """BASELINE config 2 (GLM-4.7 INT8, 4096-token prefill, Zipf routing; the same
-    layer also at 32 and 128 tokens, the per-rank decode batches of config 4) and
-    config 3 (Qwen3-Coder-Next shape, 1-token decode and 8192-token prefill)."""
+    layer also at the 1-64-token decode batches the INT8 target names and at 32 and
+    128 tokens, the per-rank decode batches of config 4) and config 3
+    (Qwen3-Coder-Next shape, 1-token decode and 8192-token prefill)."""
     import torch
     from moe_sm100 import MoeLayer, MoeLayerConfig
     from moe_sm100.synthetic import SyntheticSpec, build_device_layer
@@ -306,12 +307,17 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
         ("cfg2_glm47_int8_prefill", dict(GLM, family="glm", expert_dtype="int8", seed=4321,
                                          zipf_s=1.1, zipf_amp=1.0),
          dict(weight_format="int8", routed_scaling_factor=2.5, rms_norm_eps=1e-5),
-         [32, 128, 4096]),
+         [1, 8, 32, 64, 128, 4096]),
         ("cfg3_qwen3_next", dict(QWEN3, family="qwen3", expert_dtype="bfloat16", seed=5678),
          dict(use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
               rms_norm_eps=1e-6), [1, 8192]),
     ]
     for name, spec_kw, cfg_kw, tokens in runs:
+        if args.other_tokens:  # profiling aid: only the listed batch sizes
+            keep = {int(v) for v in args.other_tokens.split(",")}
+            tokens = [t for t in tokens if t in keep]
+            if not tokens:
+                continue
         spec = SyntheticSpec(**spec_kw)
         blob, meta = build_device_layer(spec, device=f"cuda:{local}")
         shape = {k: spec_kw[k] for k in ("hidden", "n_experts", "top_k", "inter", "shared_inter")}
@@ -644,6 +650,27 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
 
 
 # ------------------------------------------------------------------ arms
+def _decode_batches(t_main: int, seed: int, with_sub: bool) -> dict:
+    """The seeded input batches of the config-1 lines, drawn in a fixed order
+    (T = 1, 8, then the headline batch) so both arms time the same tokens."""
+    import torch
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    out = {}
+    for T in (sorted({1, 8, t_main}) if with_sub else [t_main]):
+        out[T] = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
+    return out
+
+
+def _config1(t_main: int, world: int) -> dict:
+    return {"workload": "BASELINE config 1: GLM-4.7-shape MoE layer, bf16 decode",
+            "tokens_per_rank": t_main, "hidden": GLM["hidden"], "experts": GLM["n_experts"],
+            "top_k": GLM["top_k"], "moe_intermediate": GLM["inter"],
+            "shared_intermediate": GLM["shared_inter"],
+            "routing": "reference softmax(logits+bias), scale 2.5",
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "inputs larger than L2 (touched weights >= 425 MB)"}
+
+
 def run_ours(args) -> None:  # noqa: ANN001
     import torch
     world, rank, local = _dist_init()
@@ -661,11 +688,9 @@ def run_ours(args) -> None:  # noqa: ANN001
     hbm, peak_kind = _peaks()
     T_main = args.tokens
     ml, blob, meta = _make_layer(local, seed=1234, max_tokens=max(64, T_main))
-    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
 
     results = {}
-    for T in (sorted({1, 8, T_main}) if not args.no_sub else [T_main]):
-        x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
+    for T, x in _decode_batches(T_main, 1000 + rank, not args.no_sub).items():
         out = torch.empty_like(x)
         ws = ml.workspace(T)
         stream = torch.cuda.current_stream().cuda_stream
@@ -750,12 +775,7 @@ def run_ours(args) -> None:  # noqa: ANN001
             "vs_baseline": None,
             "dtype": "f16 MMA / fp32 accumulate (bf16-valued weights); fp32 routing",
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, random-init)",
-            "config": {"workload": "BASELINE config 1: GLM-4.7-shape MoE layer, bf16 decode",
-                       "tokens_per_rank": T_main, "hidden": 5120, "experts": 160, "top_k": 8,
-                       "moe_intermediate": 1536, "shared_intermediate": 1536,
-                       "routing": "reference softmax(logits+bias), scale 2.5",
-                       "parallelism": "replicas" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (touched weights >= 425 MB)"},
+            "config": _config1(T_main, world),
             "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel gate/up (swap-AB tcgen05)",
                          "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
                          "frac": gate_gbs / hbm, "peak_source": peak_kind,
@@ -809,8 +829,8 @@ def run_reference(args) -> None:  # noqa: ANN001
     spec = SyntheticSpec(**GLM, family="glm", expert_dtype="bfloat16", seed=1234)
     blob, meta = build_device_layer(spec, device=f"cuda:{local}")
     T = args.tokens
-    x = torch.randn((T, GLM["hidden"]), generator=torch.Generator(device="cuda").manual_seed(1000),
-                    device="cuda").cpu().numpy()
+    # the same tokens the GPU arm times for its headline line (rank 0's batches)
+    x = _decode_batches(T, 1000, not args.no_sub)[T].cpu().numpy()
     cfg = OracleConfig(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536,
                        routed_scaling_factor=2.5, eps=1e-5)
     lazy = LazyHostTensors(blob, meta)
@@ -834,8 +854,8 @@ def run_reference(args) -> None:  # noqa: ANN001
         "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
         "data": "synthetic (same seeds as the GPU arm)",
-        "config": {"workload": "BASELINE config 1: GLM-4.7-shape MoE layer, bf16 decode",
-                   "tokens_per_rank": T, "parallelism": "host cores, rank 0 only"},
+        "config": _config1(T, 1),
+        "reference_run": "host cores, rank 0 only",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"oracle port of GLM4MoeExecutor._moe_mlp_block, T={T}, "
                                    f"{args.steps} steps after {args.warmup} warm-up"},
@@ -856,6 +876,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
     ap.add_argument("--only-other", action="store_true",
                     help="only BASELINE configs 2 and 3 (profiling aid)")
+    ap.add_argument("--other-tokens", default="",
+                    help="comma-separated batch sizes: run configs 2 and 3 only at these")
     ap.add_argument("--no-other", action="store_true",
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,

@@ -890,6 +890,13 @@ int moe_rt_set_device(int32_t device) {
   MOE_CUDA(cudaSetDevice(device));
   return MOE_OK;
 }
+int moe_rt_can_access_peer(int32_t device, int32_t peer, int32_t* can_access) {
+  if (!can_access) return fail(MOE_ERR_INVALID, "null out pointer");
+  int ok = 0;
+  MOE_CUDA(cudaDeviceCanAccessPeer(&ok, device, peer));
+  *can_access = ok;
+  return MOE_OK;
+}
 int moe_rt_malloc(uint64_t nbytes, void** dev_ptr) {
   if (!dev_ptr) return fail(MOE_ERR_INVALID, "null out pointer");
   MOE_CUDA(cudaMalloc(dev_ptr, nbytes));

@@ -63,14 +63,35 @@ int cuda_fail(cudaError_t st, const char* what) {
     if (st_ != cudaSuccess) return cuda_fail(st_, #call);  \
   } while (0)
 
+// Makes `device` current for the lifetime of the object and puts the caller's
+// current device back afterwards, so that a host thread driving several GPUs
+// keeps the device it had selected.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    st_ = cudaGetDevice(&prev_);
+    if (st_ == cudaSuccess && prev_ != device) {
+      st_ = cudaSetDevice(device);
+      switched_ = st_ == cudaSuccess;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  cudaError_t status() const { return st_; }
+
+ private:
+  int prev_ = 0;
+  bool switched_ = false;
+  cudaError_t st_ = cudaSuccess;
+};
+
 extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, float* out_dev,
                                           int32_t T, void* stream) {
   using namespace moe;
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
   Plan& p = plan->p;
   if (!p.bound) return fail(MOE_ERR_NOT_BOUND, "moe_bind_layer has not been called");
-  if (p.E == 0)
-    return fail(MOE_ERR_UNSUPPORTED, "a dense MLP plan runs through moe_forward");
   if (p.n_local != p.E)
     return fail(MOE_ERR_UNSUPPORTED,
                 "this plan holds a share of the experts: use the moe_ep_* entry points");
@@ -88,17 +109,26 @@ extern "C" int moe_forward_static_scratch(MoePlan* plan, const float* x_dev, flo
                 "this layer needs " + std::to_string(L.total) + " bytes of scratch for T=" +
                     std::to_string(T) + ", more than the " + std::to_string(kStaticScratchBytes) +
                     "-byte static scratch; use moe_forward with a workspace or a smaller T");
-  MOE_NA_CUDA(cudaSetDevice(p.device));
+  // The symbol lookup below needs the plan's device current; the guard puts the
+  // caller's device back on every return path.
+  DeviceGuard guard(p.device);
+  MOE_NA_CUDA(guard.status());
   void* scratch = nullptr;
   MOE_NA_CUDA(scratch_address(p.device, &scratch));
 
   // Same kernel sequence as moe_forward.  The router's split counters must
   // start at zero: launch_route clears them with a stream memset at the start of
-  // every call.  Every other scratch byte a kernel reads is written earlier in
-  // the same call, so nothing else has to be cleared between calls.
+  // every call, and the tile-list builders zero the split-K arrival counters.
+  // Every other scratch byte a kernel reads is written earlier in the same call,
+  // so nothing else has to be cleared between calls.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(scratch);
-  MOE_NA_CUDA(launch_route(p, L, ws, x_dev, T, true, s));
+  if (p.E == 0) {  // dense MLP plan: normalised rows and the shared-expert tile map
+    MOE_NA_CUDA(launch_row_prep(p, L, ws, x_dev, T, s));
+    MOE_NA_CUDA(launch_shared_tiles(p, L, ws, T, s));
+  } else {
+    MOE_NA_CUDA(launch_route(p, L, ws, x_dev, T, true, s));
+  }
   MOE_NA_CUDA(launch_gemm(p, L, ws, false, T, s));
   MOE_NA_CUDA(launch_gemm(p, L, ws, true,
                        GemmIO{T * p.K, T, reinterpret_cast<__half*>(ws + L.y), nullptr, p.n_local}, s));

@@ -96,6 +96,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_version": (c_char_p, []),
     "moe_rt_device_count": (c_int32, [POINTER(c_int32)]),
     "moe_rt_set_device": (c_int32, [c_int32]),
+    "moe_rt_can_access_peer": (c_int32, [c_int32, c_int32, POINTER(c_int32)]),
     "moe_rt_malloc": (c_int32, [c_uint64, POINTER(c_void_p)]),
     "moe_rt_free": (c_int32, [c_void_p]),
     "moe_rt_malloc_host": (c_int32, [c_uint64, POINTER(c_void_p)]),

@@ -1,4 +1,3 @@
-from .base import DeviceBackend
 from .cuda_backend import CUDABackend
 
-__all__ = ["CUDABackend", "DeviceBackend"]
+__all__ = ["CUDABackend"]

@@ -1,7 +1,9 @@
 """CUDA backend as a thin ctypes layer over libmoe_sm100's runtime entry points.
 
-Same class name, methods and error behaviour as
-offload_runtime/backends/cuda_backend.py:35-128 (status != 0 -> ``RuntimeError``,
+It satisfies the reference's ``DeviceBackend`` contract
+(offload_runtime/backends/base.py:9-77) by its methods alone, so the reference
+runtime accepts it without this package importing the reference.  Same class
+name, methods and error behaviour as offload_runtime/backends/cuda_backend.py:35-128 (status != 0 -> ``RuntimeError``,
 host buffer too small -> ``ValueError``, read-only host view -> ``ValueError``),
 but bound to ``moe_rt_*`` in libmoe_sm100.so instead of cuda-python, so the
 device pointers it hands out are the ones the MoE entry points consume.
@@ -14,7 +16,6 @@ from typing import Any
 
 from .._lib import check, lib
 from ..types import DeviceBuffer, HostBuffer
-from .base import DeviceBackend
 
 
 def _ptr_from_writable_view(view: memoryview) -> int:
@@ -33,7 +34,7 @@ def _stream(stream: Any) -> c_void_p:
     return c_void_p(int(stream))
 
 
-class CUDABackend(DeviceBackend):
+class CUDABackend:
     name = "cuda"
 
     def __init__(self, device_id: int = 0) -> None:
@@ -46,7 +47,15 @@ class CUDABackend(DeviceBackend):
 
     @property
     def supports_peer_to_peer(self) -> bool:
-        return True
+        """True when this device can map the memory of at least one other device."""
+        for peer in range(self.device_count()):
+            if peer == self.device_id:
+                continue
+            ok = c_int32(0)
+            check(lib().moe_rt_can_access_peer(self.device_id, peer, byref(ok)))
+            if ok.value:
+                return True
+        return False
 
     @property
     def supports_graph_capture(self) -> bool:

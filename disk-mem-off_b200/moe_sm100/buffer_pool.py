@@ -1,81 +1,68 @@
-"""Device buffer reuse plus expert-weight residency.
+"""Expert-weight residency for the offload runtime.
 
-``DeviceBufferPool`` keeps the reference's size-keyed free list
-(offload_runtime/buffer_pool.py:9-30).  ``ResidentLayerPool`` adds residency:
-a layer marked resident keeps its device blob across forwards instead of being
-freed after ``run_layer`` (runtime.py:180), so its packed MoE weights stay in
-HBM and later passes skip storage, H2D and packing for it.  A byte budget bounds
-what stays resident (e.g. ~170 GB of a 180 GB B200); least-recently-used
-layers are evicted first.
+The reference runtime frees every layer's device weights after ``run_layer``
+(offload_runtime/runtime.py:180) and copies them again on the next forward.
+``ResidentLayerPool`` is the accounting side of keeping them: a layer admitted
+here stays on the device (its packed MoE weights in HBM) across forwards, so later
+passes skip storage, the H2D copy and packing for it.  A byte budget bounds what
+stays resident (for example ~170 GB of a 180 GB B200); the least recently used
+layer is released first.  What "releasing" means belongs to the owner of the
+device memory (the executor's packed plan, a device blob), so each layer is
+admitted with the callable that frees it.
 """
 from __future__ import annotations
 
-from collections import OrderedDict, defaultdict
-from typing import Any, Callable
-
-from .types import DeviceBuffer
-
-
-class DeviceBufferPool:
-    def __init__(self, backend: Any) -> None:
-        self._backend = backend
-        self._free: dict[int, list[DeviceBuffer]] = defaultdict(list)
-
-    def acquire(self, nbytes: int) -> DeviceBuffer:
-        pool = self._free.get(nbytes)
-        if pool:
-            return pool.pop()
-        return self._backend.alloc_device(nbytes)
-
-    def release(self, buf: DeviceBuffer) -> None:
-        self._free[buf.nbytes].append(buf)
-
-    def drain(self) -> None:
-        for pool in self._free.values():
-            for buf in pool:
-                self._backend.free_device(buf)
-            pool.clear()
-        self._free.clear()
+from collections import OrderedDict
+from typing import Callable
 
 
 class ResidentLayerPool:
-    """Layer-id keyed device blobs that outlive one forward pass."""
+    """Layer-id keyed device residency with a byte budget and LRU release."""
 
-    def __init__(self, backend: Any, budget_bytes: int,
-                 on_evict: Callable[[int], None] | None = None) -> None:
-        self._backend = backend
-        self.budget_bytes = budget_bytes
+    def __init__(self, budget_bytes: int, on_evict: Callable[[int], None] | None = None) -> None:
+        self.budget_bytes = int(budget_bytes)
         self._on_evict = on_evict
-        self._layers: OrderedDict[int, DeviceBuffer] = OrderedDict()
+        self._layers: OrderedDict[int, tuple[int, Callable[[], None]]] = OrderedDict()
         self.resident_bytes = 0
+
+    def __contains__(self, layer_id: int) -> bool:
+        return layer_id in self._layers
 
     def is_resident(self, layer_id: int) -> bool:
         return layer_id in self._layers
 
-    def get(self, layer_id: int) -> DeviceBuffer | None:
-        buf = self._layers.get(layer_id)
-        if buf is not None:
-            self._layers.move_to_end(layer_id)
-        return buf
-
-    def admit(self, layer_id: int, buf: DeviceBuffer) -> bool:
-        """Keep ``buf`` resident; returns False (caller frees it) if it cannot fit."""
-        if buf.nbytes > self.budget_bytes:
+    def touch(self, layer_id: int) -> bool:
+        """Mark a resident layer as just used; False if it is not resident."""
+        if layer_id not in self._layers:
             return False
-        while self.resident_bytes + buf.nbytes > self.budget_bytes and self._layers:
+        self._layers.move_to_end(layer_id)
+        return True
+
+    def admit(self, layer_id: int, nbytes: int, release: Callable[[], None]) -> bool:
+        """Keep a layer of ``nbytes`` resident, releasing older layers to make room.
+
+        Returns False, without releasing anything, when the layer alone exceeds
+        the budget; the caller then frees it itself."""
+        nbytes = int(nbytes)
+        if layer_id in self._layers:
+            self.evict(layer_id)
+        if nbytes > self.budget_bytes:
+            return False
+        while self._layers and self.resident_bytes + nbytes > self.budget_bytes:
             self.evict(next(iter(self._layers)))
-        self._layers[layer_id] = buf
-        self.resident_bytes += buf.nbytes
+        self._layers[layer_id] = (nbytes, release)
+        self.resident_bytes += nbytes
         return True
 
     def evict(self, layer_id: int) -> None:
-        buf = self._layers.pop(layer_id, None)
-        if buf is None:
+        entry = self._layers.pop(layer_id, None)
+        if entry is None:
             return
-        self.resident_bytes -= buf.nbytes
+        nbytes, release = entry
+        self.resident_bytes -= nbytes
+        release()
         if self._on_evict is not None:
             self._on_evict(layer_id)
-        self._backend.free_device(buf)
 
     def drain(self) -> None:
         for lid in list(self._layers):

@@ -20,6 +20,8 @@ Drop-in for the reference executors' MoE block:
 """
 from __future__ import annotations
 
+import weakref
+from collections import OrderedDict
 from typing import Any, Callable
 
 import numpy as np
@@ -65,6 +67,11 @@ class DeviceMoeExecutor:
             overrides["score_func"] = score_func
         self.moe_config = self._parse(self.config, overrides)
         self._bound: dict[Any, MoeLayer] = {}
+        # layers bound from host tensor dicts (the reference's ``_moe_mlp_block(x, t)``
+        # call): a few most recent ones, each remembered by weak references to the
+        # very arrays it was packed from
+        self.tensor_cache_size = 2
+        self._by_tensors: OrderedDict[tuple[int, bool], tuple[dict[str, Any], MoeLayer]] = OrderedDict()
 
     # -- overridden by the families --------------------------------------------------
     def _parse(self, config: dict[str, Any], overrides: dict[str, Any]) -> MoeLayerConfig:
@@ -118,16 +125,42 @@ class DeviceMoeExecutor:
             ml.close()
 
     # -- the block -------------------------------------------------------------------
+    def _layer_for_tensors(self, t: dict[str, Any], dense: bool) -> MoeLayer:
+        """The bound layer packed from the host tensor dict ``t``.
+
+        The reference builds a fresh dict of numpy views for every call
+        (_common.py:43-58), and CPython reuses the id of a collected dict, so the
+        dict's id alone could name another layer's weights.  An entry therefore
+        holds weak references to every array it was packed from and matches only
+        when ``t`` maps the same names to those very (still alive) arrays; no
+        host memory is kept alive by the cache, and at most
+        ``tensor_cache_size`` packed layers stay bound."""
+        names = sorted(k for k in t if is_moe_tensor(k))
+        key = (id(t), dense)
+        hit = self._by_tensors.get(key)
+        if hit is not None:
+            refs, ml = hit
+            if refs.keys() == set(names) and all(refs[n]() is t[n] for n in names):
+                self._by_tensors.move_to_end(key)
+                return ml
+            self._by_tensors.pop(key)
+            ml.close()
+        ml = self.bind_tensors(t, dense=dense)
+        refs: dict[str, Any] = {}
+        for n in names:
+            try:
+                refs[n] = weakref.ref(t[n])
+            except TypeError:  # not weak-referenceable: never match this entry again
+                refs[n] = lambda: None
+        self._by_tensors[key] = (refs, ml)
+        while len(self._by_tensors) > max(self.tensor_cache_size, 0):
+            _k, (_r, old) = self._by_tensors.popitem(last=False)
+            old.close()
+        return ml
+
     def _moe_mlp_block(self, x: Any, t: Any) -> Any:
         """``x + MoE(rms_norm(x))`` on the device; same contract as the reference."""
-        if isinstance(t, MoeLayer):
-            ml = t
-        else:
-            key = ("tensors", id(t))
-            ml = self._bound.get(key)
-            if ml is None:
-                ml = self.bind_tensors(t)
-                self._bound[key] = ml
+        ml = t if isinstance(t, MoeLayer) else self._layer_for_tensors(t, dense=False)
         if isinstance(x, np.ndarray):
             return ml.forward_host(x)
         return ml.forward(x)
@@ -135,14 +168,7 @@ class DeviceMoeExecutor:
     def _dense_mlp_block(self, x: Any, t: Any) -> Any:
         """``x + down(silu(gate(h)) * up(h))``, ``h = rms_norm(x)``, on the device;
         same contract as the reference (glm4_moe.py:166-172)."""
-        if isinstance(t, MoeLayer):
-            ml = t
-        else:
-            key = ("dense", id(t))
-            ml = self._bound.get(key)
-            if ml is None:
-                ml = self.bind_tensors(t, dense=True)
-                self._bound[key] = ml
+        ml = t if isinstance(t, MoeLayer) else self._layer_for_tensors(t, dense=True)
         if isinstance(x, np.ndarray):
             return ml.forward_host(x)
         return ml.forward(x)

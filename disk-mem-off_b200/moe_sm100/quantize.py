@@ -1,9 +1,12 @@
-"""Dequantizer protocol of offload_runtime/quantize.py:14-97 plus per-channel INT8.
+"""Per-channel INT8 for the runtime's dequantizer hook.
 
-``Int8Dequantizer`` / ``Float16Dequantizer`` / ``CompositeDequantizer`` keep the
-reference's host-side whole-layer behaviour (scalar ``(q - zero_point) * scale``,
-fp16 -> fp32), because the runtime applies them before the H2D copy
-(runtime.py:147-151).
+The runtime calls a dequantizer before the H2D copy of a layer
+(offload_runtime/runtime.py:147-151) through the protocol of
+offload_runtime/quantize.py:14-21 (``needs_dequantize`` / ``dequantize`` /
+``decompressed_nbytes``).  The reference's own scalar dequantizers
+(``Int8Dequantizer``, ``Float16Dequantizer``, ``CompositeDequantizer``,
+offload_runtime/quantize.py:24-97) stay where they are; this module adds one
+more implementation of that protocol, which a ``CompositeDequantizer`` can list.
 
 ``Int8PerChannelDequantizer`` handles layers packed by ``moe_sm100.packing`` with
 ``expert_format="int8"`` (``metadata["dtype"] == "int8_per_channel"``).  With
@@ -28,37 +31,6 @@ class Dequantizer(Protocol):
     def dequantize(self, layer: LayerSpec, buf: HostBuffer) -> HostBuffer: ...
 
     def decompressed_nbytes(self, layer: LayerSpec) -> int: ...
-
-
-class Int8Dequantizer:
-    """Scalar int8 -> fp32: ``metadata`` keys ``dtype == "int8"``, ``scale``, ``zero_point``."""
-
-    def needs_dequantize(self, layer: LayerSpec) -> bool:
-        return layer.metadata.get("dtype") == "int8"
-
-    def decompressed_nbytes(self, layer: LayerSpec) -> int:
-        return layer.nbytes * 4
-
-    def dequantize(self, layer: LayerSpec, buf: HostBuffer) -> HostBuffer:
-        scale = layer.metadata.get("scale", 1.0)
-        zero_point = layer.metadata.get("zero_point", 0)
-        arr = np.frombuffer(buf.view, dtype=np.int8)
-        out = (arr.astype(np.float32) - zero_point) * scale
-        return HostBuffer(view=memoryview(out.tobytes()), pinned=False)
-
-
-class Float16Dequantizer:
-    """fp16 -> fp32 for ``metadata["dtype"] == "float16"``."""
-
-    def needs_dequantize(self, layer: LayerSpec) -> bool:
-        return layer.metadata.get("dtype") == "float16"
-
-    def decompressed_nbytes(self, layer: LayerSpec) -> int:
-        return layer.nbytes * 2
-
-    def dequantize(self, layer: LayerSpec, buf: HostBuffer) -> HostBuffer:
-        arr = np.frombuffer(buf.view, dtype=np.float16)
-        return HostBuffer(view=memoryview(arr.astype(np.float32).tobytes()), pinned=False)
 
 
 class Int8PerChannelDequantizer:
@@ -114,24 +86,3 @@ class Int8PerChannelDequantizer:
             offset += len(b)
         layer.metadata["dequantized_tensors"] = out_meta
         return HostBuffer(view=memoryview(bytearray(b"".join(parts))), pinned=False)
-
-
-class CompositeDequantizer:
-    def __init__(self, dequantizers: list[Any] | None = None) -> None:
-        self._dequantizers = dequantizers or [Int8Dequantizer(), Float16Dequantizer(),
-                                              Int8PerChannelDequantizer()]
-
-    def needs_dequantize(self, layer: LayerSpec) -> bool:
-        return any(d.needs_dequantize(layer) for d in self._dequantizers)
-
-    def decompressed_nbytes(self, layer: LayerSpec) -> int:
-        for d in self._dequantizers:
-            if d.needs_dequantize(layer):
-                return d.decompressed_nbytes(layer)
-        return layer.nbytes
-
-    def dequantize(self, layer: LayerSpec, buf: HostBuffer) -> HostBuffer:
-        for d in self._dequantizers:
-            if d.needs_dequantize(layer):
-                return d.dequantize(layer, buf)
-        return buf

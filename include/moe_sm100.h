@@ -68,7 +68,7 @@ typedef struct MoePlan MoePlan;
  * (offload_runtime/executors/glm4_moe.py:166-172, _dense_mlp_block), whose
  * mlp.{gate,up,down}_proj weights bind as a shared expert of shared_inter
  * (= intermediate_size) columns; moe_forward then returns x + MLP(rms_norm(x)).
- * moe_route, moe_forward_static_scratch and moe_ep_* refuse dense plans.
+ * moe_route and moe_ep_* refuse dense plans.
  *
  * Shape limits (moe_plan_create refuses others with MOE_ERR_UNSUPPORTED /
  * MOE_ERR_INVALID): hidden, inter and shared_inter multiples of 16 (16-byte
@@ -149,7 +149,9 @@ int moe_forward_timed(MoePlan* plan, const float* x_dev, float* out_dev, int32_t
  *   - The caller passes x and out as for moe_forward.
  *   - The first call on a device looks up the scratch's device address (once per
  *     device, with the plan's device current); make that first call before any
- *     stream capture.
+ *     stream capture.  The calling thread's current device is the same after
+ *     the call as before it.
+ *   - Dense-MLP plans (n_experts = 0) run here as through moe_forward.
  *   - A T whose moe_workspace_bytes(T) exceeds MOE_STATIC_SCRATCH_BYTES is
  *     rejected with MOE_ERR_WORKSPACE (for the GLM-4.7 shape, T <= 64 fits).
  *   - All calls in the process share the one scratch array and it keeps the last
@@ -232,6 +234,9 @@ const char* moe_version(void);
 /* ------------------------------------------- runtime (CUDABackend, ctypes) */
 int moe_rt_device_count(int32_t* count);
 int moe_rt_set_device(int32_t device);
+/* *can_access = 1 when `device` can map the memory of `peer`
+ * (cudaDeviceCanAccessPeer); backs CUDABackend.supports_peer_to_peer. */
+int moe_rt_can_access_peer(int32_t device, int32_t peer, int32_t* can_access);
 int moe_rt_malloc(uint64_t nbytes, void** dev_ptr);
 int moe_rt_free(void* dev_ptr);
 int moe_rt_malloc_host(uint64_t nbytes, void** host_ptr);

@@ -7,8 +7,12 @@
   produces) and from bf16 / int8 blobs;
 * full GLM-4.7 shape (H 5120, E 160, top-8, I 1536): routing exact against the
   oracle at T = 1, 8, 64 and 4096 (a flip is tolerated only at an oracle score gap
-  below 1e-6 relative, and is counted), output parity at T = 1 and 4 on the
-  experts the tokens touch, size-independent properties at T = 64 / 4096;
+  below 1e-6 relative, and is counted), output parity at T = 1, 4, 8 and 64 (the
+  benchmarked layer and batches), sigmoid routing on the decode path,
+  size-independent properties at T = 64 / 4096;
+* the benchmarked INT8 layer of BASELINE config 2 (160 experts, Zipf routing) at
+  T = 1, 8, 32, 64, 128 (every row) and 4096 (256 rows), and the Qwen3-Next layer
+  of config 3 at T = 1 and 8192 (256 rows), against the oracle;
 * prefill routing (tensor-core candidates, fp32 decision) on exact ties;
 * the dense MLP of first_k_dense_replace layers against the reference's output.
 """
@@ -26,7 +30,8 @@ pytestmark = [pytest.mark.gpu,
 
 from moe_sm100 import MoeLayer, MoeLayerConfig  # noqa: E402
 from moe_sm100.packing import pack_layer  # noqa: E402
-from moe_sm100.synthetic import GLM47, LazyHostTensors, SyntheticSpec, build_device_layer  # noqa: E402
+from moe_sm100.synthetic import (GLM47, QWEN3_NEXT, LazyHostTensors, SyntheticSpec,  # noqa: E402
+                                 build_device_layer)
 from oracle.cases import DENSE_SPECS, GOLDEN_SPECS, make_case, make_dense_case  # noqa: E402
 from oracle.moe_oracle import (OracleConfig, dense_mlp_block, int8_pc_dequantize,  # noqa: E402
                                int8_pc_quantize, moe_block, permutation, rms_norm, route)
@@ -87,6 +92,30 @@ def test_golden_parity(name: str, fmt: str) -> None:
     # two calls in a row give the same bits (deterministic combine, no atomics)
     out2 = ml.forward(xd)
     assert torch.equal(out, out2)
+
+
+def test_golden_sigmoid_decode() -> None:
+    """HF GLM-4.x sigmoid routing through the decode path (64 tokens, one-CTA tail):
+    ids bit-exact and weights to 1e-5 against the fixture pinned to transformers,
+    block output against the oracle's sigmoid mode."""
+    from oracle.cases import SIGMOID_SPECS
+    spec = SIGMOID_SPECS["glm_sigmoid"]
+    with np.load(os.path.join(GOLDEN, "glm_sigmoid.npz")) as z:
+        g = {k: z[k] for k in z.files}
+    x, t, _quant, cfg = make_case(spec)
+    blob, meta = pack_layer(t, expert_format="bfloat16")
+    ml = MoeLayer(_layer_cfg(spec, "f16", spec.tokens))
+    ml.bind_host(blob, meta)
+    xd = torch.from_numpy(x).cuda()
+    r = ml.route(xd)
+    out = ml.forward(xd)
+    ml.status()
+    np.testing.assert_array_equal(r["topk_ids"].cpu().numpy(), g["topk_ids"])
+    np.testing.assert_allclose(r["topk_w"].cpu().numpy(), g["topk_w"], rtol=1e-5, atol=1e-7)
+    ref, _aux = moe_block(x, t, cfg)
+    err = rel_l2(out.cpu().numpy(), ref)
+    assert err <= TOL_16, f"rel-L2 {err:.3e}"
+    ml.close()
 
 
 def test_host_buffers_end_to_end() -> None:
@@ -288,15 +317,149 @@ def test_prefill_router_exact_ties(score_func: str) -> None:
     ml.close()
 
 
-@pytest.mark.parametrize("T", [1, 4])
+def _block_parity(got_out: np.ndarray, got_ids: np.ndarray, x: np.ndarray, lazy, ocfg,  # noqa: ANN001
+                  tol: float) -> tuple[float, int]:
+    """Device output and expert ids against the oracle on the same rows.
+
+    Both routers are fp32, but the 5120-term logit sums are added in different
+    orders (~4e-6 absolute apart), so a token whose k-th and (k+1)-th selection
+    keys are closer than that may pick the other expert.  Such a token is
+    accepted only at an oracle key gap below 1e-6 relative and is left out of
+    the output comparison (its expert set differs); every other token's ids must
+    be identical and the output of those tokens within ``tol`` rel-L2."""
+    ref, aux = moe_block(x, lazy, ocfg)
+    ids = aux["topk_ids"]
+    k = ocfg.top_k
+    if ocfg.score_func == "sigmoid":
+        keys = 1.0 / (1.0 + np.exp(-aux["logits"].astype(np.float64)))
+        bias = lazy.get("mlp.gate.e_score_correction_bias")
+        if ocfg.use_bias and bias is not None:
+            keys = keys + bias
+    else:
+        keys = aux["logits"].astype(np.float64)  # biased logits rank like the softmax
+    same = (got_ids == ids).all(axis=1)
+    for row in np.nonzero(~same)[0]:
+        srt = np.sort(keys[row])[::-1]
+        gap = np.min(np.abs(np.diff(srt[: k + 1]))) / max(abs(srt[k - 1]), 1e-30)
+        assert gap < 1e-6, f"token {row}: routing differs at key gap {gap:.2e}"
+    flips = int((~same).sum())
+    assert flips <= max(1, x.shape[0] // 500), f"{flips} tokens routed differently"
+    err = rel_l2(got_out[same], ref[same])
+    assert err <= tol, f"rel-L2 {err:.3e} over {int(same.sum())} rows"
+    return err, flips
+
+
+@pytest.mark.parametrize("T", [1, 4, 8, 64])
 def test_full_shape_output(glm_full, T: int) -> None:  # noqa: ANN001
+    """BASELINE config 1 (the benchmarked layer: seed 1234, 160 experts) at its decode
+    batches, 64 being the headline line: output vs the oracle on the same weights."""
     ml, lazy, ocfg = glm_full
     x = np.random.default_rng(200 + T).standard_normal((T, 5120), dtype=np.float32)
-    out = ml.forward(torch.from_numpy(x).cuda())
+    xd = torch.from_numpy(x).cuda()
+    out = ml.forward(xd)
+    ids = ml.route(xd)["topk_ids"]
     ml.status()
-    ref, _aux = moe_block(x, lazy, ocfg)
-    err = rel_l2(out.cpu().numpy(), ref)
-    assert err <= TOL_16, f"rel-L2 {err:.3e}"
+    _block_parity(out.cpu().numpy(), ids.cpu().numpy(), x, lazy, ocfg, TOL_16)
+
+
+def test_full_shape_sigmoid_decode(glm_full) -> None:  # noqa: ANN001
+    """HF GLM-4.x sigmoid routing on the decode path (one-CTA tail) at the full
+    GLM-4.7 shape: ids, weights and output against the oracle's sigmoid mode."""
+    _ml, lazy, ocfg = glm_full
+    blob, meta = lazy._blob, lazy._meta
+    cfg = MoeLayerConfig(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536,
+                         score_func="sigmoid", routed_scaling_factor=2.5, rms_norm_eps=1e-5,
+                         max_tokens=64)
+    ml = MoeLayer(cfg)
+    ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+    scfg = OracleConfig(**{**ocfg.__dict__, "score_func": "sigmoid"})
+    h_w = lazy["post_attention_layernorm.weight"]
+    for T in (1, 8, 64):
+        x = np.random.default_rng(300 + T).standard_normal((T, 5120), dtype=np.float32)
+        xd = torch.from_numpy(x).cuda()
+        r = ml.route(xd)
+        out = ml.forward(xd)
+        ml.status()
+        got = r["topk_ids"].cpu().numpy()
+        _block_parity(out.cpu().numpy(), got, x, lazy, scfg, TOL_16)
+        h = rms_norm(x, h_w, scfg.eps)
+        ids, w, _logits = route(h, lazy["mlp.gate.weight"],
+                                lazy["mlp.gate.e_score_correction_bias"], scfg)
+        np.testing.assert_allclose(r["topk_w"].cpu().numpy()[got == ids], w[got == ids], rtol=5e-5)
+    ml.close()
+
+
+def _slice_parity(ml, lazy, ocfg, x: np.ndarray, rows: np.ndarray, tol: float) -> float:  # noqa: ANN001
+    """Forward the whole batch on the device, then check the given rows against
+    the oracle run on those rows alone.  The block is row-independent (routing is
+    per token, every expert product is per row), so the rows of the full-batch
+    output must equal the oracle's output for the sliced batch."""
+    xd = torch.from_numpy(x).cuda()
+    out = ml.forward(xd)
+    ids = ml.route(xd)["topk_ids"]
+    ml.status()
+    err, _flips = _block_parity(out.cpu().numpy()[rows], ids.cpu().numpy()[rows],
+                                np.ascontiguousarray(x[rows]), lazy, ocfg, tol)
+    return err
+
+
+# ------------------------------------------------------------------ BASELINE configs 2 and 3
+@pytest.fixture(scope="module")
+def glm_int8_cfg2():
+    """The benchmarked config-2 layer: GLM-4.7 shape, 160 experts, per-channel INT8,
+    Zipf(1.1)-skewed router bias (seed 4321, as bench.py builds it)."""
+    spec = SyntheticSpec(**GLM47, expert_dtype="int8", seed=4321, zipf_s=1.1, zipf_amp=1.0)
+    blob, meta = build_device_layer(spec)
+    ml = MoeLayer(MoeLayerConfig(hidden=5120, n_experts=160, top_k=8, inter=1536,
+                                 shared_inter=1536, weight_format="int8",
+                                 routed_scaling_factor=2.5, rms_norm_eps=1e-5, max_tokens=4096))
+    ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    ocfg = OracleConfig(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536,
+                        routed_scaling_factor=2.5, eps=1e-5)
+    # one host cache per layer: the oracle fetches each touched expert once
+    yield ml, LazyHostTensors(blob, meta), ocfg
+    ml.close()
+    del blob
+
+
+@pytest.mark.parametrize("T", [1, 8, 32, 64, 128, 4096])
+def test_cfg2_int8_full_shape(glm_int8_cfg2, T: int) -> None:  # noqa: ANN001
+    """BASELINE config 2 at every batch the bench times (INT8 decode 1-128, prefill
+    4096): the device output against the oracle on the dequantised weights.  Up to
+    128 tokens every row is checked; at 4096 a spread of 256 rows."""
+    ml, lazy, ocfg = glm_int8_cfg2
+    x = np.random.default_rng(400 + T).standard_normal((T, 5120), dtype=np.float32)
+    rows = np.arange(T) if T <= 128 else np.linspace(0, T - 1, 256).astype(np.int64)
+    _slice_parity(ml, lazy, ocfg, x, rows, TOL_I8)
+
+
+@pytest.fixture(scope="module")
+def qwen3_cfg3():
+    """The benchmarked config-3 layer: Qwen3-Coder-Next shape, bf16, seed 5678."""
+    spec = SyntheticSpec(**QWEN3_NEXT, expert_dtype="bfloat16", seed=5678)
+    blob, meta = build_device_layer(spec)
+    ml = MoeLayer(MoeLayerConfig(hidden=2048, n_experts=512, top_k=10, inter=512, shared_inter=512,
+                                 use_bias=False, has_shared_gate=True, routed_scaling_factor=1.0,
+                                 rms_norm_eps=1e-6, max_tokens=8192))
+    ml.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    ocfg = OracleConfig(hidden=2048, n_experts=512, top_k=10, inter=512, shared_inter=512,
+                        use_bias=False, routed_scaling_factor=1.0, eps=1e-6,
+                        shared_prefix="mlp.shared_expert.")
+    yield ml, LazyHostTensors(blob, meta), ocfg
+    ml.close()
+    del blob
+
+
+@pytest.mark.parametrize("T", [1, 8192])
+def test_cfg3_qwen3_full_shape(qwen3_cfg3, T: int) -> None:  # noqa: ANN001
+    """BASELINE config 3 at the batches the bench times: 1-token decode (whole
+    batch) and 8192-token prefill (256 rows spread over the batch)."""
+    ml, lazy, ocfg = qwen3_cfg3
+    x = np.random.default_rng(500 + T).standard_normal((T, 2048), dtype=np.float32)
+    rows = np.arange(T) if T <= 128 else np.linspace(0, T - 1, 256).astype(np.int64)
+    _slice_parity(ml, lazy, ocfg, x, rows, TOL_16)
 
 
 @pytest.mark.parametrize("T", [64, 4096])

@@ -9,13 +9,12 @@ import numpy as np
 import pytest
 import torch
 
-from moe_sm100.buffer_pool import DeviceBufferPool, ResidentLayerPool
+from moe_sm100.buffer_pool import ResidentLayerPool
 from moe_sm100.config import MoeLayerConfig
 from moe_sm100.layer import _descs, layer_shapes
 from moe_sm100.packing import (bf16_bits, bf16_to_f32, dequantize_int8_per_channel, is_expert_weight,
                                pack_layer, quantize_int8_per_channel)
-from moe_sm100.quantize import (CompositeDequantizer, Float16Dequantizer, Int8Dequantizer,
-                                Int8PerChannelDequantizer)
+from moe_sm100.quantize import Int8PerChannelDequantizer
 from moe_sm100.types import DeviceBuffer, HostBuffer, LayerSpec
 from oracle.moe_oracle import bf16_round, int8_pc_quantize
 
@@ -125,29 +124,6 @@ def test_layer_shapes_from_metadata() -> None:
 
 
 # ------------------------------------------------------------------ dequantizers
-def test_scalar_int8_dequantizer_known_answers() -> None:
-    d = Int8Dequantizer()
-    layer = LayerSpec(0, "L0", 2, {"dtype": "int8", "scale": 0.5, "zero_point": 0})
-    out = d.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("2b", 4, -2)))))
-    assert struct.unpack("2f", out.view.tobytes()) == (2.0, -1.0)
-    layer = LayerSpec(0, "L0", 1, {"dtype": "int8", "scale": 1.0, "zero_point": 10})
-    out = d.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("1b", 15)))))
-    assert struct.unpack("1f", out.view.tobytes()) == (5.0,)
-    assert d.decompressed_nbytes(LayerSpec(0, "L0", 100, {"dtype": "int8"})) == 400
-
-
-def test_float16_and_composite_dequantizers() -> None:
-    f = Float16Dequantizer()
-    layer = LayerSpec(0, "L0", 4, {"dtype": "float16"})
-    out = f.dequantize(layer, HostBuffer(memoryview(bytearray(struct.pack("2e", 1.0, 2.0)))))
-    assert struct.unpack("2f", out.view.tobytes()) == (1.0, 2.0)
-    c = CompositeDequantizer()
-    plain = LayerSpec(0, "L0", 16)
-    buf = HostBuffer(memoryview(bytearray(16)))
-    assert not c.needs_dequantize(plain) and c.dequantize(plain, buf) is buf
-    assert c.decompressed_nbytes(LayerSpec(0, "L0", 4, {"dtype": "int8", "scale": 1.0})) == 16
-
-
 def test_per_channel_dequantizer_keeps_blob_compressed_by_default() -> None:
     rng = np.random.default_rng(3)
     t = {"mlp.experts.0.up_proj.weight": (rng.standard_normal((16, 32)) * 0.02).astype(np.float32),
@@ -156,7 +132,7 @@ def test_per_channel_dequantizer_keeps_blob_compressed_by_default() -> None:
     layer = LayerSpec(0, "L0", len(blob), {"dtype": "int8_per_channel", "tensors": meta})
     keep = Int8PerChannelDequantizer()
     assert not keep.needs_dequantize(layer)
-    assert not CompositeDequantizer().needs_dequantize(layer)
+    assert keep.decompressed_nbytes(layer) == layer.nbytes
     host = Int8PerChannelDequantizer(keep_on_device=False)
     assert host.needs_dequantize(layer)
     out = host.dequantize(layer, HostBuffer(memoryview(blob)))
@@ -168,46 +144,24 @@ def test_per_channel_dequantizer_keeps_blob_compressed_by_default() -> None:
 
 
 # ------------------------------------------------------------------ residency
-class _FakeBackend:
-    name = "fake"
-
-    def __init__(self) -> None:
-        self.live: set[int] = set()
-        self.n = 0
-
-    def alloc_device(self, nbytes: int) -> DeviceBuffer:
-        self.n += 1
-        self.live.add(self.n)
-        return DeviceBuffer(handle=self.n, nbytes=nbytes, backend=self.name)
-
-    def free_device(self, buf: DeviceBuffer) -> None:
-        self.live.remove(buf.handle)
-
-
-def test_buffer_pool_reuses_by_size() -> None:
-    be = _FakeBackend()
-    pool = DeviceBufferPool(be)
-    a = pool.acquire(10)
-    pool.release(a)
-    assert pool.acquire(10) is a
-    pool.release(a)
-    pool.drain()
-    assert not be.live
-
-
 def test_resident_pool_budget_and_lru_eviction() -> None:
-    be = _FakeBackend()
+    released: list[int] = []
     evicted: list[int] = []
-    pool = ResidentLayerPool(be, budget_bytes=100, on_evict=evicted.append)
+    pool = ResidentLayerPool(budget_bytes=100, on_evict=evicted.append)
     for lid in range(3):
-        assert pool.admit(lid, be.alloc_device(40))
-    assert evicted == [0] and pool.resident_bytes == 80
-    pool.get(1)  # touch -> 2 is now the oldest
-    assert pool.admit(3, be.alloc_device(40))
-    assert evicted == [0, 2] and pool.is_resident(1) and pool.is_resident(3)
-    assert not pool.admit(9, DeviceBuffer(handle=-1, nbytes=101, backend="fake"))
+        assert pool.admit(lid, 40, lambda lid=lid: released.append(lid))
+    assert evicted == [0] and released == [0] and pool.resident_bytes == 80
+    assert pool.touch(1)  # 2 is now the oldest
+    assert pool.admit(3, 40, lambda: released.append(3))
+    assert evicted == [0, 2] and 1 in pool and pool.is_resident(3)
+    # a layer larger than the whole budget is refused without releasing anything
+    assert not pool.admit(9, 101, lambda: released.append(9))
+    assert released == [0, 2] and not pool.touch(9)
+    # admitting a resident layer again replaces (and releases) the old entry
+    assert pool.admit(3, 10, lambda: released.append(33))
+    assert released == [0, 2, 3] and pool.resident_bytes == 50
     pool.drain()
-    assert not be.live and pool.resident_bytes == 0
+    assert sorted(released) == [0, 1, 2, 3, 33] and pool.resident_bytes == 0
 
 
 def test_executor_rejects_non_cuda_backend() -> None:
@@ -268,3 +222,40 @@ def test_fixed_capacity_needs_a_capacity() -> None:
     with pytest.raises(ValueError, match="capacity"):
         ExpertParallelMoe(NoCapacity(), padded_tokens=8)
     ExpertParallelMoe(NoCapacity(), padded_tokens=0)  # exact exchange only: no capacity asked
+
+
+def test_tensor_dict_cache_never_serves_other_weights() -> None:
+    """``_moe_mlp_block(x, t)`` with host dicts: a dict is matched by the arrays it
+    holds, not by its id (which CPython reuses), and the cache stays bounded."""
+    from moe_sm100.executors import GLM4MoeExecutor
+
+    class _FakeLayer:
+        def __init__(self, tag: int) -> None:
+            self.tag, self.closed = tag, False
+
+        def close(self) -> None:
+            self.closed = True
+
+    ex = GLM4MoeExecutor({"hidden_size": 64, "moe_intermediate_size": 16, "n_routed_experts": 4,
+                          "num_experts_per_tok": 2})
+    made: list[_FakeLayer] = []
+
+    def fake_bind(t, expert_format="float32", dense=False):  # noqa: ANN001, ANN202
+        made.append(_FakeLayer(len(made)))
+        return made[-1]
+
+    ex.bind_tensors = fake_bind  # type: ignore[method-assign]
+    t1 = {"mlp.gate.weight": np.zeros((4, 64), np.float32)}
+    a = ex._layer_for_tensors(t1, dense=False)
+    assert ex._layer_for_tensors(t1, dense=False) is a  # same dict, same arrays: hit
+    t1["mlp.gate.weight"] = np.ones((4, 64), np.float32)  # same dict id, new array
+    b = ex._layer_for_tensors(t1, dense=False)
+    assert b is not a and a.closed
+    keep = [{"mlp.gate.weight": np.zeros((4, 64), np.float32)} for _ in range(2)]
+    for t in keep:
+        ex._layer_for_tensors(t, dense=False)
+    assert len(ex._by_tensors) == ex.tensor_cache_size and b.closed
+    # a collected dict whose id comes back with other arrays is not a hit
+    for _ in range(3):
+        c = ex._layer_for_tensors({"mlp.gate.weight": np.zeros((4, 64), np.float32)}, dense=False)
+        assert c is made[-1]

@@ -6,11 +6,16 @@ pool has already taken the GPU, or a serving loop that may not call cudaMalloc
 because it synchronises the device.  For them the library runs the MoE forward
 with a fixed scratch array of its own instead of a caller workspace.
 
-This test calls that entry point through the C ABI and checks its output
-against ``moe_forward`` (the workspace entry point) on two calls in a row, with
-different batches so the second call runs over the first call's leftovers, and
-checks that a batch too large for the fixed scratch is refused with a clear
-error.  It lives in its own file so that pytest collects it last.
+These tests call that entry point through the C ABI and compare its output with
+``moe_forward`` (the workspace entry point) on calls in a row, with different
+batches so that each call runs over the previous call's leftovers.  Both paths
+launch the same deterministic kernels on the same weights and inputs, so the
+outputs must be identical bit for bit: any difference means leftover scratch
+contents leaked into a result.  Covered: decode batches (one-CTA routing tail),
+a prefill batch (T > 256: tensor-core router, permutation counters), a dense-MLP
+plan, the refusal of a batch too large for the fixed scratch, and that the
+caller's current device is left alone.  The file is named so that pytest
+collects it last.
 """
 from __future__ import annotations
 
@@ -27,7 +32,6 @@ pytestmark = [pytest.mark.gpu,
 from moe_sm100 import MoeLayer, MoeLayerConfig, _lib  # noqa: E402
 from moe_sm100.packing import pack_layer  # noqa: E402
 
-TOL = 2e-3  # the rel-L2 bound the 16-bit parity tests use
 H, E, K, I, SI = 512, 32, 8, 128, 128
 
 
@@ -47,6 +51,20 @@ def _layer(max_tokens: int) -> MoeLayer:
     ml = MoeLayer(MoeLayerConfig(hidden=H, n_experts=E, top_k=K, inter=I, shared_inter=SI,
                                  routed_scaling_factor=2.5, rms_norm_eps=1e-5,
                                  max_tokens=max_tokens))
+    ml.bind_host(blob, meta)
+    return ml
+
+
+def _dense_layer(max_tokens: int) -> MoeLayer:
+    rng = np.random.default_rng(78)
+    inter = 384
+    t = {"post_attention_layernorm.weight": (1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
+         "mlp.gate_proj.weight": (rng.standard_normal((inter, H)) * 0.02).astype(np.float32),
+         "mlp.up_proj.weight": (rng.standard_normal((inter, H)) * 0.02).astype(np.float32),
+         "mlp.down_proj.weight": (rng.standard_normal((H, inter)) * 0.02).astype(np.float32)}
+    blob, meta = pack_layer(t, expert_format="bfloat16")
+    ml = MoeLayer(MoeLayerConfig.dense_mlp({"hidden_size": H, "intermediate_size": inter},
+                                           rms_norm_eps=1e-5, max_tokens=max_tokens))
     ml.bind_host(blob, meta)
     return ml
 
@@ -75,19 +93,38 @@ def _rel_l2(a: "torch.Tensor", b: "torch.Tensor") -> float:
     return float((a64 - b64).norm() / b64.norm())
 
 
+def _assert_same(got: "torch.Tensor", ref: "torch.Tensor", what: str) -> None:
+    # identical kernels on identical inputs: any difference is leftover scratch
+    assert torch.equal(got, ref), f"{what}: differs from moe_forward (rel-L2 {_rel_l2(got, ref):.3e})"
+
+
 def test_static_scratch_matches_workspace_forward_twice() -> None:
-    ml = _layer(max_tokens=128)
+    ml = _layer(max_tokens=384)
     gen = torch.Generator(device="cuda").manual_seed(5)
-    x1 = torch.randn((96, H), generator=gen, device="cuda")
-    x2 = torch.randn((7, H), generator=gen, device="cuda")
-    ref1 = _forward_workspace(ml, x1)
-    ref2 = _forward_workspace(ml, x2)
-    got1 = _forward_static(ml, x1)   # first call on this device sets up the scratch address
-    got2 = _forward_static(ml, x2)   # second call reuses the scratch left by the first
+    batches = [torch.randn((t, H), generator=gen, device="cuda") for t in (96, 7, 300, 13)]
+    refs = [_forward_workspace(ml, x) for x in batches]
+    device_before = torch.cuda.current_device()
+    # the first call on this device sets up the scratch address; each later call
+    # runs over the scratch the previous one left (decode, decode, prefill, decode)
+    gots = [_forward_static(ml, x) for x in batches]
     torch.cuda.synchronize()
     ml.status()
-    assert _rel_l2(got1, ref1) <= TOL
-    assert _rel_l2(got2, ref2) <= TOL
+    assert torch.cuda.current_device() == device_before
+    for i, (got, ref) in enumerate(zip(gots, refs)):
+        _assert_same(got, ref, f"call {i + 1} (T={batches[i].shape[0]})")
+    ml.close()
+
+
+def test_static_scratch_dense_plan() -> None:
+    ml = _dense_layer(max_tokens=64)
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    xs = [torch.randn((t, H), generator=gen, device="cuda") for t in (40, 3)]
+    refs = [_forward_workspace(ml, x) for x in xs]
+    gots = [_forward_static(ml, x) for x in xs]
+    torch.cuda.synchronize()
+    ml.status()
+    for i, (got, ref) in enumerate(zip(gots, refs)):
+        _assert_same(got, ref, f"dense call {i + 1}")
     ml.close()
 
 
