@@ -67,6 +67,7 @@ class DeviceMoeExecutor:
             overrides["score_func"] = score_func
         self.moe_config = self._parse(self.config, overrides)
         self._bound: dict[Any, MoeLayer] = {}
+        self._host_tensors: dict[int, dict[str, Any]] = {}  # non-MoE tensors of resident layers
         # layers bound from host tensor dicts (the reference's ``_moe_mlp_block(x, t)``
         # call): a few most recent ones, each remembered by weak references to the
         # very arrays it was packed from
@@ -118,11 +119,6 @@ class DeviceMoeExecutor:
         ml = MoeLayer(self._dense_config(meta) if dense else self._layer_config(meta))
         ml.bind_host(blob, meta)
         return ml
-
-    def evict(self, key: Any) -> None:
-        ml = self._bound.pop(key, None)
-        if ml is not None:
-            ml.close()
 
     # -- the block -------------------------------------------------------------------
     def _layer_for_tensors(self, t: dict[str, Any], dense: bool) -> MoeLayer:
@@ -176,36 +172,76 @@ class DeviceMoeExecutor:
     # -- LayerExecutor protocol ----------------------------------------------------------
     def run_layer(self, layer: Any, activations: Any, device_weights: Any, backend: Any,
                   stream: Any) -> Any:
+        """One decoder layer (runtime.py:15-26).  ``device_weights`` is the layer blob
+        the runtime copied to the device; ``None`` asks for a layer this executor
+        holds from an earlier pass (``resident_nbytes`` is not None), which then
+        runs without touching storage or the blob."""
         if getattr(backend, "name", None) != "cuda":
             raise ValueError("the sm_100a MoE executor runs on the 'cuda' backend only")
-        meta = layer.metadata["tensors"]
-        host_meta = [m for m in meta if not is_moe_tensor(_short(m["name"], layer))]
-        t_host = _read_ranges(backend, device_weights, host_meta, stream) if host_meta else {}
+        lid = layer.layer_id
+        if device_weights is None:
+            held = self._host_tensors.get(lid)
+            if held is None or not self._holds_block(layer):
+                raise KeyError(f"layer {lid} is not resident in this executor")
+            t_host = held
+        else:
+            meta = layer.metadata["tensors"]
+            host_meta = [m for m in meta if not is_moe_tensor(_short(m["name"], layer))]
+            t_host = _read_ranges(backend, device_weights, host_meta, stream) if host_meta else {}
+            if self.resident:
+                self._host_tensors[lid] = t_host
         x = activations
-        if host_meta:
+        if t_host:
             if self.attention is None:
                 raise NotImplementedError(
                     "layer has attention tensors; pass attention=<callable(layer, x, t)> "
                     "(e.g. moe_sm100.executors.reference_delegates(ref_executor))")
             x = self.attention(layer, x, t_host)
-        if self._is_moe_layer(layer):
-            stream_handle = getattr(stream, "value", stream)
-            ml = self.bind_device_blob(layer.layer_id, int(device_weights.handle),
-                                       int(device_weights.nbytes),
-                                       [dict(m, name=_short(m["name"], layer)) for m in meta],
-                                       stream_handle)
-            x = self._moe_mlp_block(x, ml)
-        elif self.dense_mlp is not None:
-            t_all = _read_ranges(backend, device_weights, meta, stream)
-            x = self.dense_mlp(x, t_all)
-        else:  # the dense MLP on the device, packed straight from the blob
-            stream_handle = getattr(stream, "value", stream)
-            ml = self.bind_device_blob(("dense", layer.layer_id), int(device_weights.handle),
-                                       int(device_weights.nbytes),
-                                       [dict(m, name=_short(m["name"], layer)) for m in meta],
-                                       stream_handle, dense=True)
-            x = self._dense_mlp_block(x, ml)
-        return x
+        if not self._is_moe_layer(layer) and self.dense_mlp is not None:
+            if device_weights is None:
+                raise KeyError(f"layer {lid}: a host dense-MLP delegate needs the layer blob")
+            t_all = _read_ranges(backend, device_weights, layer.metadata["tensors"], stream)
+            return self.dense_mlp(x, t_all)
+        ml = self._block_for(layer, device_weights, stream)
+        return self._moe_mlp_block(x, ml) if self._is_moe_layer(layer) else self._dense_mlp_block(x, ml)
+
+    def _block_key(self, layer: Any) -> Any:
+        return layer.layer_id if self._is_moe_layer(layer) else ("dense", layer.layer_id)
+
+    def _holds_block(self, layer: Any) -> bool:
+        if not self._is_moe_layer(layer) and self.dense_mlp is not None:
+            return False  # the host delegate needs the blob on every pass
+        return self._block_key(layer) in self._bound
+
+    def _block_for(self, layer: Any, device_weights: Any, stream: Any) -> MoeLayer:
+        key = self._block_key(layer)
+        if device_weights is None:
+            return self._bound[key]
+        stream_handle = getattr(stream, "value", stream)
+        meta = [dict(m, name=_short(m["name"], layer)) for m in layer.metadata["tensors"]]
+        return self.bind_device_blob(key, int(device_weights.handle), int(device_weights.nbytes),
+                                     meta, stream_handle, dense=not self._is_moe_layer(layer))
+
+    # -- residency (used by moe_sm100.runtime.ResidentOffloadRuntime) -------------------
+    def resident_nbytes(self, layer_id: int) -> int | None:
+        """Device bytes this executor keeps for ``layer_id`` between passes, or None
+        when it cannot run the layer again without its blob."""
+        if not self.resident or layer_id not in self._host_tensors:
+            return None
+        for key in (layer_id, ("dense", layer_id)):
+            ml = self._bound.get(key)
+            if ml is not None:
+                return ml.weight_bytes
+        return None
+
+    def evict(self, key: Any) -> None:
+        """Release what is kept for a layer id (or a bind key): its packed plan and
+        the host copies of its non-MoE tensors."""
+        for k in (key, ("dense", key)):
+            ml = self._bound.pop(k, None)
+            if ml is not None:
+                ml.close()
+        self._host_tensors.pop(key, None)
 
 
 def _read_ranges(backend: Any, buf: Any, metas: list[dict[str, Any]], stream: Any) -> dict[str, Any]:

@@ -177,3 +177,75 @@ def make_dense_case(spec: CaseSpec) -> tuple[np.ndarray, dict[str, np.ndarray], 
         if qs is not None:
             quant[key] = qs
     return x, t, quant
+
+
+# ---------------------------------------------------------------------------
+# GLM-4 MoE attention blocks (glm4_moe.py:112-162)
+# ---------------------------------------------------------------------------
+@dataclass
+class AttnSpec:
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    tokens: int
+    seed: int = 0
+    qk_norm: bool = True
+    bias: bool = True
+    partial_rotary_factor: float = 0.5
+    rope_theta: float = 1_000_000.0
+    eps: float = 1e-5
+    weights: str = "bf16"          # "f32" | "bf16"
+    norm_w_std: float = 0.1
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    def hf_config(self) -> dict[str, Any]:
+        """The config keys GLM4MoeExecutor reads for its attention (glm4_moe.py:70-84)."""
+        return {"hidden_size": self.hidden, "num_attention_heads": self.heads,
+                "num_key_value_heads": self.kv_heads, "head_dim": self.head_dim,
+                "rms_norm_eps": self.eps, "rope_theta": self.rope_theta,
+                "partial_rotary_factor": self.partial_rotary_factor,
+                "intermediate_size": 4 * self.hidden}
+
+
+def make_attn_tensors(spec: AttnSpec, rng: np.random.Generator) -> dict[str, np.ndarray]:
+    """Attention tensors of one layer, named as the loader names them
+    (``input_layernorm.weight``, ``self_attn.{q,k,v,o}_proj.weight``, biases,
+    ``self_attn.{q,k}_norm.weight``)."""
+    H, nh, nkv, hd = spec.hidden, spec.heads, spec.kv_heads, spec.head_dim
+    t: dict[str, np.ndarray] = {}
+    t["input_layernorm.weight"] = (
+        1.0 + spec.norm_w_std * rng.standard_normal(H, dtype=np.float32)).astype(np.float32)
+    for name, rows in (("q", nh * hd), ("k", nkv * hd), ("v", nkv * hd)):
+        t[f"self_attn.{name}_proj.weight"], _ = _weights(rng, (rows, H), spec.weights)
+        if spec.bias:
+            t[f"self_attn.{name}_proj.bias"] = (
+                rng.standard_normal(rows, dtype=np.float32) * np.float32(0.02))
+    if spec.qk_norm:
+        for name in ("q", "k"):
+            t[f"self_attn.{name}_norm.weight"] = (
+                1.0 + spec.norm_w_std * rng.standard_normal(hd, dtype=np.float32)).astype(np.float32)
+    t["self_attn.o_proj.weight"], _ = _weights(rng, (H, nh * hd), spec.weights)
+    return t
+
+
+def make_attn_case(spec: AttnSpec) -> tuple[np.ndarray, dict[str, np.ndarray]]:
+    rng = np.random.default_rng(spec.seed)
+    x = rng.standard_normal((spec.tokens, spec.hidden), dtype=np.float32)
+    return x, make_attn_tensors(spec, rng)
+
+
+ATTN_SPECS: dict[str, AttnSpec] = {
+    # GLM-4.5/4.7 style: GQA, per-head q/k norm, q/k/v bias, half the head rotated
+    "attn_glm_small": AttnSpec(hidden=256, heads=4, kv_heads=2, head_dim=64, tokens=17, seed=41),
+    # full rotary embedding, no q/k norm, no bias, plain multi-head
+    "attn_glm_fullrope": AttnSpec(hidden=256, heads=4, kv_heads=4, head_dim=64, tokens=5, seed=42,
+                                  qk_norm=False, bias=False, partial_rotary_factor=1.0,
+                                  rope_theta=10000.0, weights="f32"),
+    # a single token (the first decode step of a fresh sequence)
+    "attn_glm_t1": AttnSpec(hidden=256, heads=4, kv_heads=1, head_dim=64, tokens=1, seed=43),
+    # GLM-4.7 head geometry (head_dim 128, 8 query heads per kv head), two key tiles
+    "attn_glm_mid": AttnSpec(hidden=1024, heads=16, kv_heads=2, head_dim=128, tokens=200, seed=44),
+}

@@ -17,6 +17,9 @@ does not implement) it records transformers' ``Glm4MoeMoE.route_tokens_to_expert
 For ``oracle.cases.DENSE_SPECS`` it runs the reference ``_dense_mlp_block`` (the MLP
 of GLM-4 first_k_dense_replace layers, glm4_moe.py:166-172) and stores its output.
 
+For ``oracle.cases.ATTN_SPECS`` it runs the reference ``_attention_block`` (GLM-4 MoE
+attention, glm4_moe.py:112-162) and stores its output.
+
 ``--only NAME ...`` regenerates just those fixtures (the manifest keeps the others).
 
 Fixtures hold outputs and input checksums only; inputs are rebuilt from the seed.
@@ -33,8 +36,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
-from oracle.cases import (DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS, input_checksum,  # noqa: E402
-                          make_case, make_dense_case)
+from oracle.cases import (ATTN_SPECS, DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS,  # noqa: E402
+                          input_checksum, make_attn_case, make_case, make_dense_case)
 from oracle.moe_oracle import rms_norm  # noqa: E402
 
 
@@ -91,6 +94,12 @@ def run_reference_dense(spec, x, t):  # noqa: ANN001, ANN201
         "rms_norm_eps": spec.eps,
     })
     return np.asarray(ex._dense_mlp_block(x, t), dtype=np.float32)
+
+
+def run_reference_attention(spec, x, t):  # noqa: ANN001, ANN201
+    import offload_runtime.executors.glm4_moe as mod
+    ex = mod.GLM4MoeExecutor(spec.hf_config())
+    return np.asarray(ex._attention_block(x, t), dtype=np.float32)
 
 
 def run_hf_sigmoid(spec, x, t):  # noqa: ANN001, ANN201
@@ -150,6 +159,14 @@ def main() -> None:
         out = run_reference_dense(spec, x, t)
         np.savez_compressed(out_dir / f"{name}.npz", out=out, checksum=input_checksum(x, t))
         manifest[name] = {"spec": spec.to_dict(), "source": "reference _dense_mlp_block"}
+        print(name, out.shape)
+    for name, spec in ATTN_SPECS.items():
+        if not want(name):
+            continue
+        x, t = make_attn_case(spec)
+        out = run_reference_attention(spec, x, t)
+        np.savez_compressed(out_dir / f"{name}.npz", out=out, checksum=input_checksum(x, t))
+        manifest[name] = {"spec": spec.to_dict(), "source": "reference _attention_block"}
         print(name, out.shape)
     mpath.write_text(json.dumps(manifest, indent=1, sort_keys=True))
 

@@ -11,8 +11,9 @@ import os
 import numpy as np
 import pytest
 
-from oracle.cases import (DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS, CaseSpec, input_checksum,
-                          make_case, make_dense_case)
+from oracle.attention_oracle import AttnConfig, glm4_attention_block
+from oracle.cases import (ATTN_SPECS, DENSE_SPECS, GOLDEN_SPECS, SIGMOID_SPECS, CaseSpec,
+                          input_checksum, make_attn_case, make_case, make_dense_case)
 from oracle.moe_oracle import (dense_mlp_block, int8_pc_dequantize, int8_pc_quantize, moe_block,
                                permutation, rms_norm, route, select_topk)
 
@@ -101,3 +102,15 @@ def test_int8_per_channel_known_answers() -> None:
     assert q[0, 1] == -127 and q[2, 0] == 127 and q[2, 1] == -127
     deq = int8_pc_dequantize(q, s)
     assert np.max(np.abs(deq - w)) <= float(np.max(s.astype(np.float32))) * 0.5 + 1e-7
+
+
+@pytest.mark.parametrize("name", sorted(ATTN_SPECS))
+def test_attention_oracle_reproduces_reference(name: str) -> None:
+    """glm4_attention_block against the reference's own _attention_block output."""
+    spec = ATTN_SPECS[name]
+    g = _load(name)
+    x, t = make_attn_case(spec)
+    np.testing.assert_array_equal(input_checksum(x, t), g["checksum"],
+                                  err_msg="seeded inputs drifted from the fixture")
+    out = glm4_attention_block(x, t, AttnConfig.from_hf(spec.hf_config()))
+    np.testing.assert_array_equal(out, g["out"])  # bit-exact
