@@ -75,7 +75,15 @@ struct TileCfg {
   static constexpr int kStageA = kBM * kBK * 2;      // f16 A tile, 16 KiB
   static constexpr int kStageA8 = kBM * kBK;         // int8 staging tile, 8 KiB
   static constexpr int kStageB = BN * kBK * 2;
-  static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  // Decode tiles (N <= 64) spread the four K = 16 MMAs of a k-block over four
+  // independent TMEM accumulators ("chains"): with a handful of token columns an
+  // MMA is short, and MMAs that accumulate into one accumulator wait on each
+  // other, so a single chain ran one k-block per ~0.39 us whatever its bytes.  The
+  // epilogue adds the chains in a fixed order.  Wide prefill tiles keep one.
+  static constexpr int kChains = BN <= 64 ? 4 : 1;
+  static constexpr int kAccCols = kChains * BN;  // one accumulator buffer
+  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
+                                   : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
   // Epilogue warps: a 256-column accumulator takes 8 (each TMEM lane quarter
   // twice, splitting the columns) so that draining a tile stays shorter than
   // its MMAs; narrow decode tiles keep 4.
@@ -347,7 +355,8 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + buf * BN;
+        constexpr int CH = TileCfg<BN>::kChains;
+        const uint32_t d = tmem_base + buf * TileCfg<BN>::kAccCols;
         const uint32_t idesc = idesc_f16_f32(kBM, (t.nvalid + 15) & ~15);
         bool ok = true;
         for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
@@ -363,8 +372,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
           const uint32_t a0 = smem_u32(sA + s * SA), b0 = smem_u32(sB + s * SB);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            tc_mma_f16(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
-                       (kb > t.kb0 || k > 0) ? 1u : 0u);
+            // MMA k feeds chain k % CH; a chain's first MMA of the tile starts it
+            tc_mma_f16(d + (k % CH) * BN, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
+                       (kb > t.kb0 || k >= CH) ? 1u : 0u);
           }
           tc_commit(&empty[s]);
           issued = true;
@@ -414,11 +424,20 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
         rs = sh ? args.scale_shared[mrow]
                 : args.scale_routed[static_cast<size_t>(t.group) * args.rows_a_routed + mrow];
       }
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      constexpr int CH = TileCfg<BN>::kChains;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * TileCfg<BN>::kAccCols;
       const int ncol = (t.nvalid + 15) & ~15;
       for (int c0 = cfirst; c0 < ncol; c0 += cstep) {
         float v[16];
         tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int ch = 1; ch < CH; ++ch) {  // add the other chains, in chain order
+          float w[16];
+          tmem_ld16(taddr + ch * BN + c0, w);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += w[i];
+        }
         if constexpr (BN == kSplitTileRows) {
           if (nsplit > 1) {
             // K split: publish this split's partial, count arrivals; the last

@@ -96,8 +96,8 @@ def test_golden_parity(name: str, fmt: str) -> None:
 
 def test_golden_sigmoid_decode() -> None:
     """HF GLM-4.x sigmoid routing through the decode path (64 tokens, one-CTA tail):
-    ids bit-exact and weights to 1e-5 against the fixture pinned to transformers,
-    block output against the oracle's sigmoid mode."""
+    expert sets exact and weights to 1e-5 against the fixture pinned to
+    transformers, slot order and block output against the oracle's sigmoid mode."""
     from oracle.cases import SIGMOID_SPECS
     spec = SIGMOID_SPECS["glm_sigmoid"]
     with np.load(os.path.join(GOLDEN, "glm_sigmoid.npz")) as z:
@@ -110,9 +110,16 @@ def test_golden_sigmoid_decode() -> None:
     r = ml.route(xd)
     out = ml.forward(xd)
     ml.status()
-    np.testing.assert_array_equal(r["topk_ids"].cpu().numpy(), g["topk_ids"])
-    np.testing.assert_allclose(r["topk_w"].cpu().numpy(), g["topk_w"], rtol=1e-5, atol=1e-7)
-    ref, _aux = moe_block(x, t, cfg)
+    # transformers returns the chosen experts unordered (torch.topk, sorted=False):
+    # compare each token's expert set, and each expert's weight by id
+    got_ids, got_w = r["topk_ids"].cpu().numpy(), r["topk_w"].cpu().numpy()
+    go, ho = np.argsort(got_ids, axis=1), np.argsort(g["topk_ids"], axis=1)
+    np.testing.assert_array_equal(np.take_along_axis(got_ids, go, 1),
+                                  np.take_along_axis(g["topk_ids"], ho, 1))
+    np.testing.assert_allclose(np.take_along_axis(got_w, go, 1),
+                               np.take_along_axis(g["topk_w"], ho, 1), rtol=1e-5, atol=1e-7)
+    ref, aux = moe_block(x, t, cfg)
+    np.testing.assert_array_equal(got_ids, aux["topk_ids"])  # descending-score slot order
     err = rel_l2(out.cpu().numpy(), ref)
     assert err <= TOL_16, f"rel-L2 {err:.3e}"
     ml.close()
