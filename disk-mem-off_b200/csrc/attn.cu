@@ -1,0 +1,727 @@
+// GLM-4 MoE attention block on the device: replaces
+// GLM4MoeExecutor._attention_block (offload_runtime/executors/glm4_moe.py:112-162),
+// which the reference runs in NumPy after copying the whole layer back to the host:
+//
+//   h   = rms_norm(x, input_layernorm.weight)                      (launch_norm_rows)
+//   qkv = h . [Wq; Wk; Wv]^T                  tcgen05 GEMM, fp32 K-split planes
+//   q, k, v: + bias, per-head RMS norm * q_norm / k_norm, partial rotate-half
+//            RoPE at positions 0..T-1                               (attn_qkv_kernel)
+//   o   = softmax(q k^T / sqrt(d) + causal mask) v, GQA              (attn_fwd_kernel)
+//   out = x + o . Wo^T                         tcgen05 GEMM planes + attn_out_kernel
+//
+// attn_fwd_kernel is a flash-attention kernel on the 5th-generation tensor cores:
+// one CTA per (128-query tile, head); S = Q K^T and O += P V are tcgen05.mma with
+// operands in shared memory (Q, K and V^T tiles by TMA, P written by the softmax
+// warps) and accumulators in TMEM; the softmax warps keep the running row max /
+// sum in registers and rescale O in TMEM when the max moves.  Keys arrive in
+// 128-key tiles through a two-stage ring, and the S of the next tile is computed
+// while the softmax works on the current one.  All waits are bounded.
+#include <math.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+constexpr int kAttnTile = 128;  // queries per CTA and keys per tile
+
+#define MOE_CUDA_RET(call)                  \
+  do {                                      \
+    const cudaError_t e_ = (call);          \
+    if (e_ != cudaSuccess) return e_;       \
+  } while (0)
+
+struct AttnPlan {
+  MoeAttnConfig cfg{};
+  int H = 0, nh = 0, nkv = 0, hd = 0, rot = 0, nqkv = 0, nout = 0;
+  int num_sms = 148;
+  bool bound = false;
+  bool has_bias = false;
+  bool has_qk_norm = false;
+  void* alloc = nullptr;
+  size_t bytes = 0;
+  __half* wqkv = nullptr;  // [nqkv][H] f16: q rows, then k rows, then v rows
+  __half* wo = nullptr;    // [H][nh * hd] f16
+  float* bqkv = nullptr;   // [nqkv] (zeros without bias)
+  float* qn = nullptr;     // [hd] q_norm weight
+  float* kn = nullptr;     // [hd] k_norm weight
+  float* win = nullptr;    // [H] input_layernorm weight
+  int* d_err = nullptr;
+  CUtensorMap tm_qkv{}, tm_o{};
+};
+
+struct AttnWs {
+  size_t rms, h16, qkv, q, k, vt, o16, oplanes, total;
+  int tpad, s1, s2;
+};
+
+static size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static AttnWs attn_ws(const AttnPlan& a, int T) {
+  AttnWs w{};
+  w.tpad = (T + kAttnTile - 1) / kAttnTile * kAttnTile;
+  w.s1 = dense_gemm_splits(a.nqkv, T, a.H, a.num_sms);
+  w.s2 = dense_gemm_splits(a.H, T, a.nout, a.num_sms);
+  size_t o = 0;
+  auto take = [&](size_t b) { const size_t at = o; o = a256(o + b); return at; };
+  w.rms = take(static_cast<size_t>(T) * 4);
+  w.h16 = take(static_cast<size_t>(T) * a.H * 2);
+  w.qkv = take(static_cast<size_t>(w.s1) * T * a.nqkv * 4);
+  w.q = take(static_cast<size_t>(a.nh) * w.tpad * a.hd * 2);
+  w.k = take(static_cast<size_t>(a.nkv) * w.tpad * a.hd * 2);
+  w.vt = take(static_cast<size_t>(a.nkv) * a.hd * w.tpad * 2);
+  w.o16 = take(static_cast<size_t>(T) * a.nout * 2);
+  w.oplanes = take(static_cast<size_t>(w.s2) * T * a.H * 4);
+  w.total = o;
+  return w;
+}
+
+// ------------------------------------------------------------------ q / k / v
+// One CTA per (padded) token, a warp per head vector.  Sums the GEMM's K-split
+// planes in split order, adds the bias, applies the per-head RMS norm
+// (x / sqrt(mean(x^2) + eps) * w, _common.py:139-142) to q and k and the
+// rotate-half RoPE (_common.py:106-126: frequencies theta^(-j / half) and angles
+// in float64, angles rounded to float32) to their first `rot` dims, then writes
+// q and k as f16 rows [head][tpad][hd] and v transposed [kv head][hd][tpad] (the
+// K-major B operand of O += P V).  Rows past T are written as zeros.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_qkv_kernel(
+    const float* __restrict__ planes, int nsplit, int T, int tpad, int nh, int nkv,
+    const float* __restrict__ bias, const float* __restrict__ qn, const float* __restrict__ kn,
+    int rot, float theta, float eps, __half* __restrict__ q16, __half* __restrict__ k16,
+    __half* __restrict__ vt16) {
+  pdl_enter();
+  constexpr int V = HD / 32;
+  __shared__ float sh[8][HD];
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = nh + 2 * nkv;
+  const size_t nqkv = static_cast<size_t>(heads) * HD;
+  const int half = rot / 2;
+  for (int hh = warp; hh < heads; hh += 8) {
+    const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
+    float v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int d = lane * V + i;
+      float acc = 0.f;
+      if (t < T) {
+        for (int s = 0; s < nsplit; ++s) acc += planes[(static_cast<size_t>(s) * T + t) * nqkv + hh * HD + d];
+        acc += bias[hh * HD + d];
+      }
+      v[i] = acc;
+    }
+    if (t < T && kind < 2) {
+      const float* nw = kind == 0 ? qn : kn;
+      if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < V; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = sqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = (v[i] / r) * nw[lane * V + i];
+      }
+      if (half > 0) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) sh[warp][lane * V + i] = v[i];
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const int d = lane * V + i;
+          if (d < rot) {
+            const int j = d < half ? d : d - half;
+            const double freq = 1.0 / pow(static_cast<double>(theta),
+                                          static_cast<double>(j) / static_cast<double>(half));
+            const float ang = static_cast<float>(static_cast<double>(t) * freq);
+            const float c = static_cast<float>(cos(static_cast<double>(ang)));
+            const float sn = static_cast<float>(sin(static_cast<double>(ang)));
+            v[i] = d < half ? v[i] * c - sh[warp][d + half] * sn
+                            : v[i] * c + sh[warp][d - half] * sn;
+          }
+        }
+        __syncwarp();
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int d = lane * V + i;
+      const __half hv = __float2half_rn(v[i]);
+      if (kind == 0) q16[(static_cast<size_t>(hh) * tpad + t) * HD + d] = hv;
+      else if (kind == 1) k16[(static_cast<size_t>(hh - nh) * tpad + t) * HD + d] = hv;
+      else vt16[(static_cast<size_t>(hh - nh - nkv) * HD + d) * tpad + t] = hv;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ flash attention
+template <int HD>
+struct FaCfg {
+  static constexpr int kQ = kAttnTile * HD * 2;        // Q tile: HD / 64 blocks of 16 KiB
+  static constexpr int kK = kAttnTile * HD * 2;        // one K stage
+  static constexpr int kVblk = HD * 128;               // one 64-key block of V^T (HD rows x 128 B)
+  static constexpr int kV = 2 * kVblk;                 // one V^T stage (128 keys)
+  static constexpr int kP = kAttnTile * kAttnTile * 2; // P tile: 2 blocks of 64 keys
+  // at least 120 KiB, so that one CTA holds an SM (and all 512 TMEM columns) for
+  // either head size: a second CTA would only wait in tcgen05.alloc
+  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + kP + 256;
+  static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
+  static constexpr uint32_t kTmemCols = 512;           // S[2] at 0 / 128, O at 256
+};
+
+struct FaArgs {
+  CUtensorMap tq, tk, tv;
+  int T, tpad, nh, nkv, nqt;
+  float scale_log2;  // log2(e) / sqrt(head_dim)
+  __half* out16;     // [T][nh * HD]
+  int* err;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant__ FaArgs args) {
+  using C = FaCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + C::kQ;
+  uint8_t* sV = sK + 2 * C::kK;
+  uint8_t* sP = sV + 2 * C::kV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kP);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* mma_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = args.nqt - 1 - static_cast<int>(blockIdx.x);  // long (late) tiles first
+  const int h = blockIdx.y;
+  const int kvh = h / (args.nh / args.nkv);
+  const int q0 = qt * kAttnTile;
+  const int nkt = qt + 1;  // causal: key tiles 0..qt
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&kv_full[b], 1);
+      mbar_init(&kv_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&args.tq);
+    tma_prefetch_desc(&args.tk);
+    tma_prefetch_desc(&args.tv);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, C::kQ);
+#pragma unroll
+      for (int kb = 0; kb < HD / 64; ++kb)
+        tma_load_2d(sQ + kb * 16384, &args.tq, kb * 64, h * args.tpad + q0, q_full);
+      int issued = 0;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          *abort_flag = 1;
+          record_error(args.err, DEV_TIMEOUT_EMPTY);
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+#pragma unroll
+        for (int kb = 0; kb < HD / 64; ++kb)
+          tma_load_2d(sK + s * C::kK + kb * 16384, &args.tk, kb * 64, kvh * args.tpad + j * kAttnTile,
+                      &kv_full[s]);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_2d(sV + s * C::kV + kb * C::kVblk, &args.tv, j * kAttnTile + kb * 64, kvh * HD,
+                      &kv_full[s]);
+        issued = j + 1;
+      }
+      // every copy this thread started must land before the CTA exits
+      mbar_wait_drain(q_full, 0);
+      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) mbar_wait_drain(&kv_full[j & 1], (j >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_f16_f32(kAttnTile, kAttnTile);
+      const uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD);
+      const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const int kb = k >> 2, kk = k & 3;
+          tc_mma_f16(tmem_base + s * kAttnTile, sw128_desc(aq + kb * 16384 + kk * 32),
+                     sw128_desc(ak + s * C::kK + kb * 16384 + kk * 32), idesc_s, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < nkt; ++j) {
+        if (j + 1 < nkt && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_bounded(p_full, j & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int s = j & 1;
+#pragma unroll
+        for (int k = 0; k < kAttnTile / 16; ++k) {
+          const int kb = k >> 2, kk = k & 3;
+          tc_mma_f16(tmem_base + 2 * kAttnTile, sw128_desc(ap + kb * 16384 + kk * 32),
+                     sw128_desc(av + s * C::kV + kb * C::kVblk + kk * 32), idesc_o,
+                     (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(o_done);
+        tc_commit(&kv_empty[s]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        record_error(args.err, DEV_TIMEOUT_FULL);
+      }
+      tc_commit(mma_done);  // no MMA may still write TMEM when it is released
+      mbar_wait_drain(mma_done, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 2-5)
+    const int qrow = (warp & 3) * 32 + lane;  // TMEM lane = query row of the tile
+    const int qi = q0 + qrow;
+    const uint32_t lbase = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t ocol = 2 * kAttnTile;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      const int s = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[s], (j >> 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sc[kAttnTile];
+#pragma unroll
+      for (int c = 0; c < kAttnTile / 32; ++c) {
+        float part[32];
+        tmem_ld32(lbase + s * kAttnTile + c * 32, part);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sc[c * 32 + i] = part[i];
+      }
+      // S is in registers: the MMA may overwrite this buffer with tile j + 2
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const bool diag = j == qt;  // keys after the query are masked (causal)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kAttnTile; ++c) {
+        if (diag && c > qrow) sc[c] = -INFINITY;
+        mx = fmaxf(mx, sc[c]);
+      }
+      const float m_new = fmaxf(m, mx);  // finite: key 0 is never masked
+      const float alpha = exp2f((m - m_new) * args.scale_log2);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kAttnTile; ++c) {
+        sc[c] = exp2f((sc[c] - m_new) * args.scale_log2);
+        rs += sc[c];
+      }
+      l = l * alpha + rs;
+      if (j > 0) {
+        // P V of tile j - 1 has finished: O is complete up to j - 1 and P is free
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (j - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < HD / 16; ++c) {
+            float o[16];
+            tmem_ld16(lbase + ocol + c * 16, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tmem_st16(lbase + ocol + c * 16, o);
+          }
+        }
+      }
+      // P row -> the 128-byte-swizzled K-major A operand (chunk c of row r at c ^ (r & 7))
+#pragma unroll
+      for (int cb = 0; cb < kAttnTile / 8; ++cb) {
+        __half2 hp[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hp[i] = __floats2half2_rn(sc[cb * 8 + 2 * i], sc[cb * 8 + 2 * i + 1]);
+        const int blk = cb >> 3, ch = cb & 7;
+        *reinterpret_cast<uint4*>(sP + blk * 16384 + qrow * 128 + ((ch ^ (qrow & 7)) << 4)) =
+            *reinterpret_cast<uint4*>(hp);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      m = m_new;
+    }
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (nkt - 1) & 1, abort_flag))) ok = false;
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const int ld = args.nh * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 16; ++c) {
+        float o[16];
+        tmem_ld16(lbase + ocol + c * 16, o);
+        __half2 hv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+        if (qi < args.T) {
+          uint4* dst = reinterpret_cast<uint4*>(args.out16 + static_cast<size_t>(qi) * ld + h * HD + c * 16);
+          dst[0] = *reinterpret_cast<uint4*>(&hv[0]);
+          dst[1] = *reinterpret_cast<uint4*>(&hv[4]);
+        }
+      }
+    } else {
+      *abort_flag = 1;
+      record_error(args.err, DEV_TIMEOUT_TMEM_FULL);
+    }
+  }
+  pdl_release();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// out = x + sum_s planes[s] (the o_proj K-split planes, added in split order)
+__global__ void __launch_bounds__(256) attn_out_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ planes, int nsplit,
+                                                       size_t n, float* __restrict__ out) {
+  pdl_enter();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < nsplit; ++s) acc += planes[static_cast<size_t>(s) * n + i];
+    out[i] = x[i] + acc;
+  }
+}
+
+template <int HD>
+static cudaError_t attn_launch(const AttnPlan& a, const AttnWs& w, char* ws, const float* x,
+                               float* out, int T, cudaStream_t s) {
+  MOE_CUDA_RET(launch_norm_rows(x, a.win, a.H, a.cfg.rms_norm_eps, T,
+                                reinterpret_cast<float*>(ws + w.rms),
+                                reinterpret_cast<__half*>(ws + w.h16), a.d_err, s));
+  MOE_CUDA_RET(launch_dense_gemm(a.tm_qkv, a.nqkv, a.H, reinterpret_cast<const __half*>(ws + w.h16), T,
+                                 reinterpret_cast<float*>(ws + w.qkv), w.s1, a.d_err, a.num_sms, s));
+  MOE_PDL(attn_qkv_kernel<HD>, dim3(w.tpad), dim3(256), 0, s, reinterpret_cast<const float*>(ws + w.qkv),
+          w.s1, T, w.tpad, a.nh, a.nkv, a.bqkv, a.has_qk_norm ? a.qn : nullptr,
+          a.has_qk_norm ? a.kn : nullptr, a.rot, a.cfg.rope_theta, a.cfg.rms_norm_eps,
+          reinterpret_cast<__half*>(ws + w.q), reinterpret_cast<__half*>(ws + w.k),
+          reinterpret_cast<__half*>(ws + w.vt));
+  FaArgs fa{};
+  std::string err;
+  if (!make_tmap_2d(&fa.tq, ws + w.q, false, HD, static_cast<uint64_t>(a.nh) * w.tpad, 64, kAttnTile,
+                    true, &err) ||
+      !make_tmap_2d(&fa.tk, ws + w.k, false, HD, static_cast<uint64_t>(a.nkv) * w.tpad, 64, kAttnTile,
+                    true, &err) ||
+      !make_tmap_2d(&fa.tv, ws + w.vt, false, w.tpad, static_cast<uint64_t>(a.nkv) * HD, 64, HD, true,
+                    &err)) {
+    set_error(err);
+    return cudaErrorInvalidValue;
+  }
+  fa.T = T;
+  fa.tpad = w.tpad;
+  fa.nh = a.nh;
+  fa.nkv = a.nkv;
+  fa.nqt = w.tpad / kAttnTile;
+  fa.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(HD)));
+  fa.out16 = reinterpret_cast<__half*>(ws + w.o16);
+  fa.err = a.d_err;
+  constexpr size_t smem = FaCfg<HD>::kSmem;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    const cudaError_t st = cudaFuncSetAttribute(attn_fwd_kernel<HD>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem));
+    if (st != cudaSuccess) return st;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  MOE_PDL(attn_fwd_kernel<HD>, dim3(fa.nqt, a.nh), dim3(192), smem, s, fa);
+  MOE_CUDA_RET(launch_dense_gemm(a.tm_o, a.H, a.nout, reinterpret_cast<const __half*>(ws + w.o16), T,
+                                 reinterpret_cast<float*>(ws + w.oplanes), w.s2, a.d_err, a.num_sms, s));
+  const size_t n = static_cast<size_t>(T) * a.H;
+  const int grid = static_cast<int>(std::min<size_t>((n + 255) / 256, static_cast<size_t>(a.num_sms) * 8));
+  MOE_PDL(attn_out_kernel, dim3(grid), dim3(256), 0, s, x, reinterpret_cast<const float*>(ws + w.oplanes),
+          w.s2, n, out);
+  return cudaSuccess;
+}
+
+}  // namespace moe
+
+// ====================================================================== C ABI
+using namespace moe;
+
+struct MoeAttn {
+  AttnPlan a;
+};
+
+namespace {
+
+int afail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+#define MOE_ATT_CUDA(call)                                                               \
+  do {                                                                                   \
+    const cudaError_t st_ = (call);                                                      \
+    if (st_ != cudaSuccess) return afail(MOE_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(st_)); \
+  } while (0)
+
+int parse_dtype_name(const char* d) {
+  const std::string s(d ? d : "");
+  if (s == "float32" || s == "<f4" || s == "f4") return SRC_F32;
+  if (s == "float16" || s == "<f2" || s == "f2") return SRC_F16;
+  if (s == "bfloat16" || s == "bf16") return SRC_BF16;
+  return -1;
+}
+
+// the part of a tensor name after an optional "model.layers.N." prefix
+std::string short_name(const char* n) {
+  std::string s(n ? n : "");
+  const size_t p = s.find("self_attn.");
+  if (p != std::string::npos) return s.substr(p);
+  const size_t q = s.find("input_layernorm.weight");
+  if (q != std::string::npos) return s.substr(q);
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_attn_create(const MoeAttnConfig* cfg, MoeAttn** out) {
+  if (!cfg || !out) return afail(MOE_ERR_INVALID, "null argument");
+  const MoeAttnConfig& c = *cfg;
+  if (c.head_dim != 64 && c.head_dim != 128)
+    return afail(MOE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads != 0)
+    return afail(MOE_ERR_INVALID, "heads must be a positive multiple of kv_heads");
+  if (c.hidden <= 0 || c.hidden % 64 != 0)
+    return afail(MOE_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  if (c.rotary_dim < 0 || c.rotary_dim > c.head_dim || c.rotary_dim % 2 != 0)
+    return afail(MOE_ERR_INVALID, "rotary_dim must be even and at most head_dim");
+  if (c.max_tokens <= 0) return afail(MOE_ERR_INVALID, "max_tokens must be positive");
+  if (!(c.rope_theta > 0.f)) return afail(MOE_ERR_INVALID, "rope_theta must be positive");
+  MOE_ATT_CUDA(cudaSetDevice(c.device));
+  MoeAttn* h = new MoeAttn();
+  AttnPlan& a = h->a;
+  a.cfg = c;
+  a.H = c.hidden;
+  a.nh = c.heads;
+  a.nkv = c.kv_heads;
+  a.hd = c.head_dim;
+  a.rot = c.rotary_dim;
+  a.nqkv = (a.nh + 2 * a.nkv) * a.hd;
+  a.nout = a.nh * a.hd;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device);
+  a.num_sms = sms > 0 ? sms : 148;
+  cudaError_t st = cudaMalloc(&a.d_err, sizeof(int));
+  if (st == cudaSuccess) st = cudaMemset(a.d_err, 0, sizeof(int));
+  if (st != cudaSuccess) {
+    delete h;
+    return afail(MOE_ERR_CUDA, std::string("cudaMalloc(error word): ") + cudaGetErrorString(st));
+  }
+  *out = h;
+  return MOE_OK;
+}
+
+int moe_attn_destroy(MoeAttn* h) {
+  if (!h) return MOE_OK;
+  cudaSetDevice(h->a.cfg.device);
+  if (h->a.alloc) cudaFree(h->a.alloc);
+  if (h->a.d_err) cudaFree(h->a.d_err);
+  delete h;
+  return MOE_OK;
+}
+
+uint64_t moe_attn_weight_bytes(const MoeAttn* h) { return h ? h->a.bytes : 0; }
+
+int moe_attn_bind(MoeAttn* h, const void* blob_dev, uint64_t blob_bytes, const MoeTensorDesc* descs,
+                  int32_t n_descs, void* stream) {
+  if (!h || !blob_dev || !descs || n_descs <= 0) return afail(MOE_ERR_INVALID, "null argument");
+  AttnPlan& a = h->a;
+  MOE_ATT_CUDA(cudaSetDevice(a.cfg.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  struct Src {
+    const char* ptr = nullptr;
+    int dtype = -1;
+  };
+  Src wq, wk, wv, wo, bq, bk, bv, qn, kn, win;
+  const char* base = static_cast<const char*>(blob_dev);
+  const int H = a.H, nq = a.nh * a.hd, nk = a.nkv * a.hd, hd = a.hd;
+  for (int i = 0; i < n_descs; ++i) {
+    const MoeTensorDesc& d = descs[i];
+    const std::string n = short_name(d.name);
+    Src* dst = nullptr;
+    int64_t rows = 0, cols = 1;
+    if (n == "self_attn.q_proj.weight") { dst = &wq; rows = nq; cols = H; }
+    else if (n == "self_attn.k_proj.weight") { dst = &wk; rows = nk; cols = H; }
+    else if (n == "self_attn.v_proj.weight") { dst = &wv; rows = nk; cols = H; }
+    else if (n == "self_attn.o_proj.weight") { dst = &wo; rows = H; cols = nq; }
+    else if (n == "self_attn.q_proj.bias") { dst = &bq; rows = nq; }
+    else if (n == "self_attn.k_proj.bias") { dst = &bk; rows = nk; }
+    else if (n == "self_attn.v_proj.bias") { dst = &bv; rows = nk; }
+    else if (n == "self_attn.q_norm.weight") { dst = &qn; rows = hd; }
+    else if (n == "self_attn.k_norm.weight") { dst = &kn; rows = hd; }
+    else if (n == "input_layernorm.weight") { dst = &win; rows = H; }
+    if (!dst) continue;
+    const int dt = parse_dtype_name(d.dtype);
+    if (dt < 0) return afail(MOE_ERR_UNSUPPORTED, std::string("unsupported dtype for ") + d.name);
+    const int64_t esz = dt == SRC_F32 ? 4 : 2;
+    int64_t numel = 1;
+    for (int k = 0; k < d.ndim && k < 2; ++k) numel *= d.shape[k];
+    const bool shape_ok = (cols == 1) ? (numel == rows) : (d.ndim == 2 && d.shape[0] == rows && d.shape[1] == cols);
+    if (!shape_ok || numel * esz != d.nbytes)
+      return afail(MOE_ERR_INVALID, std::string("shape / nbytes mismatch for ") + d.name);
+    if (d.offset < 0 || static_cast<uint64_t>(d.offset + d.nbytes) > blob_bytes)
+      return afail(MOE_ERR_INVALID, std::string("tensor outside the blob: ") + d.name);
+    *dst = Src{base + d.offset, dt};
+  }
+  if (!wq.ptr) return afail(MOE_ERR_MISSING_TENSOR, "self_attn.q_proj.weight");
+  if (!wk.ptr) return afail(MOE_ERR_MISSING_TENSOR, "self_attn.k_proj.weight");
+  if (!wv.ptr) return afail(MOE_ERR_MISSING_TENSOR, "self_attn.v_proj.weight");
+  if (!wo.ptr) return afail(MOE_ERR_MISSING_TENSOR, "self_attn.o_proj.weight");
+  if (!win.ptr) return afail(MOE_ERR_MISSING_TENSOR, "input_layernorm.weight");
+  if ((qn.ptr != nullptr) != (kn.ptr != nullptr))
+    return afail(MOE_ERR_MISSING_TENSOR, "q_norm and k_norm come as a pair");
+  size_t o = 0;
+  auto take = [&](size_t b) { const size_t at = o; o = a256(o + b); return at; };
+  const size_t o_wqkv = take(static_cast<size_t>(a.nqkv) * H * 2);
+  const size_t o_wo = take(static_cast<size_t>(H) * a.nout * 2);
+  const size_t o_b = take(static_cast<size_t>(a.nqkv) * 4);
+  const size_t o_qn = take(static_cast<size_t>(hd) * 4);
+  const size_t o_kn = take(static_cast<size_t>(hd) * 4);
+  const size_t o_win = take(static_cast<size_t>(H) * 4);
+  const size_t o_flag = take(16);
+  if (!a.alloc) {
+    MOE_ATT_CUDA(cudaMalloc(&a.alloc, o));
+    a.bytes = o;
+  }
+  char* wb = static_cast<char*>(a.alloc);
+  a.wqkv = reinterpret_cast<__half*>(wb + o_wqkv);
+  a.wo = reinterpret_cast<__half*>(wb + o_wo);
+  a.bqkv = reinterpret_cast<float*>(wb + o_b);
+  a.qn = reinterpret_cast<float*>(wb + o_qn);
+  a.kn = reinterpret_cast<float*>(wb + o_kn);
+  a.win = reinterpret_cast<float*>(wb + o_win);
+  int* range_err = reinterpret_cast<int*>(wb + o_flag);
+  MOE_ATT_CUDA(cudaMemsetAsync(range_err, 0, sizeof(int), s));
+  MOE_ATT_CUDA(cudaMemsetAsync(a.bqkv, 0, static_cast<size_t>(a.nqkv) * 4, s));
+  MOE_ATT_CUDA(launch_pack_rows(wq.ptr, wq.dtype, a.wqkv, false, nullptr, nq, H, range_err, s));
+  MOE_ATT_CUDA(launch_pack_rows(wk.ptr, wk.dtype, a.wqkv + static_cast<size_t>(nq) * H, false, nullptr, nk, H,
+                                range_err, s));
+  MOE_ATT_CUDA(launch_pack_rows(wv.ptr, wv.dtype, a.wqkv + static_cast<size_t>(nq + nk) * H, false, nullptr,
+                                nk, H, range_err, s));
+  MOE_ATT_CUDA(launch_pack_rows(wo.ptr, wo.dtype, a.wo, false, nullptr, H, nq, range_err, s));
+  if (bq.ptr) MOE_ATT_CUDA(launch_to_f32(bq.ptr, bq.dtype, a.bqkv, nq, s));
+  if (bk.ptr) MOE_ATT_CUDA(launch_to_f32(bk.ptr, bk.dtype, a.bqkv + nq, nk, s));
+  if (bv.ptr) MOE_ATT_CUDA(launch_to_f32(bv.ptr, bv.dtype, a.bqkv + nq + nk, nk, s));
+  if (qn.ptr) {
+    MOE_ATT_CUDA(launch_to_f32(qn.ptr, qn.dtype, a.qn, hd, s));
+    MOE_ATT_CUDA(launch_to_f32(kn.ptr, kn.dtype, a.kn, hd, s));
+  }
+  MOE_ATT_CUDA(launch_to_f32(win.ptr, win.dtype, a.win, H, s));
+  int h_range = 0;
+  MOE_ATT_CUDA(cudaMemcpyAsync(&h_range, range_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MOE_ATT_CUDA(cudaStreamSynchronize(s));
+  if (h_range) return afail(MOE_ERR_RANGE, "an attention weight does not fit f16 (|w| > 65504)");
+  a.has_bias = bq.ptr || bk.ptr || bv.ptr;
+  a.has_qk_norm = qn.ptr != nullptr;
+  std::string err;
+  if (!make_tmap_2d(&a.tm_qkv, a.wqkv, false, H, a.nqkv, kBK, kBM, true, &err) ||
+      !make_tmap_2d(&a.tm_o, a.wo, false, a.nout, H, kBK, kBM, true, &err))
+    return afail(MOE_ERR_CUDA, err);
+  a.bound = true;
+  return MOE_OK;
+}
+
+uint64_t moe_attn_workspace_bytes(const MoeAttn* h, int32_t T) {
+  if (!h || T <= 0) return 0;
+  return attn_ws(h->a, T).total;
+}
+
+int moe_attn_forward(MoeAttn* h, const float* x_dev, float* out_dev, int32_t T, void* workspace,
+                     uint64_t workspace_bytes, void* stream) {
+  if (!h) return afail(MOE_ERR_INVALID, "null attention plan");
+  AttnPlan& a = h->a;
+  if (!a.bound) return afail(MOE_ERR_NOT_BOUND, "moe_attn_bind has not been called");
+  if (T < 0 || T > a.cfg.max_tokens) return afail(MOE_ERR_INVALID, "T outside [0, max_tokens]");
+  if (T == 0) return MOE_OK;
+  if (!x_dev || !out_dev) return afail(MOE_ERR_INVALID, "null x / out");
+  if (x_dev == out_dev) return afail(MOE_ERR_INVALID, "x and out may not alias");
+  if (misaligned16(x_dev) || misaligned16(out_dev))
+    return afail(MOE_ERR_INVALID, "x and out must be 16-byte aligned");
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return afail(MOE_ERR_WORKSPACE, "workspace must be a 256-byte aligned device pointer");
+  const AttnWs w = attn_ws(a, T);
+  if (workspace_bytes < w.total) return afail(MOE_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const cudaError_t st = a.hd == 128 ? attn_launch<128>(a, w, ws, x_dev, out_dev, T, s)
+                                     : attn_launch<64>(a, w, ws, x_dev, out_dev, T, s);
+  if (st != cudaSuccess) return afail(MOE_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(st));
+  return MOE_OK;
+}
+
+int moe_attn_status(MoeAttn* h, void* stream) {
+  if (!h) return afail(MOE_ERR_INVALID, "null attention plan");
+  AttnPlan& a = h->a;
+  MOE_ATT_CUDA(cudaSetDevice(a.cfg.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  MOE_ATT_CUDA(cudaMemcpyAsync(&v, a.d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MOE_ATT_CUDA(cudaMemsetAsync(a.d_err, 0, sizeof(int), s));
+  MOE_ATT_CUDA(cudaStreamSynchronize(s));
+  if (v == DEV_OK) return MOE_OK;
+  if (v >= DEV_TIMEOUT_FULL && v <= DEV_TIMEOUT_CONV)
+    return afail(MOE_ERR_TIMEOUT, "an attention wait ran out of time (code " + std::to_string(v) + ")");
+  return afail(MOE_ERR_DEVICE, "an attention kernel reported device error code " + std::to_string(v));
+}
+
+}  // extern "C"

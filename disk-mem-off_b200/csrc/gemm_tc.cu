@@ -759,4 +759,57 @@ cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T
   return run_gemm<BN, MODE_ROUTER, false>(a, grid, s);
 }
 
+// A plain f16 GEMM on the same kernel (router-grid mode): planes[s][t][r] = the
+// K-split s partial of sum_k A[r][k] * B[t][k], A = `a_map` (m_rows x K, f16,
+// 64 x 128 boxes), B = b (T x K f16, row-major).  The caller adds the planes in
+// split order (the attention projections fold that sum into their next kernel).
+int dense_gemm_splits(int m_rows, int T, int K, int num_sms) {
+  const int units = ((m_rows + kBM - 1) / kBM) * ((T + 255) / 256);
+  const int nk = (K + kBK - 1) / kBK;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int sp = 1; sp <= kRouterMaxSplit && nk / sp >= 8; ++sp) {
+    const int u = units * sp;
+    const int rounds = (u + num_sms - 1) / num_sms;
+    const double eff = static_cast<double>(u) / (static_cast<double>(rounds) * num_sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_dense_gemm(const CUtensorMap& a_map, int m_rows, int K, const __half* b, int T,
+                              float* planes, int splits, int* err, int num_sms, cudaStream_t s) {
+  constexpr int BN = 256;
+  GemmArgs a{};
+  std::string emsg;
+  a.a_routed = a_map;
+  a.a_shared = a_map;
+  if (!make_tmap_2d(&a.b_routed, b, false, K, T, kBK, BN, true, &emsg)) {
+    set_error(emsg);
+    return cudaErrorInvalidValue;
+  }
+  a.b_shared = a.b_routed;
+  a.router_grid = 1;
+  const int mt = (m_rows + kBM - 1) / kBM;
+  a.implicit_ntn = (T + BN - 1) / BN;
+  a.implicit_rows = T;
+  a.implicit_splits = splits;
+  a.max_tiles = mt * a.implicit_ntn * splits;
+  a.n_local = 1;
+  a.rows_a_routed = 0;
+  a.m_limit_routed = m_rows;
+  a.m_limit_shared = m_rows;
+  a.k_routed = K;
+  a.k_shared = K;
+  a.logits = planes;
+  a.logit_ld = m_rows;
+  a.logit_scale = 1.0f;
+  a.err = err;
+  const int grid = a.max_tiles < num_sms ? a.max_tiles : num_sms;
+  return run_gemm<BN, MODE_ROUTER, false>(a, grid, s);
+}
+
 }  // namespace moe

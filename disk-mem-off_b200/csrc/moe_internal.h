@@ -195,6 +195,13 @@ cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const fl
 cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
 bool route_uses_tc_router(const Plan& p, int T);
 int router_tc_splits(const Plan& p, int T);
+// Plain f16 GEMM with fp32 K-split planes (attention projections); see gemm_tc.cu.
+int dense_gemm_splits(int m_rows, int T, int K, int num_sms);
+cudaError_t launch_dense_gemm(const CUtensorMap& a_map, int m_rows, int K, const __half* b, int T,
+                              float* planes, int splits, int* err, int num_sms, cudaStream_t s);
+// rms[t] = sqrt(mean(x_t^2) + eps), h16[t] = f16(w * (x_t / rms[t])) for T rows.
+cudaError_t launch_norm_rows(const float* x, const float* w, int H, float eps, int T, float* rms,
+                             __half* h16, int* err, cudaStream_t s);
 // Token rows are read as float4 vectors and by bulk copies.
 inline bool misaligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, int H, int* err,

@@ -972,6 +972,13 @@ cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const fl
   return cudaSuccess;
 }
 
+cudaError_t launch_norm_rows(const float* x, const float* w, int H, float eps, int T, float* rms,
+                             __half* h16, int* err, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  MOE_PDL(router_prep_kernel, dim3(T), dim3(256), 0, s, x, w, H, eps, rms, h16, err);
+  return cudaSuccess;
+}
+
 cudaError_t launch_scale_router_weights(const float* w, __half* rw16, int rows, int H, int* err,
                                         cudaStream_t s) {
   scale_router_kernel<<<rows, 256, 0, s>>>(w, rw16, H, err);

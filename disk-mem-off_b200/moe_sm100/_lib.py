@@ -41,6 +41,14 @@ class MoeConfigC(ctypes.Structure):
     ]
 
 
+class MoeAttnConfigC(ctypes.Structure):
+    _fields_ = [
+        ("hidden", c_int32), ("heads", c_int32), ("kv_heads", c_int32), ("head_dim", c_int32),
+        ("rotary_dim", c_int32), ("rope_theta", c_float), ("rms_norm_eps", c_float),
+        ("max_tokens", c_int32), ("device", c_int32),
+    ]
+
+
 class MoeTensorDescC(ctypes.Structure):
     _fields_ = [
         ("name", c_char_p), ("dtype", c_char_p), ("shape", c_int64 * 2), ("ndim", c_int32),
@@ -92,6 +100,15 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_ep_experts_padded": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_uint64,
                                         c_void_p]),
     "moe_status": (c_int32, [c_void_p, c_void_p]),
+    "moe_attn_create": (c_int32, [POINTER(MoeAttnConfigC), POINTER(c_void_p)]),
+    "moe_attn_destroy": (c_int32, [c_void_p]),
+    "moe_attn_bind": (c_int32, [c_void_p, c_void_p, c_uint64, POINTER(MoeTensorDescC), c_int32,
+                                c_void_p]),
+    "moe_attn_weight_bytes": (c_uint64, [c_void_p]),
+    "moe_attn_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
+    "moe_attn_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_uint64,
+                                   c_void_p]),
+    "moe_attn_status": (c_int32, [c_void_p, c_void_p]),
     "moe_last_error": (c_char_p, []),
     "moe_version": (c_char_p, []),
     "moe_rt_device_count": (c_int32, [POINTER(c_int32)]),

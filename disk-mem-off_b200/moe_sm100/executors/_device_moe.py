@@ -27,7 +27,7 @@ from typing import Any, Callable
 import numpy as np
 
 from ..config import MoeLayerConfig
-from ..layer import MoeLayer, layer_shapes
+from ..layer import MoeLayer, _torch, layer_shapes
 from ..packing import pack_layer
 
 AttentionFn = Callable[[Any, Any, dict[str, Any]], Any]   # (layer, x, t_host) -> x
@@ -67,7 +67,8 @@ class DeviceMoeExecutor:
             overrides["score_func"] = score_func
         self.moe_config = self._parse(self.config, overrides)
         self._bound: dict[Any, MoeLayer] = {}
-        self._host_tensors: dict[int, dict[str, Any]] = {}  # non-MoE tensors of resident layers
+        # per resident layer: (device AttentionLayer or None, host attention tensors)
+        self._held: dict[int, tuple[Any, dict[str, Any]]] = {}
         # layers bound from host tensor dicts (the reference's ``_moe_mlp_block(x, t)``
         # call): a few most recent ones, each remembered by weak references to the
         # very arrays it was packed from
@@ -170,6 +171,11 @@ class DeviceMoeExecutor:
         return ml.forward(x)
 
     # -- LayerExecutor protocol ----------------------------------------------------------
+    def _device_attention_config(self) -> Any:
+        """AttentionConfig for layers whose attention runs on the device, or None
+        when attention goes to the host delegate (``attention=``)."""
+        return None
+
     def run_layer(self, layer: Any, activations: Any, device_weights: Any, backend: Any,
                   stream: Any) -> Any:
         """One decoder layer (runtime.py:15-26).  ``device_weights`` is the layer blob
@@ -180,30 +186,56 @@ class DeviceMoeExecutor:
             raise ValueError("the sm_100a MoE executor runs on the 'cuda' backend only")
         lid = layer.layer_id
         if device_weights is None:
-            held = self._host_tensors.get(lid)
+            held = self._held.get(lid)
             if held is None or not self._holds_block(layer):
                 raise KeyError(f"layer {lid} is not resident in this executor")
-            t_host = held
         else:
-            meta = layer.metadata["tensors"]
-            host_meta = [m for m in meta if not is_moe_tensor(_short(m["name"], layer))]
-            t_host = _read_ranges(backend, device_weights, host_meta, stream) if host_meta else {}
+            held = self._prepare_attention(layer, device_weights, backend, stream)
             if self.resident:
-                self._host_tensors[lid] = t_host
-        x = activations
-        if t_host:
-            if self.attention is None:
-                raise NotImplementedError(
-                    "layer has attention tensors; pass attention=<callable(layer, x, t)> "
-                    "(e.g. moe_sm100.executors.reference_delegates(ref_executor))")
-            x = self.attention(layer, x, t_host)
+                self._held[lid] = held
+        attn, t_host = held
         if not self._is_moe_layer(layer) and self.dense_mlp is not None:
             if device_weights is None:
                 raise KeyError(f"layer {lid}: a host dense-MLP delegate needs the layer blob")
-            t_all = _read_ranges(backend, device_weights, layer.metadata["tensors"], stream)
-            return self.dense_mlp(x, t_all)
+            x = self.attention(layer, activations, t_host) if t_host else activations
+            return self.dense_mlp(x, _read_ranges(backend, device_weights, layer.metadata["tensors"], stream))
         ml = self._block_for(layer, device_weights, stream)
+        if attn is not None:  # attention and MLP both on the device: one copy each way
+            return self._device_layer(attn, ml, activations)
+        x = activations
+        if t_host:
+            x = self.attention(layer, x, t_host)
         return self._moe_mlp_block(x, ml) if self._is_moe_layer(layer) else self._dense_mlp_block(x, ml)
+
+    def _prepare_attention(self, layer: Any, device_weights: Any, backend: Any,
+                           stream: Any) -> tuple[Any, dict[str, Any]]:
+        """(device AttentionLayer or None, host tensors for the attention delegate)."""
+        meta = layer.metadata["tensors"]
+        host_meta = [m for m in meta if not is_moe_tensor(_short(m["name"], layer))]
+        if not host_meta:
+            return None, {}
+        if self.attention is not None:
+            return None, _read_ranges(backend, device_weights, host_meta, stream)
+        acfg = self._device_attention_config()
+        if acfg is None:
+            raise NotImplementedError(
+                "layer has attention tensors; pass attention=<callable(layer, x, t)> "
+                "(e.g. moe_sm100.executors.reference_delegates(ref_executor))")
+        from ..attention import AttentionLayer
+        attn = AttentionLayer(acfg)
+        attn.bind_device(int(device_weights.handle), int(device_weights.nbytes),
+                         [dict(m, name=_short(m["name"], layer)) for m in host_meta],
+                         getattr(stream, "value", stream))
+        return attn, {}
+
+    @staticmethod
+    def _device_layer(attn: Any, ml: MoeLayer, x: Any) -> Any:
+        torch = _torch()
+        host = isinstance(x, np.ndarray)
+        xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(
+            f"cuda:{ml.cfg.device}") if host else x
+        y = ml.forward(attn.forward(xd))
+        return y.cpu().numpy() if host else y
 
     def _block_key(self, layer: Any) -> Any:
         return layer.layer_id if self._is_moe_layer(layer) else ("dense", layer.layer_id)
@@ -224,24 +256,28 @@ class DeviceMoeExecutor:
 
     # -- residency (used by moe_sm100.runtime.ResidentOffloadRuntime) -------------------
     def resident_nbytes(self, layer_id: int) -> int | None:
-        """Device bytes this executor keeps for ``layer_id`` between passes, or None
+        """Device bytes this executor keeps for ``layer_id`` between passes (packed
+        MLP / experts and, with device attention, the attention weights), or None
         when it cannot run the layer again without its blob."""
-        if not self.resident or layer_id not in self._host_tensors:
+        held = self._held.get(layer_id) if self.resident else None
+        if held is None:
             return None
         for key in (layer_id, ("dense", layer_id)):
             ml = self._bound.get(key)
             if ml is not None:
-                return ml.weight_bytes
+                return ml.weight_bytes + (held[0].weight_bytes if held[0] is not None else 0)
         return None
 
     def evict(self, key: Any) -> None:
-        """Release what is kept for a layer id (or a bind key): its packed plan and
-        the host copies of its non-MoE tensors."""
+        """Release what is kept for a layer id (or a bind key): its packed plans and
+        the host copies of its attention tensors."""
         for k in (key, ("dense", key)):
             ml = self._bound.pop(k, None)
             if ml is not None:
                 ml.close()
-        self._host_tensors.pop(key, None)
+        held = self._held.pop(key, None)
+        if held is not None and held[0] is not None:
+            held[0].close()
 
 
 def _read_ranges(backend: Any, buf: Any, metas: list[dict[str, Any]], stream: Any) -> dict[str, Any]:

@@ -1,9 +1,10 @@
 """GLM-4 MoE (Glm4MoeForCausalLM) executor with the MoE block on sm_100a.
 
 Constructor and attribute names follow offload_runtime/executors/glm4_moe.py:70-84;
-the MoE block (glm4_moe.py:176-240) runs through libmoe_sm100, and so does the
+the MoE block (glm4_moe.py:176-240) runs through libmoe_sm100, and so do the
 dense MLP of ``first_k_dense_replace`` layers (``metadata["is_moe"] == False``,
-glm4_moe.py:102-106, 166-172) unless a ``dense_mlp`` delegate is given.
+glm4_moe.py:102-106, 166-172) and the attention block (glm4_moe.py:112-162),
+unless ``dense_mlp`` / ``attention`` delegates are given.
 """
 from __future__ import annotations
 
@@ -37,3 +38,11 @@ class GLM4MoeExecutor(DeviceMoeExecutor):
 
     def _is_moe_layer(self, layer: Any) -> bool:
         return bool(layer.metadata.get("is_moe", False))
+
+    def _device_attention_config(self) -> Any:
+        """Without an ``attention=`` delegate the attention block
+        (glm4_moe.py:112-162) runs on the device too (moe_sm100.attention)."""
+        if "num_attention_heads" not in self.config:
+            return None
+        from ..attention import AttentionConfig
+        return AttentionConfig.glm4_moe(self.config, max_tokens=self.max_tokens, device=self.device)

@@ -231,6 +231,49 @@ int moe_status(MoePlan* plan, void* stream);
 const char* moe_last_error(void);
 const char* moe_version(void);
 
+/* --------------------------------------------------- GLM-4 MoE attention
+ * Replaces GLM4MoeExecutor._attention_block
+ * (offload_runtime/executors/glm4_moe.py:112-162; helpers _common.py:73-155):
+ *   x + o_proj(softmax(q k^T / sqrt(head_dim) + causal mask) v),
+ * q, k, v = rms_norm(x, input_layernorm.weight) . W^T (+ bias), per-head RMS norm
+ * of q and k times q_norm / k_norm when bound, rotate-half RoPE on the first
+ * rotary_dim dims at positions 0..T-1, grouped-query heads (heads / kv_heads
+ * query heads per kv head), the whole sequence at once as the reference does.
+ * Weights are packed to f16 at bind (bf16-valued weights exactly; values beyond
+ * +-65504 give MOE_ERR_RANGE); q / k / v / P are f16 tensor-core operands with
+ * fp32 accumulation, softmax and norms in fp32.  head_dim 64 or 128; hidden a
+ * multiple of 64.  Tensors are taken from the layer blob by name
+ * (self_attn.{q,k,v,o}_proj.weight, self_attn.{q,k,v}_proj.bias,
+ * self_attn.{q,k}_norm.weight, input_layernorm.weight; a model.layers.N.
+ * prefix is accepted); biases and the q/k norms are optional. */
+typedef struct MoeAttnConfig {
+  int32_t hidden;       /* hidden_size                                          */
+  int32_t heads;        /* num_attention_heads                                  */
+  int32_t kv_heads;     /* num_key_value_heads                                  */
+  int32_t head_dim;     /* 64 or 128                                            */
+  int32_t rotary_dim;   /* int(head_dim * partial_rotary_factor), even           */
+  float rope_theta;     /* rope_theta                                           */
+  float rms_norm_eps;   /* rms_norm_eps (input norm and q/k norms)              */
+  int32_t max_tokens;   /* largest sequence a forward may be called with        */
+  int32_t device;       /* CUDA device ordinal                                  */
+} MoeAttnConfig;
+
+typedef struct MoeAttn MoeAttn;
+
+int moe_attn_create(const MoeAttnConfig* cfg, MoeAttn** out);
+int moe_attn_destroy(MoeAttn* attn);
+/* Pack the attention tensors of a device-resident layer blob (metadata["tensors"]
+ * entries, as for moe_bind_layer).  Synchronises `stream`. */
+int moe_attn_bind(MoeAttn* attn, const void* blob_dev, uint64_t blob_bytes,
+                  const MoeTensorDesc* descs, int32_t n_descs, void* stream);
+uint64_t moe_attn_weight_bytes(const MoeAttn* attn);
+uint64_t moe_attn_workspace_bytes(const MoeAttn* attn, int32_t T);
+/* out[T,H] = x + attention(x); fp32, 16-byte aligned, x and out distinct. */
+int moe_attn_forward(MoeAttn* attn, const float* x_dev, float* out_dev, int32_t T,
+                     void* workspace, uint64_t workspace_bytes, void* stream);
+/* As moe_status, for the attention kernels' device error word. */
+int moe_attn_status(MoeAttn* attn, void* stream);
+
 /* ------------------------------------------- runtime (CUDABackend, ctypes) */
 int moe_rt_device_count(int32_t* count);
 int moe_rt_set_device(int32_t device);

@@ -10,8 +10,9 @@
   reference loader's fp32 blobs, against the reference executor on its
   ``NullBackend``.
 
-Attention runs on the host here through the attention delegate (the oracle's
-restatement of glm4_moe.py:112-162, or the reference executor's own method).
+Attention runs on the host through the attention delegate (the oracle's
+restatement of glm4_moe.py:112-162, or the reference executor's own method), or on
+the device (``moe_sm100.attention``, no delegate).
 """
 from __future__ import annotations
 
@@ -79,8 +80,9 @@ def _rel_l2(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64)))
 
 
-@pytest.mark.parametrize("fmt", ["bfloat16", "int8"])
-def test_resident_runtime_end_to_end(tmp_path: Path, fmt: str) -> None:
+@pytest.mark.parametrize("fmt,attention", [("bfloat16", "host"), ("int8", "host"),
+                                           ("bfloat16", "device"), ("int8", "device")])
+def test_resident_runtime_end_to_end(tmp_path: Path, fmt: str, attention: str) -> None:
     vals = tiny_glm.write_model(tmp_path)
     c = tiny_glm.CONFIG
     attn_cfg = AttnConfig.from_hf(c)
@@ -89,8 +91,10 @@ def test_resident_runtime_end_to_end(tmp_path: Path, fmt: str) -> None:
     backend = _CountingCUDABackend(0)
     storage = PreservingSafetensorsStorage.from_model_dir(tmp_path, tiny_glm.layer_specs(vals),
                                                           expert_format=fmt)
+    # attention on the host through the delegate, or on the device (no delegate)
+    delegate = {"attention": lambda layer, h, t: glm4_attention_block(h, t, attn_cfg)}
     ex = GLM4MoeExecutor(c, weight_format="int8" if fmt == "int8" else "f16", max_tokens=T,
-                         attention=lambda layer, h, t: glm4_attention_block(h, t, attn_cfg))
+                         **(delegate if attention == "host" else {}))
     ids = [s.layer_id for s in storage.layers]
     with ResidentOffloadRuntime(storage.layers, backend, storage, _Lookahead(), ex,
                                 resident_budget_bytes=8 << 30) as rt:
