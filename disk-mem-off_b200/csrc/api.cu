@@ -251,6 +251,23 @@ static int parse_dtype(const char* d) {
 
 static size_t dtype_size(int d) { return d == SRC_F32 ? 4 : (d == SRC_I8 ? 1 : 2); }
 
+// One thread waits, with the bounded wait every kernel here uses, on an mbarrier
+// that nothing ever arrives at.  The wait gives up after `limit` cycles and the
+// kernel records a timeout in the plan's error word and returns: the failure
+// path of a stuck pipeline, without a fault and without a stuck GPU.
+__global__ void wait_probe_kernel(int* err, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_bounded(&bar, 0, &abort_flag, limit))
+    record_error(err, DEV_TIMEOUT_FULL);
+}
+
 }  // namespace moe
 
 // ====================================================================== C ABI
@@ -707,7 +724,19 @@ int moe_status(MoePlan* plan, void* stream) {
   if (h == DEV_OK) return MOE_OK;
   if (h >= DEV_TIMEOUT_FULL && h <= DEV_TIMEOUT_CONV)
     return fail(MOE_ERR_TIMEOUT, "a device-side wait ran out of time (code " + std::to_string(h) + ")");
+  if (h == DEV_RANGE)
+    return fail(MOE_ERR_RANGE, "an activation or expert output overflowed f16 (|v| > 65504)");
   return fail(MOE_ERR_DEVICE, "a kernel reported device error code " + std::to_string(h));
+}
+
+int moe_wait_probe(MoePlan* plan, int64_t limit_cycles, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  if (limit_cycles <= 0 || limit_cycles > kWaitLimitCycles)
+    return fail(MOE_ERR_INVALID, "limit_cycles must be in (0, 2e9]");
+  MOE_CUDA(cudaSetDevice(plan->p.device));
+  wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(plan->p.d_err, limit_cycles);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
 }
 
 // ------------------------------------------------------------ expert parallel

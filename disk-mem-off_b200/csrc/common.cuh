@@ -25,8 +25,11 @@ enum DevErr : int {
   DEV_TIMEOUT_CONV = 5,      // int8 converter waited too long
   DEV_BAD_TILE = 6,          // tile list entry out of range
   DEV_BAD_ROUTE = 7,         // router produced an expert id out of range
-  DEV_RANGE = 8,             // an activation does not fit the f16 router operand
+  DEV_RANGE = 8,             // an activation does not fit an f16 operand or output
 };
+
+// f16 conversion of v stays finite (|v| rounds to at most 65504); false for NaN too.
+MOE_DEV bool fits_f16(float v) { return fabsf(v) < 65520.f; }
 
 // ~1 s at the B200 boost clock.  Legitimate waits in these kernels are
 // microseconds; this bound only ends a wait that can no longer complete.
@@ -91,14 +94,15 @@ MOE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity; false if the wait ran out of time
-// or the CTA was told to abort (another role already timed out).
-MOE_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// (`limit` cycles) or the CTA was told to abort (another role already timed out).
+MOE_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                               long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   long long start = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - start > kWaitLimitCycles) return false;
+    if (clock64() - start > limit) return false;
   }
 }
 

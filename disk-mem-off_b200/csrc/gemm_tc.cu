@@ -395,6 +395,7 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     const int cfirst = (ew >> 2) * 16, cstep = 16 * (EPI / 4);  // its column chunks
     const int r = q * 32 + lane;
     int tl = 0;
+    bool range_bad = false;
     for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
       const Tile t = fetch_tile(ti);
       if (!tile_ok(t)) continue;
@@ -504,9 +505,11 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
             const float lo = (lane & 1) ? o : a[j];
             const float hi = (lane & 1) ? a[j + 1] : o;
             const int col = c0 + 2 * (j + (lane & 1)) + (lane >> 4);
-            if (col < t.nvalid && row_ok)
+            if (col < t.nvalid && row_ok) {
+              range_bad |= !fits_f16(lo) || !fits_f16(hi);
               *reinterpret_cast<__half2*>(dst + static_cast<size_t>(t.row0 + col) * ld + (feat & ~1)) =
                   __floats2half2_rn(lo, hi);
+            }
           }
         } else {
           if (!sh && args.y_half) {
@@ -519,6 +522,7 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
               const float hi = (lane & 1) ? v[i + 1] : o;
               const int col = c0 + i + (lane & 1);
               if (col < t.nvalid && row_ok) {
+                range_bad |= !fits_f16(lo) || !fits_f16(hi);
                 const int orow = args.y_row_map ? args.y_row_map[t.row0 + col] : t.row0 + col;
                 *reinterpret_cast<__half2*>(args.y_half + static_cast<size_t>(orow) * args.y_ld + (mrow & ~1)) =
                     __floats2half2_rn(lo, hi);
@@ -538,6 +542,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
       mbar_arrive(&tempty[buf]);
       ++tl;
     }
+    // an f16 activation / expert output that overflowed is reported, not passed on
+    // silently as inf (moe_status -> MOE_ERR_RANGE)
+    if (__any_sync(0xffffffffu, range_bad) && lane == 0) record_error(args.err, DEV_RANGE);
   } else if constexpr (INT8) {
     // ------------------------------------------------------------ int8 -> f16
     const int r = (warp - 2 - EPI) * 32 + lane;  // one A row per thread

@@ -109,6 +109,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_attn_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_uint64,
                                    c_void_p]),
     "moe_attn_status": (c_int32, [c_void_p, c_void_p]),
+    "moe_wait_probe": (c_int32, [c_void_p, c_int64, c_void_p]),
     "moe_last_error": (c_char_p, []),
     "moe_version": (c_char_p, []),
     "moe_rt_device_count": (c_int32, [POINTER(c_int32)]),

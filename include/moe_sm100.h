@@ -225,8 +225,16 @@ int moe_ep_experts_padded(MoePlan* plan, const void* recv_rows, int32_t cap, voi
                           void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* Synchronise `stream`, then read and clear the device error word of the plan.
- * Returns MOE_OK, MOE_ERR_TIMEOUT or MOE_ERR_DEVICE. */
+ * Returns MOE_OK, MOE_ERR_TIMEOUT (a bounded wait ran out), MOE_ERR_RANGE (an f16
+ * activation or expert output overflowed) or MOE_ERR_DEVICE. */
 int moe_status(MoePlan* plan, void* stream);
+
+/* Failure-path check (no counterpart in the reference): launch a one-thread kernel
+ * that waits, with the same bounded mbarrier wait every kernel here uses, on a
+ * barrier nothing arrives at, so the wait gives up after limit_cycles (<= 2e9,
+ * about one second) and records a timeout in the plan's device error word; the
+ * next moe_status returns MOE_ERR_TIMEOUT and the context stays usable. */
+int moe_wait_probe(MoePlan* plan, int64_t limit_cycles, void* stream);
 
 const char* moe_last_error(void);
 const char* moe_version(void);
