@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 128);
+      mbar_init(&conv[s], 4);  // one arrival per converter warp
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -556,15 +556,18 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
       for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, abort_flag))) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_CONV);
           ok = false;
           break;
         }
         convert_row_i8_f16(reinterpret_cast<const int8_t*>(sA8 + s * SA8 + r * kBK), sA + s * SA, r);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&conv[s]);
+        // each thread makes its rows visible to the tensor core's (async) proxy; the
+        // warp then arrives once: 4 arrivals per stage instead of 128 serialised ones
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
       }
       if (!ok) break;
     }

@@ -76,10 +76,13 @@ def test_attention_against_oracle(spec: AttnSpec) -> None:
     ref = glm4_attention_block(x, t, AttnConfig.from_hf(spec.hf_config()))
     al = _layer(spec, t, spec.tokens)
     got = _check(al, x, ref)
-    # causal: the first rows of the sequence do not see the later ones
+    # causal: the first rows of the sequence do not see the later ones.  The
+    # projections split K by sequence length, so the shorter run adds the same
+    # products in another order (f16 roundings of q / k / v may flip): equal to
+    # ~1e-4, where a leak from later tokens would be O(1)
     n = spec.tokens // 3
     head = al.forward(torch.from_numpy(np.ascontiguousarray(x[:n])).cuda()).cpu().numpy()
-    assert _rel(head, got[:n]) <= 1e-5
+    assert _rel(head - x[:n], got[:n] - x[:n]) <= 2e-3
     al.close()
 
 
