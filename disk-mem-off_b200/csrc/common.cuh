@@ -95,10 +95,13 @@ MOE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase with the given parity; false if the wait ran out of time
 // (`limit` cycles) or the CTA was told to abort (another role already timed out).
+// Every waiting thread polls on its own: parking threads with a suspend-time
+// hint, or letting one lane poll for its warp, both measured slower (the INT8
+// decode GEMM's converter warps sit on this path once per k-block).
 MOE_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  long long start = clock64();
+  const long long start = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;

@@ -103,19 +103,41 @@ __host__ __device__ constexpr int gemm_threads() {
 // law over the ring), so a fourth INT8 stage at BN = 256 pays directly.
 constexpr int kGemmSmemBudget = 232448 - 1024 - 256 - 512;
 
+#ifndef MOE_GEMM_MAX_STAGES
+#define MOE_GEMM_MAX_STAGES 8
+#endif
+
+// k-blocks per pipeline stage.  INT8 decode tiles (N <= 64) widen two 64-column
+// k-blocks per stage: each stage costs the converter warps a fixed hand-off
+// (wait for the copy, widen, proxy fence, barrier to the MMA thread), and with
+// one k-block per stage that cost, not the bytes, set the pace (~0.39 us per
+// k-block for 8 KiB of int8, the same as for 16 KiB of f16).  Two k-blocks per
+// stage measured 13 % faster at 32 tokens; four (two stages) and a split ring
+// (14 single-k-block int8 stages feeding 3 widened slots) measured slower.  f16
+// stages and wide prefill tiles keep one k-block.
+#ifndef MOE_INT8_DECODE_KPS
+#define MOE_INT8_DECODE_KPS 2
+#endif
+
+template <int BN, bool INT8>
+__host__ __device__ constexpr int gemm_kps() { return (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1; }
+
+template <int BN, bool INT8>
+__host__ __device__ constexpr int gemm_stage_bytes() {
+  return gemm_kps<BN, INT8>() *
+         (TileCfg<BN>::kStageA + TileCfg<BN>::kStageB + (INT8 ? TileCfg<BN>::kStageA8 : 0));
+}
+
 template <int BN, bool INT8>
 __host__ __device__ constexpr int gemm_stages() {
-  constexpr int per = TileCfg<BN>::kStageA + TileCfg<BN>::kStageB + (INT8 ? TileCfg<BN>::kStageA8 : 0);
-  constexpr int s = kGemmSmemBudget / per;
-  return s > 8 ? 8 : s;
+  constexpr int s = kGemmSmemBudget / gemm_stage_bytes<BN, INT8>();
+  return s > MOE_GEMM_MAX_STAGES ? MOE_GEMM_MAX_STAGES : s;
 }
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
-  constexpr int st = gemm_stages<BN, INT8>();
   return 1024 /*align slack*/ +
-         static_cast<size_t>(st) * (TileCfg<BN>::kStageA + TileCfg<BN>::kStageB +
-                                    (INT8 ? TileCfg<BN>::kStageA8 : 0)) +
+         static_cast<size_t>(gemm_stages<BN, INT8>()) * gemm_stage_bytes<BN, INT8>() +
          256 /*barriers*/;
 }
 
@@ -212,6 +234,8 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
   constexpr bool DOWN = MODE == MODE_DOWN;
   constexpr int STAGES = gemm_stages<BN, INT8>();
+  constexpr int KPS = gemm_kps<BN, INT8>();  // k-blocks per stage
+  // per k-block operand bytes; stage s holds k-blocks [s * KPS, s * KPS + KPS) of each buffer
   constexpr int SA = TileCfg<BN>::kStageA, SB = TileCfg<BN>::kStageB, SA8 = TileCfg<BN>::kStageA8;
   // The MMA runs with N = nvalid rounded up to 16: a partial tile does not pay
   // tensor time for the token columns it does not use.
@@ -220,9 +244,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * SA;
-  uint8_t* sA8 = sB + STAGES * SB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + (INT8 ? STAGES * SA8 : 0));
+  uint8_t* sB = sA + STAGES * KPS * SA;
+  uint8_t* sA8 = sB + STAGES * KPS * SB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + (INT8 ? STAGES * KPS * SA8 : 0));
   uint64_t* full = bars;                 // TMA landed (A + B)
   uint64_t* empty = full + STAGES;       // MMA finished reading the stage
   uint64_t* conv = empty + STAGES;       // int8 tile widened to f16
@@ -319,18 +343,21 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
           a8 = (sh ? args.a8_shared : args.a8_routed + static_cast<size_t>(t.group) * args.a8_group_bytes) +
                static_cast<size_t>(t.m0 / kBM) * (sh ? args.a8_nkb_shared : args.a8_nkb_routed) * SA8;
         }
-        for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
+        for (int kb = t.kb0; kb < t.kb1; kb += KPS, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const int n = min(KPS, t.kb1 - kb);  // k-blocks in this stage
           if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag)) {
             *abort_flag = 1;
             record_error(args.err, DEV_TIMEOUT_EMPTY);
             break;
           }
-          mbar_arrive_expect_tx(&full[s], (INT8 ? SA8 : SA) + SB);
-          if constexpr (INT8) bulk_load(sA8 + s * SA8, a8 + static_cast<size_t>(kb) * SA8, SA8, &full[s]);
+          mbar_arrive_expect_tx(&full[s], n * ((INT8 ? SA8 : SA) + SB));
+          // the k-blocks of a tile-major int8 row tile are consecutive: one copy
+          if constexpr (INT8) bulk_load(sA8 + s * KPS * SA8, a8 + static_cast<size_t>(kb) * SA8, n * SA8, &full[s]);
           else tma_load_2d(sA + s * SA, ma, kb * kBK, arow, &full[s]);
-          tma_load_2d(sB + s * SB, mb, kb * kBK, t.row0, &full[s]);
+          for (int j = 0; j < n; ++j)
+            tma_load_2d(sB + (s * KPS + j) * SB, mb, (kb + j) * kBK, t.row0, &full[s]);
         }
       }
       // drain: every stage's most recent load must have landed before exit
@@ -359,9 +386,10 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
         const uint32_t d = tmem_base + buf * TileCfg<BN>::kAccCols;
         const uint32_t idesc = idesc_f16_f32(kBM, (t.nvalid + 15) & ~15);
         bool ok = true;
-        for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
+        for (int kb = t.kb0; kb < t.kb1; kb += KPS, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const int n = min(KPS, t.kb1 - kb);
           if (!mbar_wait_bounded(INT8 ? &conv[s] : &full[s], ph, abort_flag)) {
             *abort_flag = 1;
             record_error(args.err, DEV_TIMEOUT_FULL);
@@ -369,12 +397,14 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * SA), b0 = smem_u32(sB + s * SB);
+          for (int j = 0; j < n; ++j) {
+            const uint32_t a0 = smem_u32(sA + (s * KPS + j) * SA), b0 = smem_u32(sB + (s * KPS + j) * SB);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // MMA k feeds chain k % CH; a chain's first MMA of the tile starts it
-            tc_mma_f16(d + (k % CH) * BN, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
-                       (kb > t.kb0 || k >= CH) ? 1u : 0u);
+            for (int k = 0; k < kBK / 16; ++k) {
+              // MMA k feeds chain k % CH; a chain's first MMA of the tile starts it
+              tc_mma_f16(d + (k % CH) * BN, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
+                         (kb + j > t.kb0 || k >= CH) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);
           issued = true;
@@ -553,16 +583,19 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
       const Tile t = fetch_tile(ti);
       if (!tile_ok(t)) continue;
       bool ok = true;
-      for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
+      for (int kb = t.kb0; kb < t.kb1; kb += KPS, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        const int n = min(KPS, t.kb1 - kb);
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, abort_flag))) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_CONV);
           ok = false;
           break;
         }
-        convert_row_i8_f16(reinterpret_cast<const int8_t*>(sA8 + s * SA8 + r * kBK), sA + s * SA, r);
+        for (int j = 0; j < n; ++j)
+          convert_row_i8_f16(reinterpret_cast<const int8_t*>(sA8 + (s * KPS + j) * SA8 + r * kBK),
+                             sA + (s * KPS + j) * SA, r);
         // each thread makes its rows visible to the tensor core's (async) proxy; the
         // warp then arrives once: 4 arrivals per stage instead of 128 serialised ones
         fence_proxy_async_smem();
