@@ -173,6 +173,7 @@ RouterGeom router_geometry(const Plan& p, int T);
 
 constexpr int kTailMaxT = 256;  // decode: one CTA does top-k + permutation + tile lists
 bool route_uses_tail(const Plan& p, int T);
+bool route_uses_small(const Plan& p, int T);  // one-launch routing of small decode batches
 
 // ------------------------------------------------------------ launchers
 // Router (+ RMSNorm), top-k, permutation and tile lists; with `dispatch` also

@@ -17,6 +17,8 @@
 // Prefill:          router -> topk -> perm_hist -> perm_scan -> perm_scatter -> dispatch.
 #include <float.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(256) router_kernel(
 // ------------------------------------------------------------------ top-k
 // One warp scores and selects for one token.  Lane l holds experts l, l+32, ...
 // Keys rank (desc) with the lower id winning exact ties; weights follow the
-// reference formulas in fp32.  Lane 0 writes ids_out[0..K) / w_out[0..K).
+// reference formulas in fp32.  Lane r < K writes ids_out[r] / w_out[r].
 template <int VPL>
 MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
                        int K, int score_func, int norm, float scale, int lane,
@@ -238,8 +240,9 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     denom = s;
   }
-  int sel_id[kMaxTopK];
-  float sel_w[kMaxTopK];
+  // lane r keeps the r-th selection (no per-thread arrays: they lived in local memory)
+  int my_id = 0;
+  float my_w = 0.f;
   uint32_t taken = 0u;
   for (int r = 0; r < K; ++r) {
     float bk = -FLT_MAX;
@@ -270,20 +273,20 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
       record_error(err, DEV_BAD_ROUTE);
       bid = 0;
     }
-    sel_id[r] = bid;
-    sel_w[r] = (score_func == MOE_SCORE_SOFTMAX) ? bv / denom : bv;
+    if (lane == r) {
+      my_id = bid;
+      my_w = (score_func == MOE_SCORE_SOFTMAX) ? bv / denom : bv;
+    }
     if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
   }
-  if (lane == 0) {
-    float sum = 0.f;
-    if (norm)
-      for (int r = 0; r < K; ++r) sum += sel_w[r];
-    for (int r = 0; r < K; ++r) {
-      float wv = sel_w[r];
-      if (norm) wv = wv / (sum + 1e-20f);
-      ids_out[r] = sel_id[r];
-      w_out[r] = wv * scale;
-    }
+  float sum = 0.f;  // rank order, one term at a time
+  if (norm)
+    for (int r = 0; r < K; ++r) sum += __shfl_sync(0xffffffffu, my_w, r);
+  if (lane < K) {
+    float wv = my_w;
+    if (norm) wv = wv / (sum + 1e-20f);
+    ids_out[lane] = my_id;
+    w_out[lane] = wv * scale;
   }
 }
 
@@ -720,7 +723,7 @@ __device__ void build_tile_lists(int cnt, const TileArgs& a) {
     const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
     const int s1 = choose_ksplit(c1, a.num_sms, a.max_split_tiles, min(a.nk1, a.has_shared ? a.nk1s : a.nk1));
     const int s2 = choose_ksplit(c2, a.num_sms, a.max_split_tiles, min(a.nk2, a.has_shared ? a.nk2s : a.nk2));
-    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_BAD_TILE);
+    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_TILE_OVERFLOW);
     a.pre1[a.E] = tot1;
     a.pre2[a.E] = tot2;
     s_c[0] = min(c1, a.max1);
@@ -799,6 +802,261 @@ __global__ void __launch_bounds__(1024) route_tail_kernel(
     perm[r] = q;
     slot_row[q] = r;
   }
+}
+
+// ------------------------------------------------------------------ small decode batches
+// Batches of up to kSmallT tokens route in ONE launch: the router GEMV, top-k,
+// permutation and tile maps, where the launches above take two (a split-K router
+// with a last-CTA reduction, then the one-CTA tail), each a few microseconds of
+// launch, wait and reduction latency that a one-token step cannot hide.
+//   every CTA: x_t * norm_w for the batch into shared memory (and sum x^2 for the
+//              RMS), then each warp one router row: logit = sum_k (w_k x_k) r_k / rms
+//   the CTA that finishes last (a counter): top-k of every token (a warp per
+//              token), expert bitmasks, offsets, the (token, slot) permutation and
+//              both GEMMs' tile maps, as route_tail_kernel does.
+#ifndef MOE_SMALL_ROUTE_MAX_T
+#define MOE_SMALL_ROUTE_MAX_T 8
+#endif
+constexpr int kSmallT = 8;
+constexpr int kSmallRowsPerCta = 8;  // one router row per warp
+
+// Exclusive scan of one int per thread for any block size that is a multiple of
+// 32 (up to 1024); every thread gets the block total in *total.
+__device__ int block_excl_scan_any(int v, int* total) {
+  __shared__ int wsum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;
+  }
+  __syncthreads();
+  const int incl = x + (warp > 0 ? wsum[warp - 1] : 0);
+  *total = wsum[31];
+  __syncthreads();
+  return incl - v;
+}
+
+// In-place exclusive scan of a[0, n) in shared memory by the whole block (each
+// thread a contiguous run); returns the total.
+__device__ int block_scan_smem(int* a, int n) {
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int beg = min(n, threadIdx.x * per), end = min(n, beg + per);
+  int sum = 0;
+  for (int i = beg; i < end; ++i) sum += a[i];
+  int total = 0;
+  int run = block_excl_scan_any(sum, &total);
+  for (int i = beg; i < end; ++i) {
+    const int v = a[i];
+    a[i] = run;
+    run += v;
+  }
+  __syncthreads();
+  return total;
+}
+
+// build_tile_lists for any block size, from per-expert row counts in shared memory
+// (s_cnt[E]); s_a / s_b are E-entry shared scratch arrays.
+__device__ void build_tile_lists_smem(const int* s_cnt, int* s_a, int* s_b, const TileArgs& a) {
+  __shared__ int s_c[2], s_split[2];
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    const int ntn = (s_cnt[e] + a.bn - 1) / a.bn;
+    s_a[e] = ntn * a.mt1;
+    s_b[e] = ntn * a.mt2;
+  }
+  __syncthreads();
+  const int tot1 = block_scan_smem(s_a, a.E);
+  const int tot2 = block_scan_smem(s_b, a.E);
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    a.pre1[e] = s_a[e];
+    a.pre2[e] = s_b[e];
+  }
+  if (threadIdx.x == 0) {
+    const int nts = a.has_shared ? (a.T + a.bn - 1) / a.bn : 0;
+    const int c1 = tot1 + a.mt1s * nts, c2 = tot2 + a.mt2 * nts;
+    const int s1 = choose_ksplit(c1, a.num_sms, a.max_split_tiles, min(a.nk1, a.has_shared ? a.nk1s : a.nk1));
+    const int s2 = choose_ksplit(c2, a.num_sms, a.max_split_tiles, min(a.nk2, a.has_shared ? a.nk2s : a.nk2));
+    if (c1 > a.max1 || c2 > a.max2) record_error(a.err, DEV_TILE_OVERFLOW);
+    a.pre1[a.E] = tot1;
+    a.pre2[a.E] = tot2;
+    s_c[0] = min(c1, a.max1);
+    s_c[1] = min(c2, a.max2);
+    s_split[0] = s1;
+    s_split[1] = s2;
+    a.info[0] = tot1;
+    a.info[1] = s1;
+    a.info[2] = s_c[0] * s1;
+    a.info[4] = tot2;
+    a.info[5] = s2;
+    a.info[6] = s_c[1] * s2;
+  }
+  __syncthreads();
+  for (int pass = 0; pass < 2; ++pass) {
+    if (s_split[pass] > 1) {
+      int* kcount = pass ? a.kcount2 : a.kcount1;
+      for (int q = threadIdx.x; q < s_c[pass]; q += blockDim.x) kcount[q] = 0;
+    }
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) route_small_kernel(
+    const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ wr,
+    const float* __restrict__ bias, int T, int H, int E, int R, int K, int score_func, int norm,
+    float scale, float eps, float* __restrict__ logits, float* __restrict__ rms_out,
+    int* __restrict__ counter, int32_t* __restrict__ ids, float* __restrict__ wts,
+    float* __restrict__ sgate, int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
+    int32_t* __restrict__ slot_row, TileArgs ta) {
+  pdl_enter();
+  extern __shared__ __align__(16) float xs[];  // [T][H]: x * norm weight
+  __shared__ float s_rms[kSmallT];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = H >> 2;  // float4 per row
+  // the batch's x rows into shared memory, every copy in flight at once
+  for (int i = threadIdx.x; i < T * nv; i += blockDim.x) {
+    const int t = i / nv, v = i - t * nv;
+    cp_async16(xs + static_cast<size_t>(t) * H + 4 * v, x + static_cast<size_t>(t) * H + 4 * v);
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // sum of x^2 per token and x * norm weight in place; each thread the same
+  // float4 columns of every token, so its norm weights are loaded once
+  float ss[kSmallT];
+#pragma unroll
+  for (int t = 0; t < kSmallT; ++t) ss[t] = 0.f;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    const float4 g = reinterpret_cast<const float4*>(wn)[i];
+#pragma unroll
+    for (int t = 0; t < kSmallT; ++t) {
+      if (t < T) {
+        float4* p = reinterpret_cast<float4*>(xs + static_cast<size_t>(t) * H) + i;
+        const float4 v = *p;
+        float q = ss[t];
+        q = fmaf(v.x, v.x, q);
+        q = fmaf(v.y, v.y, q);
+        q = fmaf(v.z, v.z, q);
+        q = fmaf(v.w, v.w, q);
+        ss[t] = q;
+        *p = make_float4(g.x * v.x, g.y * v.y, g.z * v.z, g.w * v.w);
+      }
+    }
+  }
+  __shared__ float s_red[8][kSmallT];
+#pragma unroll
+  for (int t = 0; t < kSmallT; ++t) {
+    float q = ss[t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) s_red[warp][t] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x < T) {  // warp partials added in warp order
+    float tot = 0.f;
+    for (int w = 0; w < 8; ++w) tot += s_red[w][threadIdx.x];
+    s_rms[threadIdx.x] = sqrtf(tot / static_cast<float>(H) + eps);
+  }
+  __syncthreads();
+  // one router row per warp: T dot products over H, eight row loads in flight per lane
+  const int r = blockIdx.x * kSmallRowsPerCta + warp;
+  if (r < R) {
+    float acc[kSmallT];
+#pragma unroll
+    for (int t = 0; t < kSmallT; ++t) acc[t] = 0.f;
+    const float4* wrow = reinterpret_cast<const float4*>(wr + static_cast<size_t>(r) * H);
+    constexpr int U = 8;
+    for (int base = lane; base < nv; base += 32 * U) {
+      float4 w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + 32 * u;
+        w[u] = i < nv ? __ldcs(wrow + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + 32 * u;
+        if (i >= nv) break;
+#pragma unroll
+        for (int t = 0; t < kSmallT; ++t) {
+          if (t < T) {
+            const float4 a = reinterpret_cast<const float4*>(xs + static_cast<size_t>(t) * H)[i];
+            float c = acc[t];
+            c = fmaf(a.x, w[u].x, c);
+            c = fmaf(a.y, w[u].y, c);
+            c = fmaf(a.z, w[u].z, c);
+            c = fmaf(a.w, w[u].w, c);
+            acc[t] = c;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kSmallT; ++t) {
+      if (t < T) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) logits[static_cast<size_t>(t) * R + r] = v / s_rms[t];
+      }
+    }
+  }
+  // the CTA that finishes last selects, permutes and builds the tile maps
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  int* s_ids = reinterpret_cast<int*>(xs);  // x is no longer needed: reuse the space
+  uint32_t* s_bm = reinterpret_cast<uint32_t*>(s_ids + kSmallT * kMaxTopK);  // [E] token masks
+  int* s_cnt = reinterpret_cast<int*>(s_bm + E);
+  int* s_a = s_cnt + E;
+  int* s_b = s_a + E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_bm[e] = 0u;
+  if (threadIdx.x < T) rms_out[threadIdx.x] = s_rms[threadIdx.x];
+  __syncthreads();
+  if (warp < T) {
+    const float* lrow = logits + static_cast<size_t>(warp) * R;
+    warp_topk<VPL>(lrow, bias, E, K, score_func, norm, scale, lane, s_ids + warp * K,
+                   wts + static_cast<size_t>(warp) * K, ta.err);
+    if (sgate && lane == 0) sgate[warp] = sigmoid_f(__ldcg(lrow + E));
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < T * K; q += blockDim.x) {
+    const int e = s_ids[q];
+    ids[q] = e;
+    atomicOr(&s_bm[e], 1u << (q / K));
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = __popc(s_bm[e]);
+  __syncthreads();
+  // offsets: scan of the counts (s_a holds them while the tile maps use s_cnt)
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_a[e] = s_cnt[e];
+  __syncthreads();
+  const int all = block_scan_smem(s_a, E);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) offsets[e] = s_a[e];
+  if (threadIdx.x == 0) offsets[E] = all;
+  for (int q = threadIdx.x; q < T * K; q += blockDim.x) {
+    const int e = s_ids[q], t = q / K;
+    const int rr = s_a[e] + __popc(s_bm[e] & ((1u << t) - 1u));
+    perm[rr] = q;
+    slot_row[q] = rr;
+  }
+  __syncthreads();
+  build_tile_lists_smem(s_cnt, s_a, s_b, ta);
+  if (threadIdx.x == 0) *counter = 0;  // ready for the next call
 }
 
 // ------------------------------------------------------------------ prefill permutation
@@ -1167,10 +1425,65 @@ static TileArgs tile_args(const Plan& p, const WsLayout& L, char* ws, int T, int
 
 bool route_uses_tail(const Plan& p, int T) { return T <= kTailMaxT && T * p.K <= 8192; }
 
+// The one-launch router: small batches whose x rows fit shared memory (8 tokens of
+// GLM-4.7's 5120 features = 160 KiB) and whose slot bookkeeping fits the space it
+// reuses afterwards.
+bool route_uses_small(const Plan& p, int T) {
+  if (T > kSmallT || T > MOE_SMALL_ROUTE_MAX_T || p.E == 0) return false;
+  const size_t xs = static_cast<size_t>(T) * p.H * 4;
+  const size_t tail = (static_cast<size_t>(kSmallT) * kMaxTopK + 4 * static_cast<size_t>(p.E)) * 4;
+  return std::max(xs, tail) <= 200 * 1024;
+}
+
+static cudaError_t launch_route_small(const Plan& p, const WsLayout& L, char* ws, const float* x,
+                                      int T, cudaStream_t s) {
+  const int E = p.E, K = p.K, R = p.router_rows;
+  int* counter = reinterpret_cast<int*>(ws + L.counters);
+  cudaError_t st = cudaMemsetAsync(counter, 0, sizeof(int), s);
+  if (st != cudaSuccess) return st;
+  const size_t smem = std::max(static_cast<size_t>(T) * p.H * 4,
+                               (static_cast<size_t>(kSmallT) * kMaxTopK + 4 * static_cast<size_t>(E)) * 4);
+  const int grid = (R + kSmallRowsPerCta - 1) / kSmallRowsPerCta;
+  const TileArgs ta = tile_args(p, L, ws, T, p.E, true);
+  const float* bias = p.cfg.use_bias ? p.w.bias : nullptr;
+  float* sg = p.cfg.has_shared_gate ? reinterpret_cast<float*>(ws + L.sgate) : nullptr;
+  const int vpl = (E + 31) / 32;
+#define MOE_SMALL_CASE(V)                                                                          \
+  do {                                                                                             \
+    static bool done[64] = {};                                                                     \
+    st = set_smem_attr(reinterpret_cast<const void*>(route_small_kernel<V>), 200 * 1024, done);    \
+    if (st != cudaSuccess) return st;                                                              \
+    MOE_PDL(route_small_kernel<V>, dim3(grid), dim3(256), smem, s, x, p.w.norm_w, p.w.router_w,   \
+            bias, T, p.H, E, R, K, p.cfg.score_func, p.cfg.norm_topk_prob,                         \
+            p.cfg.routed_scaling_factor, p.cfg.rms_norm_eps, reinterpret_cast<float*>(ws + L.logits), \
+            reinterpret_cast<float*>(ws + L.rms), counter, reinterpret_cast<int32_t*>(ws + L.ids),  \
+            reinterpret_cast<float*>(ws + L.wts), sg, reinterpret_cast<int32_t*>(ws + L.offsets),   \
+            reinterpret_cast<int32_t*>(ws + L.perm), reinterpret_cast<int32_t*>(ws + L.slot_row), ta); \
+  } while (0)
+  if (vpl <= 1) MOE_SMALL_CASE(1);
+  else if (vpl <= 2) MOE_SMALL_CASE(2);
+  else if (vpl <= 4) MOE_SMALL_CASE(4);
+  else if (vpl <= 8) MOE_SMALL_CASE(8);
+  else if (vpl <= 16) MOE_SMALL_CASE(16);
+  else MOE_SMALL_CASE(32);
+#undef MOE_SMALL_CASE
+  return cudaGetLastError();
+}
+
 cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                          bool dispatch, cudaStream_t s, __half* xg_out) {
   const bool tc = route_uses_tc_router(p, T);
   cudaError_t st;
+  if (route_uses_small(p, T)) {
+    st = launch_route_small(p, L, ws, x, T, s);
+    if (st != cudaSuccess || !dispatch) return st;
+    const int rows = T * p.K + (p.SI > 0 ? T : 0);
+    MOE_PDL(dispatch_kernel, dim3(min(rows, p.num_sms * 8)), dim3(256), 0, s,
+            x, p.w.norm_w, reinterpret_cast<const float*>(ws + L.rms),
+            reinterpret_cast<const int32_t*>(ws + L.perm), T, p.K, p.H, p.SI > 0,
+            xg_out ? xg_out : reinterpret_cast<__half*>(ws + L.xg), reinterpret_cast<__half*>(ws + L.h16));
+    return cudaGetLastError();
+  }
   if (tc) {
     MOE_PDL(router_prep_kernel, dim3(T), dim3(256), 0, s, x, p.w.norm_w, p.H, p.cfg.rms_norm_eps,
                                          reinterpret_cast<float*>(ws + L.rms),
