@@ -23,9 +23,11 @@ box's host cores, all BLAS threads, same config, metric and unit.
 
 N > 1 (torchrun): expert parallel -- rank r holds routed experts
 [r*160/N, (r+1)*160/N), router and shared expert replicated, 64 tokens per rank
-(weak scaling); dispatch and combine are NCCL all-to-all exchanges of f16 rows,
-by default the fixed-capacity exchange (equal row blocks, no host synchronisation;
---ep-exchange exact: counts first, then exactly the routed rows).
+(weak scaling).  Decode batches take by default the token-replicated exchange
+(NCCL all-gather of the ranks' token records, reduce-scatter of fp32 per-token
+partial sums; no host synchronisation); --ep-exchange padded: fixed-capacity
+all-to-all of f16 rows; exact: counts first, then exactly the routed rows.
+Prefill batches take the exact exchange.
 
 --stack (torchrun, N = 2, 4 or 8): BASELINE config 4 -- 89 GLM-4.7-shape INT8 layers
 (seed + layer each, Zipf-skewed routing) resident expert parallel, 160/N experts of
@@ -350,6 +352,16 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
 
 
 # ------------------------------------------------------------------ expert parallel (N > 1)
+def _timed_forward(ep, x):  # noqa: ANN001, ANN202
+    """One instrumented forward (stage events) whose launches are all queued before
+    the device reaches them: a ~2.5 ms spin on the stream first lets the host issue
+    the whole forward, so the stage times are device time and not host issue gaps
+    (a forward issued onto an idle device runs at the host's launch pace)."""
+    import torch
+    torch.cuda._sleep(5_000_000)
+    return ep.forward(x, timed=True)
+
+
 def run_ep_qwen3(args, world: int, rank: int, local: int, tflops: float) -> dict:  # noqa: ANN001
     """BASELINE config 3 across the ranks: Qwen3-Next shape, 512/N experts per rank,
     1-token decode and 8192-token prefill per rank (weak scaling)."""
@@ -366,8 +378,8 @@ def run_ep_qwen3(args, world: int, rank: int, local: int, tflops: float) -> dict
     torch.cuda.synchronize()
     del blob
     torch.cuda.empty_cache()
-    # the 1-token decode uses the fixed-capacity exchange, the prefill the exact one
-    ep = ExpertParallelMoe(ops, padded_tokens=1 if args.ep_exchange == "padded" else 0)
+    # the 1-token decode uses the fixed-size exchange, the prefill the exact one
+    ep = ExpertParallelMoe(ops, **_small_exchange(args, 1))
     gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
     res = {}
     for T in (1, 8192):
@@ -376,7 +388,7 @@ def run_ep_qwen3(args, world: int, rank: int, local: int, tflops: float) -> dict
         ms = _time_steps(lambda: ep.forward(x), steps, args.warmup, world)
         tim = []
         for _ in range(3):
-            ep.forward(x, timed=True)
+            _timed_forward(ep, x)
             tim.append(ep.last_timing)
         a2a = float(np.median([t["a2a_ms"] for t in tim]))
         tot = float(np.median([t["total_ms"] for t in tim]))
@@ -411,7 +423,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     torch.cuda.synchronize()
     del blob
     torch.cuda.empty_cache()
-    ep = ExpertParallelMoe(ops, padded_tokens=T if args.ep_exchange == "padded" else 0)
+    ep = ExpertParallelMoe(ops, **_small_exchange(args, T))
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
     x = torch.randn((T, GLM["hidden"]), generator=gen, device="cuda")
 
@@ -422,7 +434,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
     # one instrumented forward per rank: share of the exchanges in the layer time
     tim = []
     for _ in range(max(3, min(args.steps, 10))):
-        ep.forward(x, timed=True)
+        _timed_forward(ep, x)
         tim.append(ep.last_timing)
     a2a = float(np.median([t["a2a_ms"] for t in tim]))
     tot = float(np.median([t["total_ms"] for t in tim]))
@@ -461,11 +473,12 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 MMA / fp32 accumulate (bf16-valued weights); fp32 routing; f16 exchange",
+            "dtype": "f16 MMA / fp32 accumulate (bf16-valued weights); fp32 routing; "
+                     + _exchange_dtype(args.ep_exchange),
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, random-init)",
             "config": {"workload": "BASELINE config 1 shape, expert parallel",
                        "tokens_per_rank": T, "experts_per_rank": e_loc,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)",
+                       "parallelism": f"ep{world} (NCCL collectives dispatch/combine)",
                        "exchange": _exchange_name(args.ep_exchange),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (rank 0)",
@@ -476,10 +489,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
                     "h2d_bytes_per_step": T * GLM["hidden"] * 4,
                     "d2h_bytes_per_step": T * GLM["hidden"] * 4, "ms_per_step": e2e_s * 1e3},
             "cpu_baseline": None,
-            # per forward: router, tail, dispatch (+ send metadata on the exact
-            # exchange); hist, scan, scatter, gather, two GEMMs (experts); scan, two
-            # GEMMs (shared); combine
-            "gpu_launches": (13 if args.ep_exchange == "padded" else 14) * args.steps,
+            "gpu_launches": _ep_launches(args.ep_exchange) * args.steps,
             "clocks": clocks,
             "other_configs": other,
         }))
@@ -490,8 +500,30 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
 
 
 def _exchange_name(kind: str) -> str:
-    return ("fixed-capacity (one all-to-all of equal row blocks each way, no host sync)"
-            if kind == "padded" else "exact (counts, then rows and ids; one host sync)")
+    return {"padded": "fixed-capacity (one all-to-all of equal row blocks each way, no host sync)",
+            "gathered": "token-replicated (all-gather of token records, reduce-scatter of fp32 "
+                        "partial sums; no host sync)",
+            "exact": "exact (counts, then rows and ids; one host sync)"}[kind]
+
+
+def _exchange_dtype(kind: str) -> str:
+    return ("f16 token rows and fp32 partial sums exchanged" if kind == "gathered"
+            else "f16 rows exchanged")
+
+
+def _small_exchange(args, tokens: int) -> dict:  # noqa: ANN001
+    """ExpertParallelMoe keywords for batches of at most `tokens` tokens."""
+    if args.ep_exchange == "exact":
+        return {"padded_tokens": 0}
+    return {"padded_tokens": tokens, "small_exchange": args.ep_exchange}
+
+
+def _ep_launches(kind: str) -> int:
+    """Kernels of one expert-parallel decode forward: routing (router, tail) and the
+    send rows (dispatch, + send metadata on the exact exchange); hist, scan,
+    scatter, gather, two GEMMs (experts; + the partial sums on the gathered
+    exchange); scan, two GEMMs (shared); combine."""
+    return {"padded": 13, "gathered": 14, "exact": 14}[kind]
 
 
 # ------------------------------------------------------------------ 89-layer stack (N > 1)
@@ -535,7 +567,7 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "vs_baseline": None,
             "config": {"workload": "BASELINE config 4", "layers": L, "global_tokens": batches,
                        "experts_per_rank": E // world if world else None,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/return)",
+                       "parallelism": f"ep{world} (NCCL collectives dispatch/return)",
                        "exchange": {"decode": _exchange_name(args.ep_exchange), "prefill": "exact"}}}
     if world < 2 or E % world or any(t % world for t in batches.values()):
         if rank == 0:
@@ -576,9 +608,8 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
         ops.bind_device(blob.data_ptr(), blob.numel(), meta)
         torch.cuda.synchronize()
         del blob
-        # decode batches take the fixed-capacity exchange, prefill the exact one
-        layers.append((ops, ExpertParallelMoe(
-            ops, padded_tokens=t_dec if args.ep_exchange == "padded" else 0)))
+        # decode batches take the fixed-size exchange, prefill the exact one
+        layers.append((ops, ExpertParallelMoe(ops, **_small_exchange(args, t_dec))))
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
 
@@ -604,7 +635,7 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
         touched = 0
         h = x
         for _ops, ep in layers:
-            h = ep.forward(h, timed=True)
+            h = _timed_forward(ep, h)
             a2a += ep.last_timing["a2a_ms"]
             tot += ep.last_timing["total_ms"]
             touched += ep.last_timing["recv_experts"]
@@ -635,13 +666,13 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
                           "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": results[f"decode_T{batches['decode']}"]["ms_per_step"],
                           "dtype": "INT8 weights widened to f16 in shared memory, f16 MMA / fp32 "
-                                   "accumulate; fp32 routing; f16 exchange",
+                                   "accumulate; fp32 routing; " + _exchange_dtype(args.ep_exchange),
                           "data": "synthetic (seeded N(0,1) tokens; per-layer seeded N(0,0.02) "
                                   "weights quantised per row; Zipf(1.1) router bias)",
                           "resident_gib_per_gpu": resident / 2**30, "build_s": build_s,
                           "workloads": results, "clocks": clocks,
                           "gpu_launches_per_layer": {
-                              "decode": 13 if args.ep_exchange == "padded" else 14,
+                              "decode": _ep_launches(args.ep_exchange),
                               "prefill": 20}}))
     for ops, _ep in layers:
         ops.close()
@@ -882,8 +913,9 @@ def main() -> None:
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
-    ap.add_argument("--ep-exchange", choices=["padded", "exact"], default="padded",
-                    help="N > 1 decode batches: fixed-capacity or exact all-to-all")
+    ap.add_argument("--ep-exchange", choices=["padded", "gathered", "exact"], default="gathered",
+                    help="N > 1 decode batches: fixed-capacity all-to-all, token-replicated "
+                         "all-gather/reduce-scatter, or exact all-to-all")
     ap.add_argument("--stack", action="store_true",
                     help="BASELINE config 4: resident INT8 layer stack, expert parallel (N >= 2)")
     ap.add_argument("--stack-layers", type=int, default=89)

@@ -91,7 +91,7 @@ static int pick_bn(int T) {
 // `groups` expert groups; `shared_rows` rows for the shared expert; the router
 // buffers only when `router`.
 static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, int shared_rows,
-                                  int bn, bool router) {
+                                  int bn, bool router, bool ybuf = false) {
   WsLayout L{};
   const int T = rows;
   const size_t R = static_cast<size_t>(T) * k;
@@ -116,7 +116,7 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
   L.xg = take(R * p.H * 2);
   L.act = take(R * p.I * 2);
   L.act_s = take(static_cast<size_t>(TS) * p.SI * 2);
-  L.y = take(router ? R * p.H * 2 : 0);  // routed expert outputs, f16, dispatch order
+  L.y = take((router || ybuf) ? R * p.H * 2 : 0);  // routed expert outputs, f16, dispatch order
   L.y_s = take(p.SI > 0 ? static_cast<size_t>(TS) * p.H * 4 : 0);
   if (router) {
     const RouterGeom g = router_geometry(p, T);
@@ -169,6 +169,17 @@ WsLayout ws_layout(const Plan& p, int T) {
 WsLayout ws_layout_ep_experts(const Plan& p, int R, int expect) {
   const int per_expert = (2 * expect + p.n_local - 1) / (p.n_local > 0 ? p.n_local : 1);
   return ws_layout_general(p, R, 1, p.n_local, 0, pick_bn(per_expert > 0 ? per_expert : 1), false);
+}
+
+// Expert side of the token-replicated exchange: the K slots of `rows` gathered
+// token records, of which those routed to the resident experts are grouped, with
+// the f16 expert outputs in grouped order (L.y).  On average a rank keeps 1/world
+// of the slots; the tile width follows that, the buffers the worst case.
+WsLayout ws_layout_ep_gathered(const Plan& p, int rows) {
+  const int64_t kept = static_cast<int64_t>(rows) * p.K * p.n_local / std::max(p.E, 1);
+  const int64_t per_expert = (2 * kept + p.n_local - 1) / std::max(p.n_local, 1);
+  return ws_layout_general(p, rows, p.K, p.n_local, 0,
+                           pick_bn(static_cast<int>(std::max<int64_t>(per_expert, 1))), false, true);
 }
 
 // ------------------------------------------------------------ name parsing
@@ -795,8 +806,8 @@ int moe_ep_experts(MoePlan* plan, const void* recv_rows, const int32_t* recv_exp
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const WsLayout L = ws_layout_ep_experts(p, R, R);
   char* ws = static_cast<char*>(workspace);
-  MOE_CUDA(launch_group_rows(p, L, ws, recv_experts, 1, false, static_cast<const __half*>(recv_rows),
-                             p.H, R, s));
+  MOE_CUDA(launch_group_rows(p, L, ws, RowKeys{recv_experts, 1, 1, 0, 0},
+                             static_cast<const __half*>(recv_rows), p.H, R, s));
   MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr, p.n_local}, s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
                        GemmIO{R, 0, static_cast<__half*>(y_out),
@@ -865,12 +876,93 @@ int moe_ep_experts_padded(MoePlan* plan, const void* recv_rows, int32_t cap, voi
   const __half* rows = static_cast<const __half*>(recv_rows);
   // the local expert id is the first int32 of each row's 16-byte tail
   const int32_t* keys = reinterpret_cast<const int32_t*>(rows + p.H);
-  MOE_CUDA(launch_group_rows(p, L, ws, keys, (p.H + 8) / 2, true, rows, p.H + 8, R, s));
+  MOE_CUDA(launch_group_rows(p, L, ws, RowKeys{keys, (p.H + 8) / 2, 1, 0, 1}, rows, p.H + 8, R, s));
   MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{R, 0, nullptr, nullptr, p.n_local}, s));
   MOE_CUDA(launch_gemm(p, L, ws, true,
                        GemmIO{R, 0, static_cast<__half*>(y_out),
                               reinterpret_cast<const int32_t*>(ws + L.perm), p.n_local},
                        s));
+  return MOE_OK;
+}
+
+int32_t moe_ep_token_row_halves(const MoePlan* plan) {
+  if (!plan || plan->p.E == 0) return 0;
+  return ep_token_row_halves(plan->p);
+}
+
+int moe_ep_token_pack(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap, void* send_rows,
+                      void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T above max_tokens");
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK) return rc;
+  if (cap <= 0 || cap < T) return fail(MOE_ERR_INVALID, "cap must be positive and at least T");
+  if (!send_rows || (T > 0 && !x_dev)) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(send_rows) || (T > 0 && misaligned16(x_dev)))
+    return fail(MOE_ERR_INVALID, "x and send_rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  WsLayout L{};
+  if (T > 0) {
+    L = ws_layout(p, T);
+    MOE_CUDA(launch_route(p, L, ws, x_dev, T, false, s, nullptr));
+  }
+  MOE_CUDA(launch_ep_token_pack(p, L, ws, x_dev, T, cap, static_cast<__half*>(send_rows), s));
+  return MOE_OK;
+}
+
+uint64_t moe_ep_gathered_workspace_bytes(const MoePlan* plan, int32_t rows) {
+  if (!plan || rows <= 0 || plan->p.E == 0) return 0;
+  if (static_cast<int64_t>(rows) * plan->p.K > INT32_MAX) return 0;
+  return ws_layout_ep_gathered(plan->p, rows).total;
+}
+
+int moe_ep_experts_gathered(MoePlan* plan, const void* recv_rows, int32_t rows, float* partial_out,
+                            void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (rows < 0 || static_cast<int64_t>(rows) * p.K > INT32_MAX)
+    return fail(MOE_ERR_INVALID, "bad row count");
+  int rc = check_ep(plan, rows, workspace, workspace_bytes,
+                    rows > 0 ? ws_layout_ep_gathered(p, rows).total : 0);
+  if (rc != MOE_OK || rows == 0) return rc;
+  if (!recv_rows || !partial_out) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(recv_rows) || misaligned16(partial_out))
+    return fail(MOE_ERR_INVALID, "recv_rows and partial_out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout_ep_gathered(p, rows);
+  char* ws = static_cast<char*>(workspace);
+  const __half* rec = static_cast<const __half*>(recv_rows);
+  const int ld = ep_token_row_halves(p);
+  // the K global expert ids follow each record's H values; keys outside this
+  // rank's range belong to other ranks and are skipped
+  const RowKeys keys{reinterpret_cast<const int32_t*>(rec + p.H), ld / 2, p.K, p.e_begin, 2};
+  MOE_CUDA(launch_group_rows(p, L, ws, keys, rec, ld, rows, s));
+  const int slots = rows * p.K;
+  __half* y = reinterpret_cast<__half*>(ws + L.y);
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{slots, 0, nullptr, nullptr, p.n_local}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, GemmIO{slots, 0, y, nullptr, p.n_local}, s));
+  MOE_CUDA(launch_ep_partial(p, rec, rows, y, reinterpret_cast<const int32_t*>(ws + L.slot_row),
+                             partial_out, s));
+  return MOE_OK;
+}
+
+int moe_ep_combine_partial(MoePlan* plan, const float* x_dev, int32_t T, const float* partial,
+                           float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK || T == 0) return rc;
+  if (!x_dev || !partial || !out_dev) return fail(MOE_ERR_INVALID, "null argument");
+  if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  if (misaligned16(x_dev) || misaligned16(partial) || misaligned16(out_dev))
+    return fail(MOE_ERR_INVALID, "x, partial and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_combine_partial(p, x_dev, partial, reinterpret_cast<float*>(ws + L.y_s),
+                                  reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
   return MOE_OK;
 }
 

@@ -164,6 +164,7 @@ struct WsLayout {
 
 WsLayout ws_layout(const Plan& p, int T);
 WsLayout ws_layout_ep_experts(const Plan& p, int R, int expect);
+WsLayout ws_layout_ep_gathered(const Plan& p, int rows, int cap);
 
 // Router launch geometry: rx router-row tiles x splits K-splits x tz token tiles.
 struct RouterGeom {
@@ -180,16 +181,44 @@ bool route_uses_small(const Plan& p, int T);  // one-launch routing of small dec
 // the normalised f16 rows of every routed slot (xg) and of the shared expert (h16).
 cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                          bool dispatch, cudaStream_t s, __half* xg_out = nullptr);
-// Expert-parallel helpers: group `n` received rows by their local expert key
-// (stable: receive order inside an expert), gather them into L.xg and build the
-// tile lists; and the tile lists of the shared expert alone for T local tokens.
-cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
-                              int key_stride, bool padded, const __half* rows, int row_ld, int n,
-                              cudaStream_t s);
+// Where the expert keys of received rows sit: row t has per_row slots whose keys
+// are keys[t * key_ld + k] - key_base (k < per_row); pad_mode as perm_hist_kernel
+// (0 every key must be a resident expert, 1 negative keys are unused rows,
+// 2 keys outside the resident range are skipped).
+struct RowKeys {
+  const int32_t* keys;
+  int key_ld;
+  int per_row;
+  int key_base;
+  int pad_mode;
+};
+// Expert-parallel helpers: group the slots of `n` received rows by their local
+// expert key (stable: receive order inside an expert), gather the rows of the
+// kept slots into L.xg and build the tile lists; and the tile lists of the shared
+// expert alone for T local tokens.
+cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const RowKeys& k,
+                              const __half* rows, int row_ld, int n, cudaStream_t s);
 // Fixed-capacity send rows of the expert-parallel exchange (after launch_route
 // without dispatch): [world * cap] rows of H + 8 f16, tails carrying local ids.
 cudaError_t launch_ep_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                            int cap, __half* send, cudaStream_t s);
+// Token-replicated exchange.  Row width in f16 elements of one token record:
+// H normalised values, then K int32 global expert ids and K fp32 weights,
+// padded to 16 bytes.
+int ep_token_row_halves(const Plan& p);
+// [cap] token records of the local T tokens (after launch_route without
+// dispatch); rows T..cap-1 carry expert id -1 in every slot.  Also h16 for the
+// shared expert.
+cudaError_t launch_ep_token_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                                 int cap, __half* send, cudaStream_t s);
+// partial[t] = sum over the slots k of token record t whose expert is resident
+// of w_k * y[slot_row[t*K + k]] (fp32, slot order), zero for a token without one.
+cudaError_t launch_ep_partial(const Plan& p, const __half* rows, int n, const __half* y,
+                              const int32_t* slot_row, float* partial, cudaStream_t s);
+// out = x + (partial + shared expert), the combine of the token-replicated exchange.
+cudaError_t launch_combine_partial(const Plan& p, const float* x, const float* partial,
+                                   const float* y_s, const float* sgate, float* out, int T,
+                                   cudaStream_t s);
 cudaError_t launch_shared_tiles(const Plan& p, const WsLayout& L, char* ws, int T, cudaStream_t s);
 cudaError_t launch_row_prep(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
                             cudaStream_t s);

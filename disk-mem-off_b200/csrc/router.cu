@@ -1062,11 +1062,13 @@ __global__ void __launch_bounds__(256) route_small_kernel(
 // ------------------------------------------------------------------ prefill permutation
 // Per chunk of 1024 tokens: a bitmask per expert, written to global with its
 // popcount histogram; a single-CTA scan; then one thread per (token, slot).
-// Key q sits at ids[q * key_stride]; with allow_pad a negative key marks an
-// unused row (fixed-capacity exchange) and is skipped.
+// Slot q = t * K + k (token t, slot k) has key ids[t * key_ld + k] - key_base.
+// allow_pad 1: a negative key marks an unused row (fixed-capacity exchange) and
+// is skipped; 2: every key outside [0, E) is skipped (the token-replicated
+// exchange, where other ranks own those experts); 0: such a key is an error.
 __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restrict__ ids, int T,
-                                                         int K, int E, int key_stride, int allow_pad,
-                                                         uint32_t* __restrict__ bmg,
+                                                         int K, int E, int key_ld, int key_base,
+                                                         int allow_pad, uint32_t* __restrict__ bmg,
                                                          int32_t* __restrict__ hist, int* err) {
   pdl_enter();
   extern __shared__ uint32_t bm[];  // [E][32]
@@ -1077,10 +1079,10 @@ __global__ void __launch_bounds__(1024) perm_hist_kernel(const int32_t* __restri
   __syncthreads();
   for (int q = threadIdx.x; q < tcnt * K; q += blockDim.x) {
     const int tl = q / K;
-    const int e = ids[(static_cast<size_t>(tbeg) * K + q) * key_stride];
-    if (e < 0 && allow_pad) continue;
+    const int raw = ids[static_cast<size_t>(tbeg + tl) * key_ld + (q - tl * K)];
+    const int e = raw - key_base;
     if (e < 0 || e >= E) {
-      record_error(err, DEV_BAD_ROUTE);
+      if (!(allow_pad == 2 || (allow_pad == 1 && raw < 0))) record_error(err, DEV_BAD_ROUTE);
       continue;
     }
     atomicOr(&bm[e * 32 + (tl >> 5)], 1u << (tl & 31));
@@ -1122,13 +1124,14 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
 __global__ void __launch_bounds__(256) perm_scatter_kernel(const int32_t* __restrict__ ids,
                                                            const uint32_t* __restrict__ bmg,
                                                            const int32_t* __restrict__ base,
-                                                           int T, int K, int E, int key_stride,
+                                                           int T, int K, int E, int key_ld,
+                                                           int key_base,
                                                            int32_t* __restrict__ perm,
                                                            int32_t* __restrict__ slot_row) {
   pdl_enter();
   for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < T * K; q += gridDim.x * blockDim.x) {
     const int t = q / K;
-    const int e = ids[static_cast<size_t>(q) * key_stride];
+    const int e = ids[static_cast<size_t>(t) * key_ld + (q - t * K)] - key_base;
     if (e < 0 || e >= E) continue;  // reported by perm_hist_kernel
     const int c = t / kPermChunk, tl = t % kPermChunk;
     const uint32_t* row = bmg + (static_cast<size_t>(c) * E + e) * 32;
@@ -1337,6 +1340,44 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
       for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
     } else {
       norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H, row);
+    }
+  }
+}
+
+// Token records of the token-replicated exchange, one CTA per record: H
+// normalised f16 values, then the token's K global expert ids (int32) and K
+// routing weights (fp32), zero-padded to 16 bytes.  Records T..cap-1 carry id -1
+// in every slot (no rank serves them).  With with_shared, h16 (shared expert)
+// as well.  Source: x normalised here, or the f16 rows h16src (prefill routing
+// already built them).
+__global__ void __launch_bounds__(256) ep_token_pack_kernel(
+    const float* __restrict__ x, const float* __restrict__ wn, const float* __restrict__ rms,
+    const __half* __restrict__ h16src, const int32_t* __restrict__ ids,
+    const float* __restrict__ wts, int T, int K, int H, int ld, int cap, int with_shared,
+    __half* __restrict__ send, __half* __restrict__ h16) {
+  pdl_enter();
+  const int tail_words = (ld - H) / 2;  // int32 words after the values
+  for (int t = blockIdx.x; t < cap; t += gridDim.x) {
+    __half* row = send + static_cast<size_t>(t) * ld;
+    int32_t* tail = reinterpret_cast<int32_t*>(row + H);
+    for (int i = threadIdx.x; i < tail_words; i += blockDim.x) {
+      int32_t v = 0;
+      if (i < K) {
+        v = t < T ? ids[static_cast<size_t>(t) * K + i] : -1;
+      } else if (i < 2 * K && t < T) {
+        v = __float_as_int(wts[static_cast<size_t>(t) * K + (i - K)]);
+      }
+      tail[i] = v;
+    }
+    if (t >= T) continue;
+    if (h16src) {
+      const uint4* in = reinterpret_cast<const uint4*>(h16src + static_cast<size_t>(t) * H);
+      uint4* out = reinterpret_cast<uint4*>(row);
+      for (int v = threadIdx.x; v < (H >> 3); v += blockDim.x) out[v] = in[v];
+    } else {
+      norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H, row);
+      if (with_shared) norm_row_f16(x + static_cast<size_t>(t) * H, wn, rms[t], H,
+                                    h16 + static_cast<size_t>(t) * H);
     }
   }
 }
@@ -1566,7 +1607,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
                        done_hist);
     if (st != cudaSuccess) return st;
     MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
-        ids, T, K, E, 1, 0, bmg, hist, p.d_err);
+        ids, T, K, E, K, 0, 0, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, hist, L.nchunks, base, offsets, ta);
@@ -1574,7 +1615,7 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
     if (st != cudaSuccess) return st;
     const int entries = T * K;
     MOE_PDL(perm_scatter_kernel, dim3(min((entries + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, 
-        ids, bmg, base, T, K, E, 1, perm, slot_row);
+        ids, bmg, base, T, K, E, K, 0, perm, slot_row);
   }
   st = cudaGetLastError();
   if (st != cudaSuccess || !dispatch) return st;
@@ -1592,9 +1633,8 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
 }
 
 // ------------------------------------------------------------------ expert-parallel helpers
-cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const int32_t* keys,
-                              int key_stride, bool padded, const __half* rows, int row_ld, int n,
-                              cudaStream_t s) {
+cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const RowKeys& k,
+                              const __half* rows, int row_ld, int n, cudaStream_t s) {
   const int E = p.n_local;
   uint32_t* bmg = reinterpret_cast<uint32_t*>(ws + L.bm);
   int32_t* hist = reinterpret_cast<int32_t*>(ws + L.hist);
@@ -1609,19 +1649,21 @@ cudaError_t launch_group_rows(const Plan& p, const WsLayout& L, char* ws, const 
   if (st != cudaSuccess) return st;
   if (n > 0) {
     MOE_PDL(perm_hist_kernel, dim3(L.nchunks), dim3(1024), static_cast<size_t>(E) * 32 * sizeof(uint32_t), s, 
-        keys, n, 1, E, key_stride, padded ? 1 : 0, bmg, hist, p.d_err);
+        k.keys, n, k.per_row, E, k.key_ld, k.key_base, k.pad_mode, bmg, hist, p.d_err);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
   }
   MOE_PDL(perm_scan_kernel, dim3(1), dim3(1024), 0, s, hist, L.nchunks, base, offsets, ta);
   st = cudaGetLastError();
   if (st != cudaSuccess || n == 0) return st;
-  MOE_PDL(perm_scatter_kernel, dim3(min((n + 255) / 256, p.num_sms * 8)), dim3(256), 0, s, keys, bmg, base, n, 1, E,
-                                                                         key_stride, perm, slot_row);
+  const int slots = n * k.per_row;
+  MOE_PDL(perm_scatter_kernel, dim3(min((slots + 255) / 256, p.num_sms * 8)), dim3(256), 0, s,
+          k.keys, bmg, base, n, k.per_row, E, k.key_ld, k.key_base, perm, slot_row);
   st = cudaGetLastError();
   if (st != cudaSuccess) return st;
-  MOE_PDL(gather_rows_kernel, dim3(min(n, p.num_sms * 8)), dim3(256), 0, s, rows, perm, n, p.H,
-          row_ld, 1, padded ? offsets + E : nullptr, reinterpret_cast<__half*>(ws + L.xg));
+  MOE_PDL(gather_rows_kernel, dim3(min(slots, p.num_sms * 8)), dim3(256), 0, s, rows, perm, slots,
+          p.H, row_ld, k.per_row, k.pad_mode ? offsets + E : nullptr,
+          reinterpret_cast<__half*>(ws + L.xg));
   return cudaGetLastError();
 }
 
@@ -1640,6 +1682,22 @@ cudaError_t launch_ep_pack(const Plan& p, const WsLayout& L, char* ws, const flo
           reinterpret_cast<const int32_t*>(at(L.offsets)), T, p.K, p.H, p.n_local, world, cap,
           with_shared, send, reinterpret_cast<int32_t*>(at(L.slot_row)),
           reinterpret_cast<__half*>(at(L.h16)), p.d_err);
+  return cudaGetLastError();
+}
+
+int ep_token_row_halves(const Plan& p) { return p.H + ((4 * p.K + 7) & ~7); }
+
+cudaError_t launch_ep_token_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                                 int cap, __half* send, cudaStream_t s) {
+  const bool tc = T > 0 && route_uses_tc_router(p, T);
+  const int with_shared = (T > 0 && !tc && p.SI > 0) ? 1 : 0;
+  auto at = [&](size_t off) { return T > 0 ? ws + off : nullptr; };
+  MOE_PDL(ep_token_pack_kernel, dim3(min(cap, p.num_sms * 8)), dim3(256), 0, s, x, p.w.norm_w,
+          reinterpret_cast<const float*>(at(L.rms)),
+          tc ? reinterpret_cast<const __half*>(at(L.h16)) : nullptr,
+          reinterpret_cast<const int32_t*>(at(L.ids)), reinterpret_cast<const float*>(at(L.wts)),
+          T, p.K, p.H, ep_token_row_halves(p), cap, with_shared, send,
+          reinterpret_cast<__half*>(at(L.h16)));
   return cudaGetLastError();
 }
 

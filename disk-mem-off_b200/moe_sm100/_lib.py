@@ -99,6 +99,14 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_ep_padded_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
     "moe_ep_experts_padded": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_uint64,
                                         c_void_p]),
+    "moe_ep_token_row_halves": (c_int32, [c_void_p]),
+    "moe_ep_token_pack": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                                    c_uint64, c_void_p]),
+    "moe_ep_gathered_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
+    "moe_ep_experts_gathered": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
+                                          c_uint64, c_void_p]),
+    "moe_ep_combine_partial": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
+                                         c_void_p, c_uint64, c_void_p]),
     "moe_status": (c_int32, [c_void_p, c_void_p]),
     "moe_attn_create": (c_int32, [POINTER(MoeAttnConfigC), POINTER(c_void_p)]),
     "moe_attn_destroy": (c_int32, [c_void_p]),

@@ -21,6 +21,15 @@ each row's tail (-1 marks an unused row), and steps 2-3 become one all_to_all of
 equal splits.  No counts cross and the host never waits, so the CPU runs ahead of
 the device across layers; the price is moving cap rows per rank pair.
 
+Or small batches replicate the tokens instead (``small_exchange="gathered"``):
+every rank all-gathers fixed-size token records (normalised row, top-k expert ids
+and weights; ``padded_tokens`` records per rank), applies its resident experts to
+the slots of all gathered tokens that route to them, and one reduce-scatter (sum)
+of per-token fp32 partial sums returns each rank the routed total for its own
+tokens.  The host never waits either, and the bytes per rank are world * cap
+records in and world * cap fp32 rows out, independent of top_k, where the padded
+exchange moves world * cap * min(top_k, experts per rank) rows each way.
+
 The exchanges are torch.distributed collectives (NCCL over NVLink on B200; gloo
 on CPU in the tests).  The device work is libmoe_sm100's moe_ep_* entry points.
 """
@@ -46,7 +55,11 @@ class EPOps(Protocol):
     Optional: ``start_shared(x)`` (shared expert early, overlapping the exchange);
     for the fixed-capacity exchange ``capacity(tokens)``, ``dispatch_padded(x, cap)``
     (send rows [world*cap, ...] with the local expert id, -1 unused, in each row),
-    ``experts_padded(recv, cap)`` and, for timed forwards, ``padded_ids(recv)``.
+    ``experts_padded(recv, cap)`` and, for timed forwards, ``padded_ids(recv)``;
+    for the token-replicated exchange ``token_pack(x, cap)`` (token records
+    [cap, ...]), ``experts_gathered(recv)`` (fp32 partial sums [rows, H]),
+    ``combine_partial(x, partial)`` and, for timed forwards, ``gathered_ids(recv)``
+    (global expert ids [rows, top_k], -1 for unused records).
     """
 
     def dispatch(self, x: Any) -> tuple[Any, Any, Any]: ...      # rows, local expert ids, offsets
@@ -59,21 +72,30 @@ class EPOps(Protocol):
 class ExpertParallelMoe:
     """Runs the dispatch / expert / combine protocol of one rank.
 
-    ``padded_tokens`` > 0 switches batches of at most that many tokens to the
-    fixed-capacity exchange (ops must provide ``capacity``, ``dispatch_padded`` and
-    ``experts_padded``).  Every rank must take the same branch in the same forward:
-    give all ranks the same ``padded_tokens`` and batches on the same side of it
+    ``padded_tokens`` > 0 switches batches of at most that many tokens to a
+    fixed-size exchange: ``small_exchange="padded"`` the fixed-capacity one (ops must
+    provide ``capacity``, ``dispatch_padded`` and ``experts_padded``), "gathered" the
+    token-replicated one (``token_pack``, ``experts_gathered``, ``combine_partial``).
+    Every rank must take the same branch in the same forward: give all ranks the
+    same ``padded_tokens`` and ``small_exchange`` and batches on the same side of it
     (decode steps below, prefill above).
     """
 
-    def __init__(self, ops: EPOps, group: Any = None, padded_tokens: int = 0) -> None:
+    def __init__(self, ops: EPOps, group: Any = None, padded_tokens: int = 0,
+                 small_exchange: str = "padded") -> None:
+        if small_exchange not in ("padded", "gathered"):
+            raise ValueError("small_exchange must be 'padded' or 'gathered'")
         self.ops = ops
         self.group = group
         self.last_timing: dict[str, float] = {}
         self.padded_tokens = int(padded_tokens)
-        self.cap = int(ops.capacity(self.padded_tokens)) if self.padded_tokens > 0 else 0
-        if self.padded_tokens > 0 and self.cap <= 0:
-            raise ValueError("no fixed capacity for padded_tokens")
+        self.small_exchange = small_exchange
+        self.cap = 0
+        if self.padded_tokens > 0:
+            self.cap = (self.padded_tokens if small_exchange == "gathered"
+                        else int(ops.capacity(self.padded_tokens)))
+            if self.cap <= 0:
+                raise ValueError("no fixed capacity for padded_tokens")
 
     def forward(self, x: Any, timed: bool = False) -> Any:
         torch = _torch()
@@ -86,7 +108,10 @@ class ExpertParallelMoe:
                 ev[name] = e
 
         if 0 < self.padded_tokens and x.shape[0] <= self.padded_tokens:
-            out, n_recv = self._forward_padded(x, mark)
+            if self.small_exchange == "gathered":
+                out, n_recv = self._forward_gathered(x, mark)
+            else:
+                out, n_recv = self._forward_padded(x, mark)
         else:
             out, n_recv = self._forward_exact(x, mark)
         if timed and x.is_cuda:
@@ -128,6 +153,39 @@ class ExpertParallelMoe:
             valid = ids[ids >= 0]
             return {"recv_rows": int(valid.numel()),
                     "recv_experts": int(torch.unique(valid).numel()) if valid.numel() else 0,
+                    "exchanged_rows": int(recv.shape[0])}
+        return out, counts
+
+    def _forward_gathered(self, x: Any, mark: Any) -> tuple[Any, Any]:
+        torch = _torch()
+        import torch.distributed as dist
+        g, cap = self.group, self.cap
+        world = dist.get_world_size(g)
+        mark("start")
+        send = self.ops.token_pack(x, cap)
+        mark("dispatched")
+        start_shared = getattr(self.ops, "start_shared", None)
+        if start_shared is not None:
+            start_shared(x)
+        recv = send.new_empty((world * cap,) + tuple(send.shape[1:]))
+        dist.all_gather_into_tensor(recv, send, group=g)
+        mark("exchanged")
+        partial_all = self.ops.experts_gathered(recv)
+        mark("computed")
+        partial = partial_all.new_empty((cap,) + tuple(partial_all.shape[1:]))
+        dist.reduce_scatter_tensor(partial, partial_all, op=dist.ReduceOp.SUM, group=g)
+        mark("returned")
+        out = self.ops.combine_partial(x, partial)
+        mark("end")
+
+        def counts() -> dict[str, float]:
+            ids = self.ops.gathered_ids(recv)
+            valid = ids[ids >= 0]
+            rank = dist.get_rank(g)
+            e_loc = self.ops.experts_per_rank
+            mine = valid[(valid >= rank * e_loc) & (valid < (rank + 1) * e_loc)]
+            return {"recv_rows": int(mine.numel()),
+                    "recv_experts": int(torch.unique(mine).numel()) if mine.numel() else 0,
                     "exchanged_rows": int(recv.shape[0])}
         return out, counts
 
@@ -263,6 +321,66 @@ class DeviceEPOps:
         h = self.cfg.hidden
         return recv[:, h:h + 8].contiguous().view(_torch().int32)[:, 0]
 
+    @property
+    def experts_per_rank(self) -> int:
+        return self.cfg.expert_end - self.cfg.expert_begin
+
+    def token_pack(self, x: Any, cap: int) -> Any:
+        """Token records [cap, H + tail] f16 of the local tokens (token-replicated
+        exchange): normalised row, top-k global expert ids and weights."""
+        torch = _torch()
+        t = x.shape[0]
+        plan = self.layer._plan
+        ws = self._buf("ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
+        send = torch.empty((cap, int(lib().moe_ep_token_row_halves(plan))), dtype=torch.float16,
+                           device=x.device)
+        check(lib().moe_ep_token_pack(plan, c_void_p(x.data_ptr()), t, cap,
+                                      c_void_p(send.data_ptr()), c_void_p(ws.data_ptr()),
+                                      ws.numel(), c_void_p(_stream_handle(None))))
+        self._T = t
+        return send
+
+    def experts_gathered(self, recv: Any) -> Any:
+        """fp32 partial sums [rows, H] of this rank's experts over gathered records."""
+        torch = _torch()
+        rows = recv.shape[0]
+        plan = self.layer._plan
+        partial = torch.empty((rows, self.cfg.hidden), dtype=torch.float32, device=recv.device)
+        ws = self._buf("ws_ep", int(lib().moe_ep_gathered_workspace_bytes(plan, rows)))
+        check(lib().moe_ep_experts_gathered(plan, c_void_p(recv.data_ptr()), rows,
+                                            c_void_p(partial.data_ptr()), c_void_p(ws.data_ptr()),
+                                            ws.numel(), c_void_p(_stream_handle(None))))
+        return partial
+
+    def gathered_ids(self, recv: Any) -> Any:
+        """Global expert ids [rows, top_k] of gathered token records (-1: unused)."""
+        h, k = self.cfg.hidden, self.cfg.top_k
+        return recv[:, h:].contiguous().view(_torch().int32)[:, :k]
+
+    def combine_partial(self, x: Any, partial: Any) -> Any:
+        torch = _torch()
+        out = torch.empty_like(x)
+        t = x.shape[0]
+        if t == 0:
+            return out
+        plan = self.layer._plan
+        ws = self._ws
+        s = c_void_p(_stream_handle(None))
+        self._join_shared(x, plan, ws, s)
+        check(lib().moe_ep_combine_partial(plan, c_void_p(x.data_ptr()), t,
+                                           c_void_p(partial.data_ptr()), c_void_p(out.data_ptr()),
+                                           c_void_p(ws.data_ptr()), ws.numel(), s))
+        return out
+
+    def _join_shared(self, x: Any, plan: Any, ws: Any, s: Any) -> None:
+        """Wait for the shared expert started early, or run it now."""
+        torch = _torch()
+        if self._shared_done is not None:
+            torch.cuda.current_stream(x.device).wait_event(self._shared_done)
+            self._shared_done = None
+        else:
+            check(lib().moe_ep_shared(plan, x.shape[0], c_void_p(ws.data_ptr()), ws.numel(), s))
+
     def experts(self, rows: Any, expert_ids: Any) -> Any:
         torch = _torch()
         r = rows.shape[0]
@@ -303,11 +421,7 @@ class DeviceEPOps:
         plan = self.layer._plan
         ws = self._ws
         s = c_void_p(_stream_handle(None))
-        if self._shared_done is not None:
-            torch.cuda.current_stream(x.device).wait_event(self._shared_done)
-            self._shared_done = None
-        else:
-            check(lib().moe_ep_shared(plan, t, c_void_p(ws.data_ptr()), ws.numel(), s))
+        self._join_shared(x, plan, ws, s)
         check(lib().moe_ep_combine(plan, c_void_p(x.data_ptr()), t, c_void_p(y_back.data_ptr()),
                                    c_void_p(out.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(), s))
         return out

@@ -224,6 +224,35 @@ uint64_t moe_ep_padded_workspace_bytes(const MoePlan* plan, int32_t cap);
 int moe_ep_experts_padded(MoePlan* plan, const void* recv_rows, int32_t cap, void* y_out,
                           void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Token-replicated exchange (no host synchronisation; decode batches on many
+ * ranks).  Instead of sending one row per routed slot to the slot's owner, every
+ * rank sends its whole batch once to every rank (an all-gather of fixed-size token
+ * records), each rank applies its resident experts to the slots of all gathered
+ * tokens that route to them and writes one fp32 partial sum per token, and a
+ * reduce-scatter (sum) brings each rank the total for its own tokens.  Bytes moved
+ * per rank do not grow with top_k or with padding to a capacity: world * cap token
+ * records in, world * cap fp32 rows out.  All ranks use the same cap >= their T.
+ *   1. moe_ep_token_pack: route; send_rows [cap, moe_ep_token_row_halves(plan)]
+ *      f16 token records: H normalised values, then the token's top_k global
+ *      expert ids (int32) and routing weights (fp32), zero-padded to 16 bytes;
+ *      records T..cap-1 carry id -1 in every slot.  Workspace as moe_ep_dispatch.
+ *   2. caller: all-gather of the records -> recv_rows [world*cap, ...] (rank order).
+ *   3. moe_ep_experts_gathered(rows = world*cap): partial_out [rows, H] fp32, row t
+ *      = sum over the slots of record t routed to this rank's experts of w * y
+ *      (slot order), zero where there is none.  Workspace
+ *      moe_ep_gathered_workspace_bytes(plan, rows).
+ *   4. caller: reduce-scatter (sum) of partial_out -> partial [cap, H] fp32.
+ *   5. moe_ep_shared (any time after step 1) and moe_ep_combine_partial:
+ *      out = x + (partial + shared expert), over the first T rows of partial. */
+int32_t moe_ep_token_row_halves(const MoePlan* plan);
+int moe_ep_token_pack(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap, void* send_rows,
+                      void* workspace, uint64_t workspace_bytes, void* stream);
+uint64_t moe_ep_gathered_workspace_bytes(const MoePlan* plan, int32_t rows);
+int moe_ep_experts_gathered(MoePlan* plan, const void* recv_rows, int32_t rows, float* partial_out,
+                            void* workspace, uint64_t workspace_bytes, void* stream);
+int moe_ep_combine_partial(MoePlan* plan, const float* x_dev, int32_t T, const float* partial,
+                           float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Synchronise `stream`, then read and clear the device error word of the plan.
  * Returns MOE_OK, MOE_ERR_TIMEOUT (a bounded wait ran out), MOE_ERR_RANGE (an f16
  * activation or expert output overflowed) or MOE_ERR_DEVICE. */

@@ -1,8 +1,9 @@
 """Expert-parallel protocol on CPU ranks (gloo, world size 2).
 
 moe_sm100.ep.ExpertParallelMoe is the product code that exchanges row counts,
-rows, local expert ids and expert outputs between ranks (exact exchange), or
-fixed-capacity row blocks with the ids in their tails (padded exchange).  Here each rank plugs
+rows, local expert ids and expert outputs between ranks (exact exchange),
+fixed-capacity row blocks with the ids in their tails (padded exchange), or
+token records and per-token partial sums (token-replicated exchange).  Here each rank plugs
 in oracle-based stand-ins for the device ops, so the test checks the protocol
 itself (splits, ordering, reverse exchange, combine indexing) against the
 single-process oracle, and that malformed dispatch output fails on the host
@@ -101,6 +102,63 @@ class OracleEPOps:
             y[sel] = self._swiglu(r[sel, :hdim], f"mlp.experts.{self.rank * self.e_loc + int(le)}.")
         return torch.from_numpy(y)
 
+    # token-replicated exchange: records [cap, H + 2K], the normalised row, then the
+    # K global expert ids (-1: unused record) and the K routing weights, standing
+    # in for the device format's f16 row + int32/fp32 tail
+    @property
+    def experts_per_rank(self) -> int:
+        return self.e_loc
+
+    def token_pack(self, x: torch.Tensor, cap: int) -> torch.Tensor:
+        k = self.cfg.top_k
+        hdim = x.shape[1]
+        send = np.zeros((cap, hdim + 2 * k), dtype=np.float32)
+        send[:, hdim:hdim + k] = -1
+        self.state = (np.zeros((0, hdim), np.float32),)
+        if x.shape[0] == 0:
+            return torch.from_numpy(send)
+        h, w, ids, _offsets, _perm = self._route(x)
+        n = h.shape[0]
+        send[:n, :hdim] = h
+        send[:n, hdim:hdim + k] = ids
+        send[:n, hdim + k:] = w
+        self.state = (h,)
+        return torch.from_numpy(send)
+
+    def gathered_ids(self, recv: torch.Tensor) -> torch.Tensor:
+        hdim = recv.shape[1] - 2 * self.cfg.top_k
+        return recv[:, hdim:hdim + self.cfg.top_k].to(torch.int64)
+
+    def experts_gathered(self, recv: torch.Tensor) -> torch.Tensor:
+        k = self.cfg.top_k
+        r = recv.numpy()
+        hdim = r.shape[1] - 2 * k
+        ids = r[:, hdim:hdim + k].astype(np.int64)
+        w = r[:, hdim + k:]
+        partial = np.zeros((r.shape[0], hdim), dtype=np.float32)
+        lo, hi = self.rank * self.e_loc, (self.rank + 1) * self.e_loc
+        for j in range(k):  # slot order, as the device sums
+            for g in np.unique(ids[:, j]):
+                if not lo <= g < hi:
+                    continue
+                sel = ids[:, j] == g
+                y = self._swiglu(r[sel, :hdim], f"mlp.experts.{int(g)}.")
+                partial[sel] += w[sel, j:j + 1] * y
+        return torch.from_numpy(partial)
+
+    def combine_partial(self, x: torch.Tensor, partial: torch.Tensor) -> torch.Tensor:
+        (h,) = self.state
+        if h.shape[0] == 0:
+            return x.clone()
+        acc = partial.numpy()[:h.shape[0]]
+        p = self.cfg.shared_prefix
+        if p + "gate_proj.weight" in self.t:
+            sh = self._swiglu(h, p)
+            if "mlp.shared_expert_gate.weight" in self.t:
+                sh = sh * sigmoid(h @ self.t["mlp.shared_expert_gate.weight"].T)
+            acc = acc + sh
+        return torch.from_numpy(x.numpy() + acc)
+
     def experts(self, rows: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         r, e = rows.numpy(), ids.numpy()
         y = np.zeros_like(r)
@@ -129,7 +187,7 @@ class OracleEPOps:
 
 
 def _worker(rank: int, world: int, port: int, spec: CaseSpec, corrupt: bool, q,  # noqa: ANN001
-            padded_tokens: int = 0) -> None:
+            padded_tokens: int = 0, small_exchange: str = "padded") -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -141,7 +199,7 @@ def _worker(rank: int, world: int, port: int, spec: CaseSpec, corrupt: bool, q, 
         mine = np.array_split(np.arange(spec.tokens), world)[rank]
         xr = x[mine]
         ep = ExpertParallelMoe(OracleEPOps(t, cfg, rank, world, corrupt=corrupt and rank == 0),
-                               padded_tokens=padded_tokens)
+                               padded_tokens=padded_tokens, small_exchange=small_exchange)
         try:
             out = ep.forward(torch.from_numpy(xr)).numpy()
         except ValueError as err:
@@ -163,11 +221,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(spec: CaseSpec, corrupt: bool = False, padded_tokens: int = 0) -> list:
+def _run(spec: CaseSpec, corrupt: bool = False, padded_tokens: int = 0,
+         small_exchange: str = "padded") -> list:
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, spec, corrupt, q, padded_tokens))
+    procs = [ctx.Process(target=_worker,
+                         args=(r, 2, port, spec, corrupt, q, padded_tokens, small_exchange))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -209,6 +269,27 @@ def test_fixed_capacity_exchange_with_an_empty_rank() -> None:
     still serves rank 0's rows for its experts."""
     from dataclasses import replace
     res = _run(replace(SPEC, tokens=1), padded_tokens=4)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    for _rank, _status, err in res:
+        assert err < 1e-5
+
+
+@pytest.mark.parametrize("spec", [SPEC, SPEC_QWEN], ids=["glm", "qwen3"])
+def test_token_replicated_exchange_matches_oracle(spec: CaseSpec) -> None:
+    """Gathered exchange: all-gather of token records (ids and weights in the
+    tails), per-rank partial sums over the resident experts, reduce-scatter sum.
+    The ranks hold 12 and 12 (glm) / 5 and 4 (qwen3) tokens under a cap of 16."""
+    res = _run(spec, padded_tokens=16, small_exchange="gathered")
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    for _rank, _status, err in res:
+        assert err < 1e-5
+
+
+def test_token_replicated_exchange_with_an_empty_rank() -> None:
+    """One token over two ranks: rank 1 sends only unused records, serves rank 0's
+    slots for its experts and gets an empty partial back."""
+    from dataclasses import replace
+    res = _run(replace(SPEC, tokens=1), padded_tokens=4, small_exchange="gathered")
     assert [r[1] for r in res] == ["ok", "ok"], res
     for _rank, _status, err in res:
         assert err < 1e-5
