@@ -70,20 +70,24 @@ struct GemmArgs {
 template <int NT>
 MOE_DEV void epilogue_bar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
-template <int BN>
+// TS: the widened f16 A operand lives in TMEM instead of shared memory (INT8
+// decode tiles, see gemm_ts).
+template <int BN, bool TS = false>
 struct TileCfg {
-  static constexpr int kStageA = kBM * kBK * 2;      // f16 A tile, 16 KiB
+  static constexpr int kStageA = TS ? 0 : kBM * kBK * 2;  // f16 A tile, 16 KiB (none if in TMEM)
   static constexpr int kStageA8 = kBM * kBK;         // int8 staging tile, 8 KiB
   static constexpr int kStageB = BN * kBK * 2;
   // Decode tiles (N <= 64) spread the four K = 16 MMAs of a k-block over four
   // independent TMEM accumulators ("chains"): with a handful of token columns an
   // MMA is short, and MMAs that accumulate into one accumulator wait on each
   // other, so a single chain ran one k-block per ~0.39 us whatever its bytes.  The
-  // epilogue adds the chains in a fixed order.  Wide prefill tiles keep one.
-  static constexpr int kChains = BN <= 64 ? 4 : 1;
+  // epilogue adds the chains in a fixed order.  Wide prefill tiles keep one; a
+  // 64-column tile with its A operand in TMEM keeps two (room for the A slots).
+  static constexpr int kChains = BN <= 32 ? 4 : (BN <= 64 ? (TS ? 2 : 4) : 1);
   static constexpr int kAccCols = kChains * BN;  // one accumulator buffer
-  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
+  static constexpr int kTmemCols = TS ? 512 : (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
                                    : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
+  static constexpr int kAColBase = 2 * kAccCols;  // TS: first column of the A slots
   // Epilogue warps: a 256-column accumulator takes 8 (each TMEM lane quarter
   // twice, splitting the columns) so that draining a tile stays shorter than
   // its MMAs; narrow decode tiles keep 4.
@@ -97,14 +101,31 @@ __host__ __device__ constexpr int gemm_threads() {
   return 32 * (2 + TileCfg<BN>::kEpiWarps + (INT8 ? 4 : 0));
 }
 
+// INT8 decode tiles (N <= 64) widen the int8 weight tile into TMEM (tcgen05.st by
+// the converter warps) and the MMA reads its A operand from there: no f16 copy of
+// A in shared memory, so a stage is only the int8 tile and the token tile and
+// more k-blocks of weights fit in flight per SM; the hand-off to the MMA is a
+// TMEM store and a barrier.  Prefill tiles keep A in shared memory (a 256-column
+// accumulator pair fills TMEM).
+#ifndef MOE_INT8_TMEM_A
+#define MOE_INT8_TMEM_A 1
+#endif
+template <int BN, bool INT8>
+__host__ __device__ constexpr bool gemm_ts() { return MOE_INT8_TMEM_A && INT8 && BN <= 64; }
+
 // As many stages as fit under the 227 KiB opt-in shared memory per CTA (less the
-// alignment slack, barriers and a little static shared memory), up to 8: the
-// prefill GEMMs are bound by the bytes in flight between L2 and the SM (Little's
-// law over the ring), so a fourth INT8 stage at BN = 256 pays directly.
-constexpr int kGemmSmemBudget = 232448 - 1024 - 256 - 512;
+// alignment slack, barriers and a little static shared memory), up to 8 (12 with
+// the A operand in TMEM): the prefill GEMMs are bound by the bytes in flight
+// between L2 and the SM (Little's law over the ring), so a fourth INT8 stage at
+// BN = 256 pays directly.
+constexpr int kGemmBarBytes = 1024;
+constexpr int kGemmSmemBudget = 232448 - 1024 - kGemmBarBytes - 512;
 
 #ifndef MOE_GEMM_MAX_STAGES
 #define MOE_GEMM_MAX_STAGES 8
+#endif
+#ifndef MOE_GEMM_MAX_STAGES_TS
+#define MOE_GEMM_MAX_STAGES_TS 12
 #endif
 
 // k-blocks per pipeline stage.  INT8 decode tiles (N <= 64) widen two 64-column
@@ -118,27 +139,46 @@ constexpr int kGemmSmemBudget = 232448 - 1024 - 256 - 512;
 #ifndef MOE_INT8_DECODE_KPS
 #define MOE_INT8_DECODE_KPS 2
 #endif
+// With the widened A operand in TMEM (gemm_ts) the per-stage cost dominates still
+// more: four k-blocks per stage measured 22 % faster than two at 32 tokens (one:
+// 20 % slower), whatever the number of TMEM A slots (2 to 14) or accumulator
+// chains; a second group of converter warps, and a separate ring for the token
+// tiles (so that int8 stages return to the producer once converted) gained nothing.
+#ifndef MOE_INT8_DECODE_KPS_TS
+#define MOE_INT8_DECODE_KPS_TS 4
+#endif
 
 template <int BN, bool INT8>
-__host__ __device__ constexpr int gemm_kps() { return (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1; }
+__host__ __device__ constexpr int gemm_kps() {
+  return gemm_ts<BN, INT8>() ? MOE_INT8_DECODE_KPS_TS : (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1;
+}
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr int gemm_stage_bytes() {
-  return gemm_kps<BN, INT8>() *
-         (TileCfg<BN>::kStageA + TileCfg<BN>::kStageB + (INT8 ? TileCfg<BN>::kStageA8 : 0));
+  using C = TileCfg<BN, gemm_ts<BN, INT8>()>;
+  return gemm_kps<BN, INT8>() * (C::kStageA + C::kStageB + (INT8 ? C::kStageA8 : 0));
 }
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr int gemm_stages() {
   constexpr int s = kGemmSmemBudget / gemm_stage_bytes<BN, INT8>();
-  return s > MOE_GEMM_MAX_STAGES ? MOE_GEMM_MAX_STAGES : s;
+  constexpr int cap = gemm_ts<BN, INT8>() ? MOE_GEMM_MAX_STAGES_TS : MOE_GEMM_MAX_STAGES;
+  return s > cap ? cap : s;
+}
+
+// TMEM A slots (KPS k-blocks of 32 columns each) in the columns the two
+// accumulator buffers leave free.
+template <int BN, bool INT8>
+__host__ __device__ constexpr int gemm_a_slots() {
+  using C = TileCfg<BN, gemm_ts<BN, INT8>()>;
+  return gemm_ts<BN, INT8>() ? (C::kTmemCols - C::kAColBase) / (32 * gemm_kps<BN, INT8>()) : 0;
 }
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
   return 1024 /*align slack*/ +
          static_cast<size_t>(gemm_stages<BN, INT8>()) * gemm_stage_bytes<BN, INT8>() +
-         256 /*barriers*/;
+         kGemmBarBytes;
 }
 
 // Widen one 128 x 64 int8 tile (as stored: 64-byte rows, 16-byte chunk v of row
@@ -173,6 +213,34 @@ MOE_DEV void convert_row_i8_f16(const int8_t* src_row, uint8_t* dst_tile, int r)
       const int chunk = 2 * v + h;
       uint4* dst = reinterpret_cast<uint4*>(dst_tile + r * 128 + ((chunk ^ (r & 7)) << 4));
       *dst = make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+    }
+  }
+}
+
+// The same widening into registers for a TMEM A operand, in two steps so that a
+// stage's shared-memory reads are all in flight before the first conversion:
+// load_row_i8 fetches row r's 64 int8 in k order, widen_i8 turns them into the 32
+// columns of one k-block (out[c] holds k = 2c in its lower half and 2c + 1).
+MOE_DEV void load_row_i8(const int8_t* src_row, int r, uint4 (&q)[4]) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src_row);
+  const int rot = (r >> 1) & 3;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) q[v] = s4[v ^ rot];
+}
+MOE_DEV void widen_i8(const uint4 (&q)[4], uint32_t (&out)[32]) {
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const uint32_t words[4] = {q[v].x, q[v].y, q[v].z, q[v].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u = words[i] ^ 0x80808080u;
+      uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140);
+      uint32_t hi = __byte_perm(u, 0x64646464u, 0x4342);
+      __half2 l2 = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);
+      __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+      out[8 * v + 2 * i] = *reinterpret_cast<uint32_t*>(&l2);
+      out[8 * v + 2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
     }
   }
 }
@@ -235,11 +303,17 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   constexpr bool DOWN = MODE == MODE_DOWN;
   constexpr int STAGES = gemm_stages<BN, INT8>();
   constexpr int KPS = gemm_kps<BN, INT8>();  // k-blocks per stage
+  constexpr bool TS = gemm_ts<BN, INT8>();   // widened A operand in TMEM
+  using Cfg = TileCfg<BN, TS>;
+  constexpr int NA = gemm_a_slots<BN, INT8>();  // TMEM A slots (TS)
+  constexpr int NCONV = TS ? NA : STAGES;       // "widened" barriers: per A slot or per stage
   // per k-block operand bytes; stage s holds k-blocks [s * KPS, s * KPS + KPS) of each buffer
-  constexpr int SA = TileCfg<BN>::kStageA, SB = TileCfg<BN>::kStageB, SA8 = TileCfg<BN>::kStageA8;
+  constexpr int SA = Cfg::kStageA, SB = Cfg::kStageB, SA8 = Cfg::kStageA8;
   // The MMA runs with N = nvalid rounded up to 16: a partial tile does not pay
   // tensor time for the token columns it does not use.
-  constexpr uint32_t TMEM_COLS = TileCfg<BN>::kTmemCols;
+  constexpr uint32_t TMEM_COLS = Cfg::kTmemCols;
+  static_assert(!TS || NA >= 2, "TMEM A ring needs two slots");
+  static_assert((2 * STAGES + NCONV + NA + 5) * 8 + 8 <= kGemmBarBytes, "barrier area");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -249,13 +323,14 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + (INT8 ? STAGES * KPS * SA8 : 0));
   uint64_t* full = bars;                 // TMA landed (A + B)
   uint64_t* empty = full + STAGES;       // MMA finished reading the stage
-  uint64_t* conv = empty + STAGES;       // int8 tile widened to f16
-  uint64_t* tfull = conv + STAGES;       // accumulator ready
+  uint64_t* conv = empty + STAGES;       // int8 tile widened to f16 (per stage / A slot)
+  uint64_t* aempty = conv + NCONV;       // TS: MMA finished reading an A slot
+  uint64_t* tfull = aempty + NA;         // accumulator ready
   uint64_t* tempty = tfull + 2;          // accumulator drained
   uint64_t* mma_done = tempty + 2;       // final drain of in-flight MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  constexpr int EPI = TileCfg<BN>::kEpiWarps;
+  constexpr int EPI = Cfg::kEpiWarps;
   __shared__ int s_ready[2][EPI];  // epilogue warps' per-tile readiness votes
   __shared__ volatile int s_last; // split-K: this CTA finishes the tile
 
@@ -285,8 +360,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 4);  // one arrival per converter warp
     }
+    for (int c = 0; c < NCONV; ++c) mbar_init(&conv[c], 4);  // one arrival per converter warp
+    for (int a = 0; a < NA; ++a) mbar_init(&aempty[a], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 32 * EPI);
@@ -382,15 +458,17 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
           break;
         }
         tc_fence_after();
-        constexpr int CH = TileCfg<BN>::kChains;
-        const uint32_t d = tmem_base + buf * TileCfg<BN>::kAccCols;
+        constexpr int CH = Cfg::kChains;
+        const uint32_t d = tmem_base + buf * Cfg::kAccCols;
         const uint32_t idesc = idesc_f16_f32(kBM, (t.nvalid + 15) & ~15);
         bool ok = true;
         for (int kb = t.kb0; kb < t.kb1; kb += KPS, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           const int n = min(KPS, t.kb1 - kb);
-          if (!mbar_wait_bounded(INT8 ? &conv[s] : &full[s], ph, abort_flag)) {
+          const int ca = TS ? it % (NA > 0 ? NA : 1) : s;  // widened barrier / A slot
+          const uint32_t cph = TS ? (it / (NA > 0 ? NA : 1)) & 1 : ph;
+          if (!mbar_wait_bounded(INT8 ? &conv[ca] : &full[s], cph, abort_flag)) {
             *abort_flag = 1;
             record_error(args.err, DEV_TIMEOUT_FULL);
             ok = false;
@@ -398,15 +476,25 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
           }
           tc_fence_after();
           for (int j = 0; j < n; ++j) {
-            const uint32_t a0 = smem_u32(sA + (s * KPS + j) * SA), b0 = smem_u32(sB + (s * KPS + j) * SB);
+            const uint32_t b0 = smem_u32(sB + (s * KPS + j) * SB);
+            if constexpr (TS) {
+              const uint32_t a0 = tmem_base + Cfg::kAColBase + (ca * KPS + j) * 32;
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-              // MMA k feeds chain k % CH; a chain's first MMA of the tile starts it
-              tc_mma_f16(d + (k % CH) * BN, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
-                         (kb + j > t.kb0 || k >= CH) ? 1u : 0u);
+              for (int k = 0; k < kBK / 16; ++k)
+                tc_mma_f16_ts(d + (k % CH) * BN, a0 + k * 8, sw128_desc(b0 + k * 32), idesc,
+                              (kb + j > t.kb0 || k >= CH) ? 1u : 0u);
+            } else {
+              const uint32_t a0 = smem_u32(sA + (s * KPS + j) * SA);
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k) {
+                // MMA k feeds chain k % CH; a chain's first MMA of the tile starts it
+                tc_mma_f16(d + (k % CH) * BN, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
+                           (kb + j > t.kb0 || k >= CH) ? 1u : 0u);
+              }
             }
           }
           tc_commit(&empty[s]);
+          if constexpr (TS) tc_commit(&aempty[ca]);
           issued = true;
         }
         if (!ok) break;
@@ -455,9 +543,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
         rs = sh ? args.scale_shared[mrow]
                 : args.scale_routed[static_cast<size_t>(t.group) * args.rows_a_routed + mrow];
       }
-      constexpr int CH = TileCfg<BN>::kChains;
+      constexpr int CH = Cfg::kChains;
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * TileCfg<BN>::kAccCols;
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kAccCols;
       const int ncol = (t.nvalid + 15) & ~15;
       for (int c0 = cfirst; c0 < ncol; c0 += cstep) {
         float v[16];
@@ -577,7 +665,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     if (__any_sync(0xffffffffu, range_bad) && lane == 0) record_error(args.err, DEV_RANGE);
   } else if constexpr (INT8) {
     // ------------------------------------------------------------ int8 -> f16
-    const int r = (warp - 2 - EPI) * 32 + lane;  // one A row per thread
+    // one A row per thread; with A in TMEM a warp may only write its own quarter
+    // of the TMEM lanes (warp % 4), so its rows follow that quarter
+    const int r = TS ? (warp & 3) * 32 + lane : (warp - 2 - EPI) * 32 + lane;
     int it = 0;
     for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
       const Tile t = fetch_tile(ti);
@@ -587,6 +677,37 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const int n = min(KPS, t.kb1 - kb);
+        if constexpr (TS) {
+          const int a = it % NA;
+          // the A slot must be free (the MMAs of its previous use completed) and
+          // the int8 tile in place
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(&aempty[a], ((it / NA) & 1) ^ 1, abort_flag)) ||
+              !__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, abort_flag))) {
+            *abort_flag = 1;
+            record_error(args.err, DEV_TIMEOUT_CONV);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ta = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) +
+                              Cfg::kAColBase + a * KPS * 32;
+          uint4 q[KPS][4];
+#pragma unroll
+          for (int j = 0; j < KPS; ++j)
+            if (j < n) load_row_i8(reinterpret_cast<const int8_t*>(sA8 + (s * KPS + j) * SA8 + r * kBK), r, q[j]);
+#pragma unroll
+          for (int j = 0; j < KPS; ++j)
+            if (j < n) {
+              uint32_t w[32];
+              widen_i8(q[j], w);
+              tmem_st32_nowait(ta + j * 32, w);
+            }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[a]);
+          continue;
+        }
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, abort_flag))) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_CONV);
