@@ -158,7 +158,11 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
 WsLayout ws_layout(const Plan& p, int T) {
   if (p.E == 0)  // dense MLP: normalised rows and the shared-expert GEMMs only
     return ws_layout_general(p, T, 0, 0, T, pick_bn(T), false);
-  return ws_layout_general(p, T, p.K, p.E, p.SI > 0 ? T : 0, pick_bn(T), true);
+  // INT8 decode batches keep token tiles of at most 64 columns, so that their
+  // GEMMs take the TMEM-A path (gemm_ts): an expert sees ~T*K/E tokens, far fewer
+  // than T, and the wider tiles' shared-memory A path ran ~25 % slower at T = 128.
+  const int bn = (p.int8 && route_uses_tail(p, T)) ? std::min(pick_bn(T), 64) : pick_bn(T);
+  return ws_layout_general(p, T, p.K, p.E, p.SI > 0 ? T : 0, bn, true);
 }
 
 // Expert side of the expert-parallel path: R received rows grouped by the
