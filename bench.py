@@ -503,11 +503,13 @@ def _exchange_name(kind: str) -> str:
     return {"padded": "fixed-capacity (one all-to-all of equal row blocks each way, no host sync)",
             "gathered": "token-replicated (all-gather of token records, reduce-scatter of fp32 "
                         "partial sums; no host sync)",
+            "p2p": "token-replicated over peer memory (records and fp32 partial sums stored over "
+                   "NVLink by the producing kernels, epoch flags, no NCCL)",
             "exact": "exact (counts, then rows and ids; one host sync)"}[kind]
 
 
 def _exchange_dtype(kind: str) -> str:
-    return ("f16 token rows and fp32 partial sums exchanged" if kind == "gathered"
+    return ("f16 token rows and fp32 partial sums exchanged" if kind in ("gathered", "p2p")
             else "f16 rows exchanged")
 
 
@@ -522,8 +524,8 @@ def _ep_launches(kind: str) -> int:
     """Kernels of one expert-parallel decode forward: routing (router, tail) and the
     send rows (dispatch, + send metadata on the exact exchange); hist, scan,
     scatter, gather, two GEMMs (experts; + the partial sums on the gathered
-    exchange); scan, two GEMMs (shared); combine."""
-    return {"padded": 13, "gathered": 14, "exact": 14}[kind]
+    exchange; + two flag waits on the peer-memory one); scan, two GEMMs (shared); combine."""
+    return {"padded": 13, "gathered": 14, "exact": 14, "p2p": 16}[kind]
 
 
 # ------------------------------------------------------------------ 89-layer stack (N > 1)
@@ -913,7 +915,7 @@ def main() -> None:
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
-    ap.add_argument("--ep-exchange", choices=["padded", "gathered", "exact"], default="gathered",
+    ap.add_argument("--ep-exchange", choices=["padded", "gathered", "p2p", "exact"], default="gathered",
                     help="N > 1 decode batches: fixed-capacity all-to-all, token-replicated "
                          "all-gather/reduce-scatter, or exact all-to-all")
     ap.add_argument("--stack", action="store_true",

@@ -737,7 +737,7 @@ int moe_status(MoePlan* plan, void* stream) {
   MOE_CUDA(cudaMemsetAsync(p.d_err, 0, sizeof(int), s));
   MOE_CUDA(cudaStreamSynchronize(s));
   if (h == DEV_OK) return MOE_OK;
-  if (h >= DEV_TIMEOUT_FULL && h <= DEV_TIMEOUT_CONV)
+  if ((h >= DEV_TIMEOUT_FULL && h <= DEV_TIMEOUT_CONV) || h == DEV_TIMEOUT_PEER)
     return fail(MOE_ERR_TIMEOUT, "a device-side wait ran out of time (code " + std::to_string(h) + ")");
   if (h == DEV_RANGE)
     return fail(MOE_ERR_RANGE, "an activation or expert output overflowed f16 (|v| > 65504)");
@@ -970,6 +970,119 @@ int moe_ep_combine_partial(MoePlan* plan, const float* x_dev, int32_t T, const f
   return MOE_OK;
 }
 
+// ------------------------------------------------------------ exchange over peer memory
+static int p2p_peers(const MoePlan* plan, int32_t rank, int32_t world, void* const* recv,
+                     float* const* part, int32_t* const* flags, P2PPeers* out) {
+  if (world < 1 || world > kMaxP2PRanks || rank < 0 || rank >= world)
+    return fail(MOE_ERR_INVALID, "rank / world outside [0, 8)");
+  if (plan->p.E / std::max(plan->p.n_local, 1) != world)
+    return fail(MOE_ERR_INVALID, "world does not match the plan's expert share");
+  if (plan->p.e_begin != rank * plan->p.n_local)
+    return fail(MOE_ERR_INVALID, "rank does not match the plan's expert range");
+  *out = P2PPeers{};
+  for (int d = 0; d < world; ++d) {
+    if ((recv && !recv[d]) || (part && !part[d]) || !flags || !flags[d])
+      return fail(MOE_ERR_INVALID, "null peer buffer");
+    if (recv) out->recv[d] = recv[d];
+    if (part) out->part[d] = part[d];
+    out->flags[d] = flags[d];
+  }
+  return MOE_OK;
+}
+
+int moe_ep_p2p_pack(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap, int32_t rank,
+                    int32_t world, void* const* peer_recv, int32_t* const* peer_flags, int32_t epoch,
+                    int32_t* done, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (T > p.cfg.max_tokens) return fail(MOE_ERR_INVALID, "T above max_tokens");
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK) return rc;
+  if (cap <= 0 || cap < T) return fail(MOE_ERR_INVALID, "cap must be positive and at least T");
+  if (epoch <= 0) return fail(MOE_ERR_INVALID, "epoch must be positive");
+  if (!done || !peer_recv || (T > 0 && !x_dev)) return fail(MOE_ERR_INVALID, "null argument");
+  P2PPeers peers;
+  rc = p2p_peers(plan, rank, world, peer_recv, nullptr, peer_flags, &peers);
+  if (rc != MOE_OK) return rc;
+  for (int d = 0; d < world; ++d)
+    if (misaligned16(peer_recv[d])) return fail(MOE_ERR_INVALID, "receive buffers must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  WsLayout L{};
+  if (T > 0) {
+    L = ws_layout(p, T);
+    MOE_CUDA(launch_route(p, L, ws, x_dev, T, false, s, nullptr));
+  }
+  MOE_CUDA(launch_p2p_pack(p, L, ws, x_dev, T, cap, rank, world, peers, epoch, done, s));
+  return MOE_OK;
+}
+
+int moe_ep_p2p_wait(MoePlan* plan, const int32_t* flags, int32_t world, int32_t epoch,
+                    int64_t limit_cycles, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  if (!flags || world < 1 || world > kMaxP2PRanks || epoch <= 0)
+    return fail(MOE_ERR_INVALID, "bad flags / world / epoch");
+  if (limit_cycles <= 0 || limit_cycles > kWaitLimitCycles)
+    return fail(MOE_ERR_INVALID, "limit_cycles must be in (0, 2e9]");
+  MOE_CUDA(launch_p2p_wait(flags, world, epoch, limit_cycles, plan->p.d_err,
+                           static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+
+int moe_ep_p2p_experts(MoePlan* plan, const void* recv_rows, int32_t cap, int32_t rank,
+                       int32_t world, float* const* peer_part, int32_t* const* peer_flags,
+                       int32_t epoch, int32_t* done, void* workspace, uint64_t workspace_bytes,
+                       void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  if (cap <= 0 || static_cast<int64_t>(cap) * world * p.K > INT32_MAX)
+    return fail(MOE_ERR_INVALID, "bad cap");
+  const int rows = cap * world;
+  int rc = check_ep(plan, rows, workspace, workspace_bytes, ws_layout_ep_gathered(p, rows).total);
+  if (rc != MOE_OK) return rc;
+  if (!recv_rows || !done || !peer_part || epoch <= 0) return fail(MOE_ERR_INVALID, "null argument");
+  if (misaligned16(recv_rows)) return fail(MOE_ERR_INVALID, "recv_rows must be 16-byte aligned");
+  P2PPeers peers;
+  rc = p2p_peers(plan, rank, world, nullptr, peer_part, peer_flags, &peers);
+  if (rc != MOE_OK) return rc;
+  for (int d = 0; d < world; ++d)
+    if (misaligned16(peer_part[d])) return fail(MOE_ERR_INVALID, "partial buffers must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout_ep_gathered(p, rows);
+  char* ws = static_cast<char*>(workspace);
+  const __half* rec = static_cast<const __half*>(recv_rows);
+  const int ld = ep_token_row_halves(p);
+  const RowKeys keys{reinterpret_cast<const int32_t*>(rec + p.H), ld / 2, p.K, p.e_begin, 2};
+  MOE_CUDA(launch_group_rows(p, L, ws, keys, rec, ld, rows, s));
+  const int slots = rows * p.K;
+  __half* y = reinterpret_cast<__half*>(ws + L.y);
+  MOE_CUDA(launch_gemm(p, L, ws, false, GemmIO{slots, 0, nullptr, nullptr, p.n_local}, s));
+  MOE_CUDA(launch_gemm(p, L, ws, true, GemmIO{slots, 0, y, nullptr, p.n_local}, s));
+  MOE_CUDA(launch_p2p_partial(p, rec, cap, y, reinterpret_cast<const int32_t*>(ws + L.slot_row), rank,
+                              world, peers, epoch, done, s));
+  return MOE_OK;
+}
+
+int moe_ep_p2p_combine(MoePlan* plan, const float* x_dev, int32_t T, const float* part,
+                       int32_t cap, int32_t world, float* out_dev, void* workspace,
+                       uint64_t workspace_bytes, void* stream) {
+  if (!plan) return fail(MOE_ERR_INVALID, "null plan");
+  Plan& p = plan->p;
+  int rc = check_ep(plan, T, workspace, workspace_bytes, T > 0 ? ws_layout(p, T).total : 0);
+  if (rc != MOE_OK || T == 0) return rc;
+  if (!x_dev || !part || !out_dev) return fail(MOE_ERR_INVALID, "null argument");
+  if (cap < T || world < 1 || world > kMaxP2PRanks) return fail(MOE_ERR_INVALID, "bad cap / world");
+  if (x_dev == out_dev) return fail(MOE_ERR_INVALID, "x and out may not alias");
+  if (misaligned16(x_dev) || misaligned16(part) || misaligned16(out_dev))
+    return fail(MOE_ERR_INVALID, "x, part and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WsLayout L = ws_layout(p, T);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA(launch_p2p_combine(p, x_dev, part, cap, world, reinterpret_cast<float*>(ws + L.y_s),
+                              reinterpret_cast<float*>(ws + L.sgate), out_dev, T, s));
+  return MOE_OK;
+}
+
 int moe_ep_shared(MoePlan* plan, int32_t T, void* workspace, uint64_t workspace_bytes,
                   void* stream) {
   if (!plan) return fail(MOE_ERR_INVALID, "null plan");
@@ -1027,6 +1140,30 @@ int moe_rt_malloc(uint64_t nbytes, void** dev_ptr) {
   MOE_CUDA(cudaMalloc(dev_ptr, nbytes));
   return MOE_OK;
 }
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes in the C ABI");
+
+int moe_rt_ipc_get_handle(const void* dev_ptr, void* handle) {
+  if (!dev_ptr || !handle) return fail(MOE_ERR_INVALID, "null argument");
+  cudaIpcMemHandle_t h;
+  MOE_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  std::memcpy(handle, &h, sizeof(h));
+  return MOE_OK;
+}
+
+int moe_rt_ipc_open_handle(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(MOE_ERR_INVALID, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  MOE_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MOE_OK;
+}
+
+int moe_rt_ipc_close_handle(void* dev_ptr) {
+  if (!dev_ptr) return fail(MOE_ERR_INVALID, "null argument");
+  MOE_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return MOE_OK;
+}
+
 int moe_rt_free(void* dev_ptr) {
   MOE_CUDA(cudaFree(dev_ptr));
   return MOE_OK;

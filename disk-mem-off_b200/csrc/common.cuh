@@ -27,6 +27,7 @@ enum DevErr : int {
   DEV_BAD_ROUTE = 7,         // router produced an expert id out of range
   DEV_RANGE = 8,             // an activation does not fit an f16 operand or output
   DEV_TILE_OVERFLOW = 9,     // a tile list needs more entries than the workspace holds
+  DEV_TIMEOUT_PEER = 10,     // a peer GPU's epoch flag did not arrive in time
 };
 
 // f16 conversion of v stays finite (|v| rounds to at most 65504); false for NaN too.

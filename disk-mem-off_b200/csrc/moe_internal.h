@@ -215,6 +215,25 @@ cudaError_t launch_ep_token_pack(const Plan& p, const WsLayout& L, char* ws, con
 // of w_k * y[slot_row[t*K + k]] (fp32, slot order), zero for a token without one.
 cudaError_t launch_ep_partial(const Plan& p, const __half* rows, int n, const __half* y,
                               const int32_t* slot_row, float* partial, cudaStream_t s);
+// Token-replicated exchange over peer memory (p2p.cu): every rank's buffers as
+// mapped in this process, rank d at index d (d == rank: this rank's own).
+constexpr int kMaxP2PRanks = 8;
+struct P2PPeers {
+  void* recv[kMaxP2PRanks];   // [world*cap][ep_token_row_halves] f16 token records
+  float* part[kMaxP2PRanks];  // [world][cap][H] fp32 partial sums
+  int* flags[kMaxP2PRanks];   // [2][world] int32 epochs: records, partials
+};
+cudaError_t launch_p2p_pack(const Plan& p, const WsLayout& L, char* ws, const float* x, int T,
+                            int cap, int rank, int world, const P2PPeers& peers, int epoch,
+                            int* done, cudaStream_t s);
+cudaError_t launch_p2p_wait(const int* flags, int world, int epoch, long long limit, int* err,
+                            cudaStream_t s);
+cudaError_t launch_p2p_partial(const Plan& p, const __half* rows, int cap, const __half* y,
+                               const int32_t* slot_row, int rank, int world, const P2PPeers& peers,
+                               int epoch, int* done, cudaStream_t s);
+cudaError_t launch_p2p_combine(const Plan& p, const float* x, const float* part, int cap, int world,
+                               const float* y_s, const float* sgate, float* out, int T,
+                               cudaStream_t s);
 // out = x + (partial + shared expert), the combine of the token-replicated exchange.
 cudaError_t launch_combine_partial(const Plan& p, const float* x, const float* partial,
                                    const float* y_s, const float* sgate, float* out, int T,

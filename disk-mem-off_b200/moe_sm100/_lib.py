@@ -107,6 +107,13 @@ _PROTOTYPES: dict[str, tuple] = {
                                           c_uint64, c_void_p]),
     "moe_ep_combine_partial": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
                                          c_void_p, c_uint64, c_void_p]),
+    "moe_ep_p2p_pack": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                                  c_void_p, c_int32, c_void_p, c_void_p, c_uint64, c_void_p]),
+    "moe_ep_p2p_wait": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p]),
+    "moe_ep_p2p_experts": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
+                                     c_void_p, c_int32, c_void_p, c_void_p, c_uint64, c_void_p]),
+    "moe_ep_p2p_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32,
+                                     c_void_p, c_void_p, c_uint64, c_void_p]),
     "moe_status": (c_int32, [c_void_p, c_void_p]),
     "moe_attn_create": (c_int32, [POINTER(MoeAttnConfigC), POINTER(c_void_p)]),
     "moe_attn_destroy": (c_int32, [c_void_p]),
@@ -125,6 +132,9 @@ _PROTOTYPES: dict[str, tuple] = {
     "moe_rt_can_access_peer": (c_int32, [c_int32, c_int32, POINTER(c_int32)]),
     "moe_rt_malloc": (c_int32, [c_uint64, POINTER(c_void_p)]),
     "moe_rt_free": (c_int32, [c_void_p]),
+    "moe_rt_ipc_get_handle": (c_int32, [c_void_p, c_void_p]),
+    "moe_rt_ipc_open_handle": (c_int32, [c_void_p, c_void_p]),
+    "moe_rt_ipc_close_handle": (c_int32, [c_void_p]),
     "moe_rt_malloc_host": (c_int32, [c_uint64, POINTER(c_void_p)]),
     "moe_rt_free_host": (c_int32, [c_void_p]),
     "moe_rt_stream_create": (c_int32, [POINTER(c_void_p)]),

@@ -11,7 +11,7 @@ import sys
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(os.path.dirname(_HERE), "csrc")
-SOURCES = ["api.cu", "router.cu", "gemm_tc.cu", "combine.cu", "pack.cu", "attn.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "router.cu", "gemm_tc.cu", "combine.cu", "pack.cu", "attn.cu", "noalloc.cu", "p2p.cu"]
 OUT = os.path.join(_HERE, "libmoe_sm100.so")
 
 

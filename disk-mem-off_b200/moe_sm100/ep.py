@@ -30,8 +30,15 @@ tokens.  The host never waits either, and the bytes per rank are world * cap
 records in and world * cap fp32 rows out, independent of top_k, where the padded
 exchange moves world * cap * min(top_k, experts per rank) rows each way.
 
-The exchanges are torch.distributed collectives (NCCL over NVLink on B200; gloo
-on CPU in the tests).  The device work is libmoe_sm100's moe_ep_* entry points.
+Or the same token-replicated exchange over peer memory (``small_exchange="p2p"``):
+no collective library at all.  The packing kernel stores each rank's records
+straight into every rank's receive buffer over NVLink, the partial-sum kernel
+stores each record's partial sum straight into its owner's buffer, each publishing
+an epoch flag when its stores are complete, and a bounded wait kernel on each rank
+stands in for each collective (buffers mapped once with CUDA IPC, ``p2p.py``).
+
+The collectives are torch.distributed (NCCL over NVLink on B200; gloo on CPU in
+the tests).  The device work is libmoe_sm100's moe_ep_* entry points.
 """
 from __future__ import annotations
 
@@ -83,8 +90,8 @@ class ExpertParallelMoe:
 
     def __init__(self, ops: EPOps, group: Any = None, padded_tokens: int = 0,
                  small_exchange: str = "padded") -> None:
-        if small_exchange not in ("padded", "gathered"):
-            raise ValueError("small_exchange must be 'padded' or 'gathered'")
+        if small_exchange not in ("padded", "gathered", "p2p"):
+            raise ValueError("small_exchange must be 'padded', 'gathered' or 'p2p'")
         self.ops = ops
         self.group = group
         self.last_timing: dict[str, float] = {}
@@ -92,10 +99,12 @@ class ExpertParallelMoe:
         self.small_exchange = small_exchange
         self.cap = 0
         if self.padded_tokens > 0:
-            self.cap = (self.padded_tokens if small_exchange == "gathered"
-                        else int(ops.capacity(self.padded_tokens)))
+            self.cap = (int(ops.capacity(self.padded_tokens)) if small_exchange == "padded"
+                        else self.padded_tokens)
             if self.cap <= 0:
                 raise ValueError("no fixed capacity for padded_tokens")
+            if small_exchange == "p2p":
+                ops.p2p_setup(self.cap, group)
 
     def forward(self, x: Any, timed: bool = False) -> Any:
         torch = _torch()
@@ -110,6 +119,8 @@ class ExpertParallelMoe:
         if 0 < self.padded_tokens and x.shape[0] <= self.padded_tokens:
             if self.small_exchange == "gathered":
                 out, n_recv = self._forward_gathered(x, mark)
+            elif self.small_exchange == "p2p":
+                out, n_recv = self._forward_p2p(x, mark)
             else:
                 out, n_recv = self._forward_padded(x, mark)
         else:
@@ -187,6 +198,35 @@ class ExpertParallelMoe:
             return {"recv_rows": int(mine.numel()),
                     "recv_experts": int(torch.unique(mine).numel()) if mine.numel() else 0,
                     "exchanged_rows": int(recv.shape[0])}
+        return out, counts
+
+    def _forward_p2p(self, x: Any, mark: Any) -> tuple[Any, Any]:
+        torch = _torch()
+        cap = self.cap
+        mark("start")
+        self.ops.p2p_pack(x, cap)
+        mark("dispatched")
+        start_shared = getattr(self.ops, "start_shared", None)
+        if start_shared is not None:
+            start_shared(x)
+        self.ops.p2p_wait(0)
+        mark("exchanged")
+        self.ops.p2p_experts()
+        mark("computed")
+        self.ops.p2p_wait(1)
+        mark("returned")
+        out = self.ops.p2p_combine(x)
+        mark("end")
+
+        def counts() -> dict[str, float]:
+            ids = self.ops.p2p_ids()
+            valid = ids[ids >= 0]
+            e_loc = self.ops.experts_per_rank
+            r = self.ops.rank
+            mine = valid[(valid >= r * e_loc) & (valid < (r + 1) * e_loc)]
+            return {"recv_rows": int(mine.numel()),
+                    "recv_experts": int(torch.unique(mine).numel()) if mine.numel() else 0,
+                    "exchanged_rows": int(ids.shape[0])}
         return out, counts
 
     def _forward_exact(self, x: Any, mark: Any) -> tuple[Any, Any]:
@@ -426,8 +466,86 @@ class DeviceEPOps:
                                    c_void_p(out.data_ptr()), c_void_p(ws.data_ptr()), ws.numel(), s))
         return out
 
+    # ---------------------------------------------------------------- peer memory
+    @property
+    def rank(self) -> int:
+        return self.cfg.expert_begin // self.experts_per_rank
+
+    def p2p_setup(self, cap: int, group: Any = None) -> None:
+        """Buffers of the peer-memory exchange for batches of at most `cap` tokens
+        (a collective on first use per pool; layers sharing the pool share them)."""
+        from .p2p import PeerExchange
+        st = self._pool.get("p2p")
+        if st is None or st.cap != cap:
+            if st is not None:
+                raise ValueError("layers sharing a pool must use one peer-exchange capacity")
+            st = PeerExchange(self.rank, self.world, cap, self.cfg.hidden,
+                              int(lib().moe_ep_token_row_halves(self.layer._plan)),
+                              self.cfg.device, group)
+            self._pool["p2p"] = st
+        st.users += 1
+        self._p2p = st
+        self._p2p_group = group
+
+    def p2p_pack(self, x: Any, cap: int) -> None:
+        """Route the local tokens and store their records into every rank's buffer."""
+        st = self._p2p
+        st.epoch += 1
+        t = x.shape[0]
+        plan = self.layer._plan
+        ws = self._buf("ws", int(lib().moe_workspace_bytes(plan, max(t, 1))))
+        check(lib().moe_ep_p2p_pack(plan, c_void_p(x.data_ptr()), t, cap, self.rank, self.world,
+                                    st.recv_arr, st.flags_arr, st.epoch, c_void_p(st.done_ptr),
+                                    c_void_p(ws.data_ptr()), ws.numel(),
+                                    c_void_p(_stream_handle(None))))
+        self._T = t
+
+    def p2p_wait(self, which: int) -> None:
+        """Wait (bounded, on the device) until every rank's records (0) or partial
+        sums (1) of this forward have arrived."""
+        from .p2p import WAIT_LIMIT_CYCLES
+        st = self._p2p
+        check(lib().moe_ep_p2p_wait(self.layer._plan, c_void_p(st.flags_row(which)), self.world,
+                                    st.epoch, WAIT_LIMIT_CYCLES, c_void_p(_stream_handle(None))))
+
+    def p2p_experts(self) -> None:
+        """Resident experts on every received record; partial sums to their owners."""
+        st = self._p2p
+        plan = self.layer._plan
+        ws = self._buf("ws_ep", int(lib().moe_ep_gathered_workspace_bytes(plan, self.world * st.cap)))
+        check(lib().moe_ep_p2p_experts(plan, c_void_p(st.recv), st.cap, self.rank, self.world,
+                                       st.part_arr, st.flags_arr, st.epoch,
+                                       c_void_p(st.done_ptr + 4), c_void_p(ws.data_ptr()),
+                                       ws.numel(), c_void_p(_stream_handle(None))))
+
+    def p2p_combine(self, x: Any) -> Any:
+        torch = _torch()
+        out = torch.empty_like(x)
+        t = x.shape[0]
+        if t == 0:
+            return out
+        st = self._p2p
+        plan = self.layer._plan
+        ws = self._ws
+        s = c_void_p(_stream_handle(None))
+        self._join_shared(x, plan, ws, s)
+        check(lib().moe_ep_p2p_combine(plan, c_void_p(x.data_ptr()), t, c_void_p(st.part), st.cap,
+                                       self.world, c_void_p(out.data_ptr()), c_void_p(ws.data_ptr()),
+                                       ws.numel(), s))
+        return out
+
+    def p2p_ids(self) -> Any:
+        return self._p2p.recv_ids()[:, :self.cfg.top_k]
+
     def status(self) -> None:
         self.layer.status()
 
     def close(self) -> None:
+        st = getattr(self, "_p2p", None)
+        if st is not None:
+            st.users -= 1
+            if st.users == 0:
+                st.close(self._p2p_group)
+                self._pool.pop("p2p", None)
+            self._p2p = None
         self.layer.close()

@@ -253,6 +253,46 @@ int moe_ep_experts_gathered(MoePlan* plan, const void* recv_rows, int32_t rows, 
 int moe_ep_combine_partial(MoePlan* plan, const float* x_dev, int32_t T, const float* partial,
                            float* out_dev, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Token-replicated exchange over peer memory (no counterpart in the reference; no
+ * collective library): the same records and partial sums as above, but the packing
+ * and partial-sum kernels store them straight into the other GPUs' buffers over
+ * NVLink and publish an epoch flag there, and a bounded wait kernel stands in for
+ * each collective.  Per rank, allocated once with moe_rt_malloc (cudaMalloc'd, so
+ * that moe_rt_ipc_get_handle works) and mapped on every other rank with
+ * moe_rt_ipc_open_handle:
+ *   recv   [world*cap, moe_ep_token_row_halves(plan)] f16, records of rank r at rows
+ *          [r*cap, (r+1)*cap)
+ *   part   [world, cap, H] fp32, rank r's partial sums for this rank's tokens in [r]
+ *   flags  [2, world] int32, zeroed once: [0][r] records of rank r, [1][r] its
+ *          partials, each the epoch of the last forward whose data is complete
+ *   done   2 int32 on this rank's device, zeroed once (launch counters)
+ * The peer arrays hold world device pointers, index d = rank d's buffer as mapped
+ * here (d == rank: the local one).  One forward, epoch e = 1, 2, ... the same on
+ * every rank, all on one stream:
+ *   1. moe_ep_p2p_pack(x, T, cap, peer_recv, peer_flags, e, done + 0)
+ *   2. moe_ep_p2p_wait(flags + 0, world, e)         every rank's records arrived
+ *   3. moe_ep_p2p_experts(recv, cap, peer_part, peer_flags, e, done + 1)
+ *   4. moe_ep_p2p_wait(flags + world, world, e)     every rank's partials arrived
+ *   5. moe_ep_shared (any time after step 1) and moe_ep_p2p_combine(x, T, part):
+ *      out = x + sum over source ranks (rank order) of part + shared expert.
+ * Workspaces: steps 1, 5 as moe_ep_dispatch; step 3 moe_ep_gathered_workspace_bytes(
+ * plan, world*cap).  A wait that runs out (a peer stopped, or is out of step)
+ * returns with MOE_ERR_TIMEOUT at the next moe_status; all ranks must use the same
+ * cap and epochs.  Ranks on one GPU are not supported (each wait needs the other
+ * ranks' kernels running at the same time on their own GPUs). */
+int moe_ep_p2p_pack(MoePlan* plan, const float* x_dev, int32_t T, int32_t cap, int32_t rank,
+                    int32_t world, void* const* peer_recv, int32_t* const* peer_flags, int32_t epoch,
+                    int32_t* done, void* workspace, uint64_t workspace_bytes, void* stream);
+int moe_ep_p2p_wait(MoePlan* plan, const int32_t* flags, int32_t world, int32_t epoch,
+                    int64_t limit_cycles, void* stream);
+int moe_ep_p2p_experts(MoePlan* plan, const void* recv_rows, int32_t cap, int32_t rank,
+                       int32_t world, float* const* peer_part, int32_t* const* peer_flags,
+                       int32_t epoch, int32_t* done, void* workspace, uint64_t workspace_bytes,
+                       void* stream);
+int moe_ep_p2p_combine(MoePlan* plan, const float* x_dev, int32_t T, const float* part,
+                       int32_t cap, int32_t world, float* out_dev, void* workspace,
+                       uint64_t workspace_bytes, void* stream);
+
 /* Synchronise `stream`, then read and clear the device error word of the plan.
  * Returns MOE_OK, MOE_ERR_TIMEOUT (a bounded wait ran out), MOE_ERR_RANGE (an f16
  * activation or expert output overflowed) or MOE_ERR_DEVICE. */
@@ -319,6 +359,10 @@ int moe_rt_set_device(int32_t device);
 int moe_rt_can_access_peer(int32_t device, int32_t peer, int32_t* can_access);
 int moe_rt_malloc(uint64_t nbytes, void** dev_ptr);
 int moe_rt_free(void* dev_ptr);
+/* CUDA IPC of a moe_rt_malloc'd buffer (64-byte handle) for the peer-memory exchange. */
+int moe_rt_ipc_get_handle(const void* dev_ptr, void* handle);
+int moe_rt_ipc_open_handle(const void* handle, void** dev_ptr);
+int moe_rt_ipc_close_handle(void* dev_ptr);
 int moe_rt_malloc_host(uint64_t nbytes, void** host_ptr);
 int moe_rt_free_host(void* host_ptr);
 int moe_rt_stream_create(void** stream);        /* non-blocking stream */

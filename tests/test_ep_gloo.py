@@ -293,3 +293,45 @@ def test_token_replicated_exchange_with_an_empty_rank() -> None:
     assert [r[1] for r in res] == ["ok", "ok"], res
     for _rank, _status, err in res:
         assert err < 1e-5
+
+
+class _RecordingP2POps:
+    """Records the peer-memory exchange's calls (the device work itself needs GPUs)."""
+
+    def __init__(self) -> None:
+        self.calls: list = []
+
+    def p2p_setup(self, cap: int, group) -> None:  # noqa: ANN001
+        self.calls.append(("setup", cap))
+
+    def p2p_pack(self, x: torch.Tensor, cap: int) -> None:
+        self.calls.append(("pack", int(x.shape[0]), cap))
+
+    def start_shared(self, x: torch.Tensor) -> None:
+        self.calls.append(("shared",))
+
+    def p2p_wait(self, which: int) -> None:
+        self.calls.append(("wait", which))
+
+    def p2p_experts(self) -> None:
+        self.calls.append(("experts",))
+
+    def p2p_combine(self, x: torch.Tensor) -> torch.Tensor:
+        self.calls.append(("combine",))
+        return x + 1
+
+
+def test_peer_memory_exchange_protocol_order() -> None:
+    """p2p exchange: buffers set up once at construction, then per forward pack,
+    shared expert, wait for records, experts (+ partials to owners), wait for
+    partials, combine; batches above padded_tokens take the exact path."""
+    from moe_sm100.ep import ExpertParallelMoe
+    ops = _RecordingP2POps()
+    ep = ExpertParallelMoe(ops, padded_tokens=8, small_exchange="p2p")
+    assert ops.calls == [("setup", 8)]
+    out = ep.forward(torch.zeros(5, 4))
+    assert torch.equal(out, torch.ones(5, 4))
+    assert ops.calls[1:] == [("pack", 5, 8), ("shared",), ("wait", 0), ("experts",), ("wait", 1),
+                             ("combine",)]
+    with pytest.raises(ValueError):
+        ExpertParallelMoe(ops, padded_tokens=8, small_exchange="bogus")

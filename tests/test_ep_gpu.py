@@ -4,9 +4,10 @@ Two processes, one per GPU, each holding half of the routed experts.  Each rank
 compares its expert-parallel output with a single-GPU plan holding all experts
 on the same tokens: the only arithmetic difference is that expert outputs cross
 the exchange as f16 (or are summed per rank before a reduce-scatter), so the
-bound is the 16-bit parity tolerance.  All three exchanges run: exact (counts,
-then rows and ids), fixed-capacity (equal row blocks, ids in the row tails) and
-token-replicated (all-gather of token records, reduce-scatter of partial sums).
+bound is the 16-bit parity tolerance.  All four exchanges run: exact (counts,
+then rows and ids), fixed-capacity (equal row blocks, ids in the row tails),
+token-replicated over NCCL (all-gather of token records, reduce-scatter of partial
+sums) and the same over peer memory (NVLink stores and epoch flags, no NCCL).
 """
 from __future__ import annotations
 
@@ -57,12 +58,13 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
             ep = ExpertParallelMoe(ops)
             epp = ExpertParallelMoe(ops, padded_tokens=64)
             epg = ExpertParallelMoe(ops, padded_tokens=64, small_exchange="gathered")
+            epp2p = ExpertParallelMoe(ops, padded_tokens=64, small_exchange="p2p")
             gen = torch.Generator(device=f"cuda:{rank}").manual_seed(100 + rank)
             for T in (1, 37, 300):
                 x = torch.randn((T, 2048), generator=gen, device=f"cuda:{rank}")
                 ref = full.forward(x)
-                for mode, e in (("exact", ep), ("padded", epp), ("gathered", epg)):
-                    out = e.forward(x)  # T = 300 > 64 takes the exact path in all three
+                for mode, e in (("exact", ep), ("padded", epp), ("gathered", epg), ("p2p", epp2p)):
+                    out = e.forward(x)  # T = 300 > 64 takes the exact path in all four
                     ops.status()
                     err = float((out.double() - ref.double()).norm() / ref.double().norm())
                     results.append((family, mode, T, err))
