@@ -23,11 +23,12 @@ box's host cores, all BLAS threads, same config, metric and unit.
 
 N > 1 (torchrun): expert parallel -- rank r holds routed experts
 [r*160/N, (r+1)*160/N), router and shared expert replicated, 64 tokens per rank
-(weak scaling).  Decode batches take by default the token-replicated exchange
-(NCCL all-gather of the ranks' token records, reduce-scatter of fp32 per-token
-partial sums; no host synchronisation); --ep-exchange padded: fixed-capacity
-all-to-all of f16 rows; exact: counts first, then exactly the routed rows.
-Prefill batches take the exact exchange.
+(weak scaling).  Decode batches take by default the token-replicated exchange over
+peer memory (each rank's token records and fp32 per-token partial sums stored over
+NVLink by the kernels that produce them, epoch flags and bounded device waits, no
+NCCL); --ep-exchange gathered: the same exchange as an NCCL all-gather and
+reduce-scatter; padded: fixed-capacity all-to-all of f16 rows; exact: counts first,
+then exactly the routed rows.  Prefill batches take the exact exchange.
 
 --stack (torchrun, N = 2, 4 or 8): BASELINE config 4 -- 89 GLM-4.7-shape INT8 layers
 (seed + layer each, Zipf-skewed routing) resident expert parallel, 160/N experts of
@@ -478,7 +479,7 @@ def run_ep(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, random-init)",
             "config": {"workload": "BASELINE config 1 shape, expert parallel",
                        "tokens_per_rank": T, "experts_per_rank": e_loc,
-                       "parallelism": f"ep{world} (NCCL collectives dispatch/combine)",
+                       "parallelism": f"ep{world} (" + ("NVLink peer stores" if args.ep_exchange == "p2p" else "NCCL collectives") + " dispatch/combine)",
                        "exchange": _exchange_name(args.ep_exchange),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (rank 0)",
@@ -569,7 +570,7 @@ def run_stack(args, world: int, rank: int, local: int) -> None:  # noqa: ANN001
             "vs_baseline": None,
             "config": {"workload": "BASELINE config 4", "layers": L, "global_tokens": batches,
                        "experts_per_rank": E // world if world else None,
-                       "parallelism": f"ep{world} (NCCL collectives dispatch/return)",
+                       "parallelism": f"ep{world} (expert parallel; exchanges below)",
                        "exchange": {"decode": _exchange_name(args.ep_exchange), "prefill": "exact"}}}
     if world < 2 or E % world or any(t % world for t in batches.values()):
         if rank == 0:
@@ -915,7 +916,7 @@ def main() -> None:
                     help="skip BASELINE configs 2 and 3 (INT8 prefill, Qwen3 shape)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling uses fewer to stay within a few GB)")
-    ap.add_argument("--ep-exchange", choices=["padded", "gathered", "p2p", "exact"], default="gathered",
+    ap.add_argument("--ep-exchange", choices=["padded", "gathered", "p2p", "exact"], default="p2p",
                     help="N > 1 decode batches: fixed-capacity all-to-all, token-replicated "
                          "all-gather/reduce-scatter, or exact all-to-all")
     ap.add_argument("--stack", action="store_true",
