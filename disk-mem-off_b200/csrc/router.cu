@@ -240,44 +240,50 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     denom = s;
   }
-  // lane r keeps the r-th selection (no per-thread arrays: they lived in local memory)
+  // Each candidate as one 64-bit key: the score's bits in an order-preserving
+  // form above the complemented expert id, so one unsigned max picks the largest
+  // score and, among equal scores, the lowest id.  Lane r keeps the r-th selection.
+  uint64_t pk[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int e = j * 32 + lane;
+    if (e < E) {
+      const uint32_t u = __float_as_uint(key[j]);
+      const uint32_t ob = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      pk[j] = (static_cast<uint64_t>(ob) << 32) | static_cast<uint32_t>(~e);
+    } else {
+      pk[j] = 0ull;
+    }
+  }
   int my_id = 0;
   float my_w = 0.f;
-  uint32_t taken = 0u;
   for (int r = 0; r < K; ++r) {
-    float bk = -FLT_MAX;
-    int bid = 0x7fffffff;
-    float bv = 0.f;
+    uint64_t best = 0ull;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E && !((taken >> j) & 1u) &&
-          (bid == 0x7fffffff || key[j] > bk || (key[j] == bk && e < bid))) {
-        bk = key[j];
-        bid = e;
-        bv = val[j];
-      }
-    }
+    for (int j = 0; j < VPL; ++j) best = pk[j] > best ? pk[j] : best;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
-        bk = ok;
-        bid = oid;
-        bv = ov;
-      }
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
     }
-    if (bid >= E) {  // K > E cannot happen for a validated plan
+    int bid = static_cast<int>(~static_cast<uint32_t>(best));
+    if (best == 0ull || bid < 0 || bid >= E) {  // K > E cannot happen for a validated plan
       record_error(err, DEV_BAD_ROUTE);
       bid = 0;
     }
+    const int slot = bid >> 5;
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) v = (j == slot) ? val[j] : v;
+    const float bv = __shfl_sync(0xffffffffu, v, bid & 31);
     if (lane == r) {
       my_id = bid;
       my_w = (score_func == MOE_SCORE_SOFTMAX) ? bv / denom : bv;
     }
-    if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
+    if ((bid & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) pk[j] = (j == slot) ? 0ull : pk[j];
+    }
   }
   float sum = 0.f;  // rank order, one term at a time
   if (norm)
