@@ -203,6 +203,14 @@ template <int VPL>
 MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
                        int K, int score_func, int norm, float scale, int lane,
                        int32_t* ids_out, float* w_out, int* err) {
+  // every load first (one memory round trip, not one per value), then the scores
+  float lv[VPL], bv0[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int e = j * 32 + lane;
+    lv[j] = e < E ? lrow[e] : 0.f;
+    bv0[j] = (bias && e < E) ? bias[e] : 0.f;
+  }
   float key[VPL], val[VPL];
   float m = -FLT_MAX;
 #pragma unroll
@@ -211,16 +219,16 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
     key[j] = -FLT_MAX;
     val[j] = 0.f;
     if (e < E) {
-      float l = lrow[e];
+      float l = lv[j];
       if (score_func == MOE_SCORE_SOFTMAX) {
-        if (bias) l = l + bias[e];
+        if (bias) l = l + bv0[j];
         key[j] = l;
         val[j] = l;
         m = fmaxf(m, l);
       } else {
         const float s = sigmoid_f(l);
         val[j] = s;
-        key[j] = bias ? s + bias[e] : s;
+        key[j] = bias ? s + bv0[j] : s;
       }
     }
   }
