@@ -342,10 +342,9 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
   const size_t plane = static_cast<size_t>(T) * R;
   float* lrow = logits + static_cast<size_t>(t) * R;
   const int C = min(E, K + kRefineMargin);
-  float key[VPL];
-  bool taken[VPL];
-  // all plane loads are issued before any is added (the bound is a constant)
+  // all plane and bias loads are issued before any is used (the bounds are constants)
   float pl[kRouterMaxSplit][VPL];
+  float bs[VPL];
 #pragma unroll
   for (int sp = 0; sp < kRouterMaxSplit; ++sp)
 #pragma unroll
@@ -356,16 +355,31 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int e = j * 32 + lane;
-    key[j] = -FLT_MAX;
-    taken[j] = false;
+    bs[j] = (bias && e < E) ? bias[e] : 0.f;
+  }
+  // each candidate as one 64-bit key (order-preserving score bits over the
+  // complemented id): one unsigned max per round picks the largest key and, among
+  // equal keys, the lowest id; a NaN key is reported and never selected
+  uint64_t pk[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int e = j * 32 + lane;
+    pk[j] = 0ull;
     if (e < E) {
       float l = pl[0][j];
 #pragma unroll
       for (int sp = 1; sp < kRouterMaxSplit; ++sp)
         if (sp < nplanes) l += pl[sp][j];  // split order
       if (nplanes > 1) lrow[e] = l;  // plane 0 now holds the summed logits
-      key[j] = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bias[e] : l)
-                                                 : (bias ? sigmoid_f(l) + bias[e] : sigmoid_f(l));
+      const float key = (score_func == MOE_SCORE_SOFTMAX) ? (bias ? l + bs[j] : l)
+                                                          : (bias ? sigmoid_f(l) + bs[j] : sigmoid_f(l));
+      if (key != key) {
+        record_error(err, DEV_BAD_ROUTE);
+      } else {
+        const uint32_t u = __float_as_uint(key);
+        const uint32_t ob = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        pk[j] = (static_cast<uint64_t>(ob) << 32) | static_cast<uint32_t>(~e);
+      }
     }
   }
   if (nplanes > 1 && lane == 0 && E < R) {  // the shared-expert gate row
@@ -377,26 +391,18 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
   int n = K;
   bool all_rows = false;
   for (int r = 0; r < C; ++r) {
-    float bk = -FLT_MAX;
-    int bid = 0x7fffffff;
+    uint64_t best = 0ull;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E && !taken[j] && (bid == 0x7fffffff || key[j] > bk || (key[j] == bk && e < bid))) {
-        bk = key[j];
-        bid = e;
-      }
-    }
+    for (int j = 0; j < VPL; ++j) best = pk[j] > best ? pk[j] : best;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-      if (oid != 0x7fffffff && (bid == 0x7fffffff || ok > bk || (ok == bk && oid < bid))) {
-        bk = ok;
-        bid = oid;
-      }
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
     }
-    if (bid >= E) {  // a NaN key leaves no winner
+    int bid = static_cast<int>(~static_cast<uint32_t>(best));
+    const uint32_t ob = static_cast<uint32_t>(best >> 32);
+    const float bk = __uint_as_float((ob & 0x80000000u) ? (ob & 0x7fffffffu) : ~ob);
+    if (best == 0ull || bid < 0 || bid >= E) {  // no selectable key left (NaN keys)
       record_error(err, DEV_BAD_ROUTE);
       bid = 0;
     }
@@ -410,9 +416,10 @@ __global__ void __launch_bounds__(256) route_cand_kernel(
         break;  // keys only fall from here on
       }
     }
+    const bool mine = lane == (bid & 31);
+    const int slot = bid >> 5;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j)
-      if (j == (bid >> 5) && lane == (bid & 31)) taken[j] = true;
+    for (int j = 0; j < VPL; ++j) pk[j] = (mine && j == slot) ? 0ull : pk[j];
     if (lane == 0) cand[static_cast<size_t>(t) * kCandMax + r] = bid;
   }
   if (lane == 0) nrows[t] = all_rows ? -1 : n;
