@@ -87,7 +87,10 @@ struct TileCfg {
   static constexpr int kAccCols = kChains * BN;  // one accumulator buffer
   static constexpr int kTmemCols = TS ? 512 : (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
                                    : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
-  static constexpr int kAColBase = 2 * kAccCols;  // TS: first column of the A slots
+  // accumulator buffers: two (tile i's epilogue overlaps tile i+1's MMAs), one for a
+  // 256-column tile with its A operand in TMEM (the A slots take the other half)
+  static constexpr int kAccBufs = (TS && BN > 64) ? 1 : 2;
+  static constexpr int kAColBase = kAccBufs * kAccCols;  // TS: first column of the A slots
   // Epilogue warps: a 256-column accumulator takes 8 (each TMEM lane quarter
   // twice, splitting the columns) so that draining a tile stays shorter than
   // its MMAs; narrow decode tiles keep 4.
@@ -111,7 +114,12 @@ __host__ __device__ constexpr int gemm_threads() {
 #define MOE_INT8_TMEM_A 1
 #endif
 template <int BN, bool INT8>
-__host__ __device__ constexpr bool gemm_ts() { return MOE_INT8_TMEM_A && INT8 && BN <= 64; }
+#ifndef MOE_INT8_TMEM_A_PREFILL
+#define MOE_INT8_TMEM_A_PREFILL 0
+#endif
+__host__ __device__ constexpr bool gemm_ts() {
+  return MOE_INT8_TMEM_A && INT8 && (BN <= 64 || (MOE_INT8_TMEM_A_PREFILL && BN == 256));
+}
 
 // As many stages as fit under the 227 KiB opt-in shared memory per CTA (less the
 // alignment slack, barriers and a little static shared memory), up to 8 (12 with
@@ -150,7 +158,8 @@ constexpr int kGemmSmemBudget = 232448 - 1024 - kGemmBarBytes - 512;
 
 template <int BN, bool INT8>
 __host__ __device__ constexpr int gemm_kps() {
-  return gemm_ts<BN, INT8>() ? MOE_INT8_DECODE_KPS_TS : (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1;
+  return gemm_ts<BN, INT8>() ? (BN <= 64 ? MOE_INT8_DECODE_KPS_TS : 1)
+                             : (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1;
 }
 
 template <int BN, bool INT8>
@@ -451,8 +460,9 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
       for (int ti = blockIdx.x; ti < ntiles && !*abort_flag; ti += gridDim.x) {
         const Tile t = fetch_tile(ti);
         if (!tile_ok(t)) continue;
-        const int buf = tl & 1;
-        if (!mbar_wait_bounded(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag)) {
+        constexpr int NB = Cfg::kAccBufs;
+        const int buf = tl % NB;
+        if (!mbar_wait_bounded(&tempty[buf], ((tl / NB) & 1) ^ 1, abort_flag)) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_TMEM_EMPTY);
           break;
@@ -517,12 +527,13 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
       const Tile t = fetch_tile(ti);
       if (!tile_ok(t)) continue;
-      const int buf = tl & 1;
+      constexpr int NB = Cfg::kAccBufs;
+      const int buf = tl % NB;
       // every lane polls; the warp vote re-converges the warp before the
       // .sync.aligned TMEM loads, and the epilogue warps then agree through a
       // double-buffered flag so that all of them take (or skip) the named
       // barriers below together
-      const bool my_ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl >> 1) & 1, abort_flag));
+      const bool my_ready = __all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tl / NB) & 1, abort_flag));
       if (lane == 0) s_ready[tl & 1][ew] = my_ready ? 1 : 0;
       epilogue_bar<32 * EPI>();
       bool ready = true;
