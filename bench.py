@@ -349,6 +349,47 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
             res[f"{name if T >= 1024 else name.replace('_prefill', '_decode')}_T{T}"] = entry
         ml.close()
         torch.cuda.empty_cache()
+    if not args.other_tokens:
+        res.update(run_attention(args, local, hbm, tflops))
+    return res
+
+
+GLM_ATTN = dict(hidden=5120, heads=96, kv_heads=8, head_dim=128)
+
+
+def run_attention(args, local: int, hbm: float, tflops: float) -> dict:  # noqa: ANN001
+    """The GLM-4.7-shape attention block on the device (scope row f3: x + o_proj(causal
+    GQA attention(rms_norm(x))) over a whole sequence, as GLM4MoeExecutor._attention_block
+    computes it): a 64-token and a 4096-token sequence, synthetic bf16-valued weights."""
+    import torch
+    from moe_sm100.attention import AttentionConfig, AttentionLayer
+    from moe_sm100.synthetic import build_device_attention
+    H, nh, nkv, hd = (GLM_ATTN[k] for k in ("hidden", "heads", "kv_heads", "head_dim"))
+    blob, meta = build_device_attention(H, nh, nkv, hd, seed=99, device=f"cuda:{local}")
+    cfg = AttentionConfig(hidden=H, heads=nh, kv_heads=nkv, head_dim=hd, rotary_dim=hd // 2,
+                          rope_theta=1_000_000.0, rms_norm_eps=1e-5, max_tokens=4096, device=local)
+    al = AttentionLayer(cfg)
+    al.bind_device(blob.data_ptr(), blob.numel(), meta)
+    torch.cuda.synchronize()
+    del blob
+    gen = torch.Generator(device="cuda").manual_seed(2500 + local)
+    wbytes = ((nh + 2 * nkv) * hd * H + H * nh * hd) * 2
+    res = {}
+    for T in (64, 4096):
+        x = torch.randn((T, H), generator=gen, device="cuda")
+        out = torch.empty_like(x)
+        steps = max(3, min(args.steps, 20))
+        ms = _time_steps(lambda: al.forward(x, out), steps, args.warmup, 1)
+        proj = 2.0 * T * H * (nh + 2 * nkv) * hd + 2.0 * T * nh * hd * H
+        attn = 2.0 * 2 * nh * hd * T * (T + 1) / 2  # QK^T and PV over the causal half
+        res[f"attn_glm47_T{T}"] = {
+            "tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "seq_len": T,
+            "tflops": (proj + attn) / (ms * 1e-3) / 1e12,
+            "tc_frac": (proj + attn) / (ms * 1e-3) / 1e12 / tflops,
+            "weight_hbm_frac": wbytes / (ms * 1e-3) / 1e9 / hbm}
+    al.status()
+    al.close()
+    torch.cuda.empty_cache()
     return res
 
 

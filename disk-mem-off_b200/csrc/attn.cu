@@ -101,6 +101,17 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
   const int heads = nh + 2 * nkv;
   const size_t nqkv = static_cast<size_t>(heads) * HD;
   const int half = rot / 2;
+  // this token's rotation angles, once per CTA (they do not depend on the head):
+  // the same double-precision frequency, angle and cos / sin as the reference's
+  __shared__ float s_cos[HD / 2], s_sin[HD / 2];
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    const double freq = 1.0 / pow(static_cast<double>(theta),
+                                  static_cast<double>(j) / static_cast<double>(half));
+    const float ang = static_cast<float>(static_cast<double>(t) * freq);
+    s_cos[j] = static_cast<float>(cos(static_cast<double>(ang)));
+    s_sin[j] = static_cast<float>(sin(static_cast<double>(ang)));
+  }
+  __syncthreads();
   for (int hh = warp; hh < heads; hh += 8) {
     const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
     float v[V];
@@ -135,11 +146,7 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
           const int d = lane * V + i;
           if (d < rot) {
             const int j = d < half ? d : d - half;
-            const double freq = 1.0 / pow(static_cast<double>(theta),
-                                          static_cast<double>(j) / static_cast<double>(half));
-            const float ang = static_cast<float>(static_cast<double>(t) * freq);
-            const float c = static_cast<float>(cos(static_cast<double>(ang)));
-            const float sn = static_cast<float>(sin(static_cast<double>(ang)));
+            const float c = s_cos[j], sn = s_sin[j];
             v[i] = d < half ? v[i] * c - sh[warp][d + half] * sn
                             : v[i] * c + sh[warp][d - half] * sn;
           }
@@ -168,7 +175,7 @@ struct FaCfg {
   static constexpr int kP = kAttnTile * kAttnTile * 2; // P tile: 2 blocks of 64 keys
   // at least 120 KiB, so that one CTA holds an SM (and all 512 TMEM columns) for
   // either head size: a second CTA would only wait in tcgen05.alloc
-  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + kP + 256;
+  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + 2 * kP + 256;  // two P buffers
   static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
   static constexpr uint32_t kTmemCols = 512;           // S[2] at 0 / 128, O at 256
 };
@@ -190,16 +197,16 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   uint8_t* sK = sQ + C::kQ;
   uint8_t* sV = sK + 2 * C::kK;
   uint8_t* sP = sV + 2 * C::kV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::kP);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* mma_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* p_full = bars + 9;    // [2] P buffer b written (tiles j with j % 2 == b)
+  uint64_t* o_done = bars + 11;   // [2] P V of a tile on buffer b finished
+  uint64_t* mma_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -217,8 +224,10 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+    }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -294,7 +303,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
           ok = false;
           break;
         }
-        if (!mbar_wait_bounded(p_full, j & 1, abort_flag)) {
+        if (!mbar_wait_bounded(&p_full[j & 1], (j >> 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
@@ -303,11 +312,11 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
         for (int k = 0; k < kAttnTile / 16; ++k) {
           const int kb = k >> 2, kk = k & 3;
-          tc_mma_f16(tmem_base + 2 * kAttnTile, sw128_desc(ap + kb * 16384 + kk * 32),
+          tc_mma_f16(tmem_base + 2 * kAttnTile, sw128_desc(ap + (j & 1) * C::kP + kb * 16384 + kk * 32),
                      sw128_desc(av + s * C::kV + kb * C::kVblk + kk * 32), idesc_o,
                      (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc_commit(o_done);
+        tc_commit(&o_done[j & 1]);
         tc_commit(&kv_empty[s]);
       }
       if (!ok) {
@@ -350,33 +359,49 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         if (diag && c > qrow) sc[c] = -INFINITY;
         mx = fmaxf(mx, sc[c]);
       }
-      const float m_new = fmaxf(m, mx);  // finite: key 0 is never masked
-      const float alpha = exp2f((m - m_new) * args.scale_log2);
+      // m is the max the exponentials in O and l refer to; it moves (and O and l are
+      // rescaled) only when the row max grows by more than 2^8 in exp2 units, so
+      // most tiles need neither the rescale nor to wait for the previous P V; P then
+      // holds values up to 256, well inside f16
+      const float m_cand = fmaxf(m, mx);  // finite: key 0 is never masked
+      const bool grow = (m_cand - m) * args.scale_log2 > 8.f;  // always on the first tile
+      float alpha = 1.f;
+      if (grow) {
+        alpha = exp2f((m - m_cand) * args.scale_log2);
+        m = m_cand;
+      }
       float rs = 0.f;
 #pragma unroll
       for (int c = 0; c < kAttnTile; ++c) {
-        sc[c] = exp2f((sc[c] - m_new) * args.scale_log2);
+        sc[c] = exp2f((sc[c] - m) * args.scale_log2);
         rs += sc[c];
       }
       l = l * alpha + rs;
-      if (j > 0) {
-        // P V of tile j - 1 has finished: O is complete up to j - 1 and P is free
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (j - 1) & 1, abort_flag))) {
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O must be complete up to tile j - 1 before it is rescaled
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1,
+                                                       abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < HD / 16; ++c) {
-            float o[16];
-            tmem_ld16(lbase + ocol + c * 16, o);
+        for (int c = 0; c < HD / 16; ++c) {
+          float o[16];
+          tmem_ld16(lbase + ocol + c * 16, o);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] *= alpha;
-            tmem_st16(lbase + ocol + c * 16, o);
-          }
+          for (int i = 0; i < 16; ++i) o[i] *= alpha;
+          tmem_st16(lbase + ocol + c * 16, o);
         }
       }
+      if (j >= 2) {
+        // P buffer j % 2 is free once P V of tile j - 2 has finished
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[j & 1], ((j >> 1) & 1) ^ 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+      }
+      uint8_t* sPj = sP + (j & 1) * C::kP;
       // P row -> the 128-byte-swizzled K-major A operand (chunk c of row r at c ^ (r & 7))
 #pragma unroll
       for (int cb = 0; cb < kAttnTile / 8; ++cb) {
@@ -384,15 +409,16 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
         for (int i = 0; i < 4; ++i) hp[i] = __floats2half2_rn(sc[cb * 8 + 2 * i], sc[cb * 8 + 2 * i + 1]);
         const int blk = cb >> 3, ch = cb & 7;
-        *reinterpret_cast<uint4*>(sP + blk * 16384 + qrow * 128 + ((ch ^ (qrow & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(sPj + blk * 16384 + qrow * 128 + ((ch ^ (qrow & 7)) << 4)) =
             *reinterpret_cast<uint4*>(hp);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
-      m = m_new;
+      mbar_arrive(&p_full[j & 1]);
     }
-    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (nkt - 1) & 1, abort_flag))) ok = false;
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1,
+                                                          abort_flag)))
+      ok = false;
     if (ok) {
       tc_fence_after();
       const float inv = 1.0f / l;

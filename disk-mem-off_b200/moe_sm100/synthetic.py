@@ -206,3 +206,41 @@ class LazyHostTensors:
 
     def cached_bytes(self) -> int:
         return sum(a.nbytes for a in self._cache.values())
+
+
+def build_device_attention(hidden: int, heads: int, kv_heads: int, head_dim: int, seed: int = 0,
+                           device: Any = "cuda", bias: bool = True,
+                           qk_norm: bool = True) -> tuple[Any, list[dict[str, Any]]]:
+    """``(blob uint8 CUDA tensor, tensor metadata)`` of one synthetic GLM-4 attention
+    block, named as the loader names them: bf16 projections N(0, 0.02), fp32 biases
+    and norm weights (ones)."""
+    torch = _torch()
+    H, nh, nkv, hd = hidden, heads, kv_heads, head_dim
+    items: list[tuple[str, list[int], str]] = [("input_layernorm.weight", [H], "float32")]
+    for name, rows in (("q", nh * hd), ("k", nkv * hd), ("v", nkv * hd)):
+        items.append((f"self_attn.{name}_proj.weight", [rows, H], "bfloat16"))
+        if bias:
+            items.append((f"self_attn.{name}_proj.bias", [rows], "float32"))
+    if qk_norm:
+        items += [("self_attn.q_norm.weight", [hd], "float32"), ("self_attn.k_norm.weight", [hd], "float32")]
+    items.append(("self_attn.o_proj.weight", [H, nh * hd], "bfloat16"))
+    meta: list[dict[str, Any]] = []
+    off = 0
+    for name, shape, dt in items:
+        off = (off + 255) // 256 * 256
+        nb = int(np.prod(shape)) * _ESIZE[dt]
+        meta.append({"name": name, "shape": shape, "dtype": dt, "offset": off, "nbytes": nb})
+        off += nb
+    blob = torch.empty(off, dtype=torch.uint8, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    for m in meta:
+        v = blob[m["offset"]:m["offset"] + m["nbytes"]]
+        if m["dtype"] == "bfloat16":
+            v.view(torch.bfloat16).view(m["shape"]).copy_(
+                (torch.randn(m["shape"], generator=gen, device=device) * 0.02).to(torch.bfloat16))
+        elif m["name"].endswith("_proj.bias"):
+            v.view(torch.float32).copy_(torch.randn(m["shape"], generator=gen, device=device) * 0.02)
+        else:
+            v.view(torch.float32).fill_(1.0)
+    return blob, meta
