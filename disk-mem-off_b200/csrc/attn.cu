@@ -54,7 +54,7 @@ struct AttnPlan {
 };
 
 struct AttnWs {
-  size_t rms, h16, qkv, q, k, vt, o16, oplanes, total;
+  size_t rms, h16, qkv, q, k, v, vt, o16, oplanes, total;
   int tpad, s1, s2;
 };
 
@@ -72,6 +72,7 @@ static AttnWs attn_ws(const AttnPlan& a, int T) {
   w.qkv = take(static_cast<size_t>(w.s1) * T * a.nqkv * 4);
   w.q = take(static_cast<size_t>(a.nh) * w.tpad * a.hd * 2);
   w.k = take(static_cast<size_t>(a.nkv) * w.tpad * a.hd * 2);
+  w.v = take(static_cast<size_t>(a.nkv) * w.tpad * a.hd * 2);
   w.vt = take(static_cast<size_t>(a.nkv) * a.hd * w.tpad * 2);
   w.o16 = take(static_cast<size_t>(T) * a.nout * 2);
   w.oplanes = take(static_cast<size_t>(w.s2) * T * a.H * 4);
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
     const float* __restrict__ planes, int nsplit, int T, int tpad, int nh, int nkv,
     const float* __restrict__ bias, const float* __restrict__ qn, const float* __restrict__ kn,
     int rot, float theta, float eps, __half* __restrict__ q16, __half* __restrict__ k16,
-    __half* __restrict__ vt16) {
+    __half* __restrict__ v16) {
   pdl_enter();
   constexpr int V = HD / 32;
   __shared__ float sh[8][HD];
@@ -115,15 +116,22 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
   for (int hh = warp; hh < heads; hh += 8) {
     const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
     float v[V];
+    static_assert(V == 2 || V == 4, "head size 64 or 128");
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int d = lane * V + i;
-      float acc = 0.f;
-      if (t < T) {
-        for (int s = 0; s < nsplit; ++s) acc += planes[(static_cast<size_t>(s) * T + t) * nqkv + hh * HD + d];
-        acc += bias[hh * HD + d];
+    for (int i = 0; i < V; ++i) v[i] = 0.f;
+    if (t < T) {  // V consecutive values per lane, split planes added in order
+      for (int s = 0; s < nsplit; ++s) {
+        const float* src = planes + (static_cast<size_t>(s) * T + t) * nqkv + hh * HD + lane * V;
+        if constexpr (V == 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(src);
+          v[0] += a4.x; v[1] += a4.y; v[2] += a4.z; v[3] += a4.w;
+        } else {
+          const float2 a2 = *reinterpret_cast<const float2*>(src);
+          v[0] += a2.x; v[1] += a2.y;
+        }
       }
-      v[i] = acc;
+#pragma unroll
+      for (int i = 0; i < V; ++i) v[i] += bias[hh * HD + lane * V + i];
     }
     if (t < T && kind < 2) {
       const float* nw = kind == 0 ? qn : kn;
@@ -154,14 +162,39 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
         __syncwarp();
       }
     }
+    // q, k and v rows [head][tpad][HD] (v is transposed by attn_vt_kernel)
+    __half* dst = kind == 0 ? q16 + (static_cast<size_t>(hh) * tpad + t) * HD
+                : kind == 1 ? k16 + (static_cast<size_t>(hh - nh) * tpad + t) * HD
+                            : v16 + (static_cast<size_t>(hh - nh - nkv) * tpad + t) * HD;
+    __half2 h2[V / 2];
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int d = lane * V + i;
-      const __half hv = __float2half_rn(v[i]);
-      if (kind == 0) q16[(static_cast<size_t>(hh) * tpad + t) * HD + d] = hv;
-      else if (kind == 1) k16[(static_cast<size_t>(hh - nh) * tpad + t) * HD + d] = hv;
-      else vt16[(static_cast<size_t>(hh - nh - nkv) * HD + d) * tpad + t] = hv;
-    }
+    for (int i = 0; i < V / 2; ++i) h2[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    if constexpr (V == 4) *reinterpret_cast<uint2*>(dst + lane * V) = *reinterpret_cast<uint2*>(h2);
+    else *reinterpret_cast<uint32_t*>(dst + lane * V) = *reinterpret_cast<uint32_t*>(h2);
+  }
+}
+
+// v [kv head][tpad][HD] -> vt [kv head][HD][tpad] (the K-major B operand of P V),
+// one 64 x 64 tile per CTA through shared memory.
+__global__ void __launch_bounds__(256) attn_vt_kernel(const __half* __restrict__ v16,
+                                                      __half* __restrict__ vt16, int tpad, int HD) {
+  pdl_enter();
+  __shared__ __align__(16) __half tile[64][64 + 8];
+  const int t0 = blockIdx.x * 64, d0 = blockIdx.y * 64, h = blockIdx.z;
+  const __half* src = v16 + (static_cast<size_t>(h) * tpad + t0) * HD + d0;
+  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {  // 64 rows x 8 chunks of 8 halves
+    const int r = i >> 3, c = (i & 7) * 8;
+    const uint4 q = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * HD + c);
+    const __half* qh = reinterpret_cast<const __half*>(&q);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[c + e][r] = qh[e];
+  }
+  __syncthreads();
+  __half* dst = vt16 + (static_cast<size_t>(h) * HD + d0) * tpad + t0;
+  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * tpad + c) =
+        *reinterpret_cast<const uint4*>(&tile[r][c]);
   }
 }
 
@@ -475,7 +508,9 @@ static cudaError_t attn_launch(const AttnPlan& a, const AttnWs& w, char* ws, con
           w.s1, T, w.tpad, a.nh, a.nkv, a.bqkv, a.has_qk_norm ? a.qn : nullptr,
           a.has_qk_norm ? a.kn : nullptr, a.rot, a.cfg.rope_theta, a.cfg.rms_norm_eps,
           reinterpret_cast<__half*>(ws + w.q), reinterpret_cast<__half*>(ws + w.k),
-          reinterpret_cast<__half*>(ws + w.vt));
+          reinterpret_cast<__half*>(ws + w.v));
+  MOE_PDL(attn_vt_kernel, dim3(w.tpad / 64, HD / 64, a.nkv), dim3(256), 0, s,
+          reinterpret_cast<const __half*>(ws + w.v), reinterpret_cast<__half*>(ws + w.vt), w.tpad, HD);
   FaArgs fa{};
   std::string err;
   if (!make_tmap_2d(&fa.tq, ws + w.q, false, HD, static_cast<uint64_t>(a.nh) * w.tpad, 64, kAttnTile,
