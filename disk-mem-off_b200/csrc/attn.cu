@@ -12,10 +12,12 @@
 // attn_fwd_kernel is a flash-attention kernel on the 5th-generation tensor cores:
 // one CTA per (128-query tile, head); S = Q K^T and O += P V are tcgen05.mma with
 // operands in shared memory (Q, K and V^T tiles by TMA, P written by the softmax
-// warps) and accumulators in TMEM; the softmax warps keep the running row max /
-// sum in registers and rescale O in TMEM when the max moves.  Keys arrive in
-// 128-key tiles through a two-stage ring, and the S of the next tile is computed
-// while the softmax works on the current one.  All waits are bounded.
+// warps, two buffers) and accumulators in TMEM; the softmax warps keep the row max
+// the exponentials refer to and the running sum in registers, and rescale O in
+// TMEM only when the row max grows by more than 2^8 (in exp2 units), so most
+// tiles neither rescale nor wait for the previous P V.  Keys arrive in 128-key
+// tiles through a two-stage ring, and the S of the next tile is computed while the
+// softmax works on the current one.  All waits are bounded.
 #include <math.h>
 
 #include <algorithm>
@@ -54,7 +56,7 @@ struct AttnPlan {
 };
 
 struct AttnWs {
-  size_t rms, h16, qkv, q, k, v, vt, o16, oplanes, total;
+  size_t rms, h16, qkv, rope, q, k, v, vt, o16, oplanes, total;
   int tpad, s1, s2;
 };
 
@@ -70,6 +72,7 @@ static AttnWs attn_ws(const AttnPlan& a, int T) {
   w.rms = take(static_cast<size_t>(T) * 4);
   w.h16 = take(static_cast<size_t>(T) * a.H * 2);
   w.qkv = take(static_cast<size_t>(w.s1) * T * a.nqkv * 4);
+  w.rope = take(static_cast<size_t>(T) * (a.hd / 2) * 8);  // (cos, sin) per token and pair
   w.q = take(static_cast<size_t>(a.nh) * w.tpad * a.hd * 2);
   w.k = take(static_cast<size_t>(a.nkv) * w.tpad * a.hd * 2);
   w.v = take(static_cast<size_t>(a.nkv) * w.tpad * a.hd * 2);
@@ -92,8 +95,8 @@ template <int HD>
 __global__ void __launch_bounds__(256) attn_qkv_kernel(
     const float* __restrict__ planes, int nsplit, int T, int tpad, int nh, int nkv,
     const float* __restrict__ bias, const float* __restrict__ qn, const float* __restrict__ kn,
-    int rot, float theta, float eps, __half* __restrict__ q16, __half* __restrict__ k16,
-    __half* __restrict__ v16) {
+    int rot, const float2* __restrict__ rope, float eps, __half* __restrict__ q16,
+    __half* __restrict__ k16, __half* __restrict__ v16) {
   pdl_enter();
   constexpr int V = HD / 32;
   __shared__ float sh[8][HD];
@@ -102,18 +105,16 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
   const int heads = nh + 2 * nkv;
   const size_t nqkv = static_cast<size_t>(heads) * HD;
   const int half = rot / 2;
-  // this token's rotation angles, once per CTA (they do not depend on the head):
-  // the same double-precision frequency, angle and cos / sin as the reference's
+  // this token's rotation (cos, sin) pairs from attn_rope_kernel's table
   __shared__ float s_cos[HD / 2], s_sin[HD / 2];
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
-    const double freq = 1.0 / pow(static_cast<double>(theta),
-                                  static_cast<double>(j) / static_cast<double>(half));
-    const float ang = static_cast<float>(static_cast<double>(t) * freq);
-    s_cos[j] = static_cast<float>(cos(static_cast<double>(ang)));
-    s_sin[j] = static_cast<float>(sin(static_cast<double>(ang)));
+    const float2 cs = t < T ? rope[static_cast<size_t>(t) * half + j] : make_float2(1.f, 0.f);
+    s_cos[j] = cs.x;
+    s_sin[j] = cs.y;
   }
   __syncthreads();
-  for (int hh = warp; hh < heads; hh += 8) {
+  // one head per warp; short sequences spread a token's heads over gridDim.y CTAs
+  for (int hh = blockIdx.y * 8 + warp; hh < heads; hh += 8 * gridDim.y) {
     const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
     float v[V];
     static_assert(V == 2 || V == 4, "head size 64 or 128");
@@ -172,6 +173,22 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
     if constexpr (V == 4) *reinterpret_cast<uint2*>(dst + lane * V) = *reinterpret_cast<uint2*>(h2);
     else *reinterpret_cast<uint32_t*>(dst + lane * V) = *reinterpret_cast<uint32_t*>(h2);
   }
+}
+
+// RoPE table of positions 0..T-1: (cos, sin) of pair j of token t, computed as the
+// reference does, in double precision: freq = 1 / theta^(j / half), angle =
+// float(t * freq), then cos / sin of that angle.  One thread per (token, pair).
+__global__ void __launch_bounds__(256) attn_rope_kernel(float2* __restrict__ rope, int T, int half,
+                                                        float theta) {
+  pdl_enter();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * half) return;
+  const int t = i / half, j = i - t * half;
+  const double freq = 1.0 / pow(static_cast<double>(theta),
+                                static_cast<double>(j) / static_cast<double>(half));
+  const float ang = static_cast<float>(static_cast<double>(t) * freq);
+  rope[i] = make_float2(static_cast<float>(cos(static_cast<double>(ang))),
+                        static_cast<float>(sin(static_cast<double>(ang))));
 }
 
 // v [kv head][tpad][HD] -> vt [kv head][HD][tpad] (the K-major B operand of P V),
@@ -488,11 +505,20 @@ __global__ void __launch_bounds__(256) attn_out_kernel(const float* __restrict__
                                                        const float* __restrict__ planes, int nsplit,
                                                        size_t n, float* __restrict__ out) {
   pdl_enter();
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+  // n is a multiple of 4 (H is a multiple of 64): float4 at a time, planes in order
+  const size_t n4 = n / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < nsplit; ++s) acc += planes[static_cast<size_t>(s) * n + i];
-    out[i] = x[i] + acc;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < nsplit; ++s) {
+      const float4 p = reinterpret_cast<const float4*>(planes + static_cast<size_t>(s) * n)[i];
+      acc.x += p.x;
+      acc.y += p.y;
+      acc.z += p.z;
+      acc.w += p.w;
+    }
+    const float4 xv = reinterpret_cast<const float4*>(x)[i];
+    reinterpret_cast<float4*>(out)[i] = make_float4(xv.x + acc.x, xv.y + acc.y, xv.z + acc.z, xv.w + acc.w);
   }
 }
 
@@ -504,9 +530,19 @@ static cudaError_t attn_launch(const AttnPlan& a, const AttnWs& w, char* ws, con
                                 reinterpret_cast<__half*>(ws + w.h16), a.d_err, s));
   MOE_CUDA_RET(launch_dense_gemm(a.tm_qkv, a.nqkv, a.H, reinterpret_cast<const __half*>(ws + w.h16), T,
                                  reinterpret_cast<float*>(ws + w.qkv), w.s1, a.d_err, a.num_sms, s));
-  MOE_PDL(attn_qkv_kernel<HD>, dim3(w.tpad), dim3(256), 0, s, reinterpret_cast<const float*>(ws + w.qkv),
+  const int half = a.rot / 2;
+  if (half > 0) {
+    MOE_PDL(attn_rope_kernel, dim3((T * half + 255) / 256), dim3(256), 0, s,
+            reinterpret_cast<float2*>(ws + w.rope), T, half, a.cfg.rope_theta);
+  }
+  // enough CTAs for every SM to hold several: one per token at long sequences, a
+  // token's heads in groups of 8 across CTAs at short ones
+  const int groups = (a.nh + 2 * a.nkv + 7) / 8;
+  const int gy = std::max(1, std::min(groups, (8 * a.num_sms + w.tpad - 1) / w.tpad));
+  MOE_PDL(attn_qkv_kernel<HD>, dim3(w.tpad, gy), dim3(256), 0, s, reinterpret_cast<const float*>(ws + w.qkv),
           w.s1, T, w.tpad, a.nh, a.nkv, a.bqkv, a.has_qk_norm ? a.qn : nullptr,
-          a.has_qk_norm ? a.kn : nullptr, a.rot, a.cfg.rope_theta, a.cfg.rms_norm_eps,
+          a.has_qk_norm ? a.kn : nullptr, a.rot, reinterpret_cast<const float2*>(ws + w.rope),
+          a.cfg.rms_norm_eps,
           reinterpret_cast<__half*>(ws + w.q), reinterpret_cast<__half*>(ws + w.k),
           reinterpret_cast<__half*>(ws + w.v));
   MOE_PDL(attn_vt_kernel, dim3(w.tpad / 64, HD / 64, a.nkv), dim3(256), 0, s,
