@@ -11,12 +11,14 @@
 //
 // attn_fwd_kernel is a flash-attention kernel on the 5th-generation tensor cores:
 // one CTA per (128-query tile, head); S = Q K^T and O += P V are tcgen05.mma with
-// operands in shared memory (Q, K and V^T tiles by TMA, P written by the softmax
-// warps, two buffers) and accumulators in TMEM; the softmax warps keep the row max
-// the exponentials refer to and the running sum in registers, and rescale O in
-// TMEM only when the row max grows by more than 2^8 (in exp2 units), so most
-// tiles neither rescale nor wait for the previous P V.  Keys arrive in 128-key
-// tiles through a two-stage ring, and the S of the next tile is computed while the
+// Q, K and V^T tiles in shared memory (by TMA), accumulators in TMEM, and P, the
+// A operand of P V, written to TMEM by the softmax warps (two buffers).  Two
+// softmax warpgroups split each query row's 128 keys (and O's columns) in halves
+// and swap their partial row max through shared memory; they keep the max the
+// exponentials refer to and the running sum in registers, and rescale O in TMEM
+// only when the row max grows by more than 2^8 (in exp2 units), so most tiles
+// neither rescale nor wait for the previous P V.  Keys arrive in 128-key tiles
+// through a two-stage ring, and the S of the next tile is computed while the
 // softmax works on the current one.  All waits are bounded.
 #include <math.h>
 
@@ -113,65 +115,86 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
     s_sin[j] = cs.y;
   }
   __syncthreads();
-  // one head per warp; short sequences spread a token's heads over gridDim.y CTAs
-  for (int hh = blockIdx.y * 8 + warp; hh < heads; hh += 8 * gridDim.y) {
-    const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
-    float v[V];
-    static_assert(V == 2 || V == 4, "head size 64 or 128");
+  // one head per warp, two heads per pass with their loads issued together;
+  // short sequences spread a token's heads over gridDim.y CTAs
+  static_assert(V == 2 || V == 4, "head size 64 or 128");
+  const int hstride = 8 * gridDim.y;
+  const size_t trow = static_cast<size_t>(t < T ? t : 0) * nqkv;  // rows t >= T stay zero
+  for (int hh0 = blockIdx.y * 8 + warp; hh0 < heads; hh0 += 2 * hstride) {
+    float vv[2][V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = 0.f;
-    if (t < T) {  // V consecutive values per lane, split planes added in order
-      for (int s = 0; s < nsplit; ++s) {
-        const float* src = planes + (static_cast<size_t>(s) * T + t) * nqkv + hh * HD + lane * V;
+    for (int u = 0; u < 2; ++u) {
+      const int hu = min(hh0 + u * hstride, heads - 1);
+      const float* src = planes + trow + hu * HD + lane * V;
+      if constexpr (V == 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(src);
+        vv[u][0] = a4.x; vv[u][1] = a4.y; vv[u][2] = a4.z; vv[u][3] = a4.w;
+      } else {
+        const float2 a2 = *reinterpret_cast<const float2*>(src);
+        vv[u][0] = a2.x; vv[u][1] = a2.y;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int hu = min(hh0 + u * hstride, heads - 1);
+      for (int s = 1; s < nsplit; ++s) {  // split planes added in order
+        const float* src = planes + static_cast<size_t>(s) * T * nqkv + trow + hu * HD + lane * V;
         if constexpr (V == 4) {
           const float4 a4 = *reinterpret_cast<const float4*>(src);
-          v[0] += a4.x; v[1] += a4.y; v[2] += a4.z; v[3] += a4.w;
+          vv[u][0] += a4.x; vv[u][1] += a4.y; vv[u][2] += a4.z; vv[u][3] += a4.w;
         } else {
           const float2 a2 = *reinterpret_cast<const float2*>(src);
-          v[0] += a2.x; v[1] += a2.y;
+          vv[u][0] += a2.x; vv[u][1] += a2.y;
         }
       }
 #pragma unroll
-      for (int i = 0; i < V; ++i) v[i] += bias[hh * HD + lane * V + i];
+      for (int i = 0; i < V; ++i) vv[u][i] = t < T ? vv[u][i] + bias[hu * HD + lane * V + i] : 0.f;
     }
-    if (t < T && kind < 2) {
-      const float* nw = kind == 0 ? qn : kn;
-      if (nw) {
-        float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < V; ++i) ss = fmaf(v[i], v[i], ss);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float r = sqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-        for (int i = 0; i < V; ++i) v[i] = (v[i] / r) * nw[lane * V + i];
-      }
-      if (half > 0) {
-#pragma unroll
-        for (int i = 0; i < V; ++i) sh[warp][lane * V + i] = v[i];
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const int d = lane * V + i;
-          if (d < rot) {
-            const int j = d < half ? d : d - half;
-            const float c = s_cos[j], sn = s_sin[j];
-            v[i] = d < half ? v[i] * c - sh[warp][d + half] * sn
-                            : v[i] * c + sh[warp][d - half] * sn;
+    for (int u = 0; u < 2; ++u) {
+      const int hh = hh0 + u * hstride;
+      if (hh >= heads) break;
+      float* v = vv[u];
+      const int kind = hh < nh ? 0 : (hh < nh + nkv ? 1 : 2);  // q, k, v
+      if (t < T && kind < 2) {
+        const float* nw = kind == 0 ? qn : kn;
+        if (nw) {
+          float ss = 0.f;
+  #pragma unroll
+          for (int i = 0; i < V; ++i) ss = fmaf(v[i], v[i], ss);
+  #pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          const float r = sqrtf(ss / static_cast<float>(HD) + eps);
+  #pragma unroll
+          for (int i = 0; i < V; ++i) v[i] = (v[i] / r) * nw[lane * V + i];
+        }
+        if (half > 0) {
+  #pragma unroll
+          for (int i = 0; i < V; ++i) sh[warp][lane * V + i] = v[i];
+          __syncwarp();
+  #pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const int d = lane * V + i;
+            if (d < rot) {
+              const int j = d < half ? d : d - half;
+              const float c = s_cos[j], sn = s_sin[j];
+              v[i] = d < half ? v[i] * c - sh[warp][d + half] * sn
+                              : v[i] * c + sh[warp][d - half] * sn;
+            }
           }
+          __syncwarp();
         }
-        __syncwarp();
       }
+      // q, k and v rows [head][tpad][HD] (v is transposed by attn_vt_kernel)
+      __half* dst = kind == 0 ? q16 + (static_cast<size_t>(hh) * tpad + t) * HD
+                  : kind == 1 ? k16 + (static_cast<size_t>(hh - nh) * tpad + t) * HD
+                              : v16 + (static_cast<size_t>(hh - nh - nkv) * tpad + t) * HD;
+      __half2 h2[V / 2];
+  #pragma unroll
+      for (int i = 0; i < V / 2; ++i) h2[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      if constexpr (V == 4) *reinterpret_cast<uint2*>(dst + lane * V) = *reinterpret_cast<uint2*>(h2);
+      else *reinterpret_cast<uint32_t*>(dst + lane * V) = *reinterpret_cast<uint32_t*>(h2);
     }
-    // q, k and v rows [head][tpad][HD] (v is transposed by attn_vt_kernel)
-    __half* dst = kind == 0 ? q16 + (static_cast<size_t>(hh) * tpad + t) * HD
-                : kind == 1 ? k16 + (static_cast<size_t>(hh - nh) * tpad + t) * HD
-                            : v16 + (static_cast<size_t>(hh - nh - nkv) * tpad + t) * HD;
-    __half2 h2[V / 2];
-#pragma unroll
-    for (int i = 0; i < V / 2; ++i) h2[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-    if constexpr (V == 4) *reinterpret_cast<uint2*>(dst + lane * V) = *reinterpret_cast<uint2*>(h2);
-    else *reinterpret_cast<uint32_t*>(dst + lane * V) = *reinterpret_cast<uint32_t*>(h2);
   }
 }
 
@@ -222,12 +245,17 @@ struct FaCfg {
   static constexpr int kK = kAttnTile * HD * 2;        // one K stage
   static constexpr int kVblk = HD * 128;               // one 64-key block of V^T (HD rows x 128 B)
   static constexpr int kV = 2 * kVblk;                 // one V^T stage (128 keys)
-  static constexpr int kP = kAttnTile * kAttnTile * 2; // P tile: 2 blocks of 64 keys
+  static constexpr int kXch = 2 * 2 * kAttnTile * 4;   // row-max / row-sum exchange [2][2][128]
   // at least 120 KiB, so that one CTA holds an SM (and all 512 TMEM columns) for
   // either head size: a second CTA would only wait in tcgen05.alloc
-  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + 2 * kP + 256;  // two P buffers
+  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + 256 + kXch;
   static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
-  static constexpr uint32_t kTmemCols = 512;           // S[2] at 0 / 128, O at 256
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM columns: S[2] at 0 / 128 (f32), O at 256 (HD f32), P[2] at 384 / 448
+  // (128 keys as f16 pairs, the A operand of P V)
+  static constexpr uint32_t kOCol = 2 * kAttnTile;
+  static constexpr uint32_t kPCol = 3 * kAttnTile;
+  static constexpr uint32_t kPCols = kAttnTile / 2;
 };
 
 struct FaArgs {
@@ -238,26 +266,42 @@ struct FaArgs {
   int* err;
 };
 
+// warps: 0 Q / K loads, 1 MMA issue, 2-9 softmax (two warpgroups: key columns
+// 0-63 and 64-127), 10 V loads
+constexpr int kFaSoftmaxThreads = 256;
+constexpr int kFaThreads = 64 + kFaSoftmaxThreads + 32;
+
+// 2^x on the special-function unit, subnormal results flushed to zero (P is
+// rounded to f16 afterwards, whose smallest subnormal is 2^-24)
+MOE_DEV float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant__ FaArgs args) {
+__global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_constant__ FaArgs args) {
   using C = FaCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + C::kQ;
   uint8_t* sV = sK + 2 * C::kK;
-  uint8_t* sP = sV + 2 * C::kV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::kP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * C::kV);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;    // [2] P buffer b written (tiles j with j % 2 == b)
-  uint64_t* o_done = bars + 11;   // [2] P V of a tile on buffer b finished
-  uint64_t* mma_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;    // [2] K ring (freed when S = Q K^T completes)
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2] V^T ring (freed when P V completes)
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_free = bars + 11;   // [2]
+  uint64_t* p_full = bars + 13;   // [2] P buffer b written (tiles j with j % 2 == b)
+  uint64_t* o_done = bars + 15;   // [2] P V of a tile on buffer b finished
+  uint64_t* mma_done = bars + 17;
+  uint64_t* xch_full = bars + 18; // [2] both halves' partial row max (row sum at the end) written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xch = reinterpret_cast<float*>(bars + 32);  // [parity][half][query row]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = args.nqt - 1 - static_cast<int>(blockIdx.x);  // long (late) tiles first
@@ -269,14 +313,15 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&kv_full[b], 1);
-      mbar_init(&kv_empty[b], 1);
+      mbar_init(&k_full[b], 1);
+      mbar_init(&k_empty[b], 1);
+      mbar_init(&v_full[b], 1);
+      mbar_init(&v_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&p_full[b], 128);
+      mbar_init(&s_free[b], kFaSoftmaxThreads);
+      mbar_init(&p_full[b], kFaSoftmaxThreads);
       mbar_init(&o_done[b], 1);
+      mbar_init(&xch_full[b], kFaSoftmaxThreads);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -296,46 +341,57 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------------------ TMA producers
+    // warp 0: Q, then K tiles; warp 10: V^T tiles.  A K stage is free as soon as
+    // its S completes, so the next K tiles load while the softmax still runs.
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, C::kQ);
+      const bool kside = warp == 0;
+      if (kside) {
+        mbar_arrive_expect_tx(q_full, C::kQ);
 #pragma unroll
-      for (int kb = 0; kb < HD / 64; ++kb)
-        tma_load_2d(sQ + kb * 16384, &args.tq, kb * 64, h * args.tpad + q0, q_full);
+        for (int kb = 0; kb < HD / 64; ++kb)
+          tma_load_2d(sQ + kb * 16384, &args.tq, kb * 64, h * args.tpad + q0, q_full);
+      }
+      uint64_t* full = kside ? k_full : v_full;
+      uint64_t* empty = kside ? k_empty : v_empty;
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
         const int s = j & 1;
-        if (!mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
+        if (!mbar_wait_bounded(&empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_EMPTY);
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+        if (kside) {
+          mbar_arrive_expect_tx(&full[s], C::kK);
 #pragma unroll
-        for (int kb = 0; kb < HD / 64; ++kb)
-          tma_load_2d(sK + s * C::kK + kb * 16384, &args.tk, kb * 64, kvh * args.tpad + j * kAttnTile,
-                      &kv_full[s]);
+          for (int kb = 0; kb < HD / 64; ++kb)
+            tma_load_2d(sK + s * C::kK + kb * 16384, &args.tk, kb * 64, kvh * args.tpad + j * kAttnTile,
+                        &full[s]);
+        } else {
+          mbar_arrive_expect_tx(&full[s], C::kV);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-          tma_load_2d(sV + s * C::kV + kb * C::kVblk, &args.tv, j * kAttnTile + kb * 64, kvh * HD,
-                      &kv_full[s]);
+          for (int kb = 0; kb < 2; ++kb)
+            tma_load_2d(sV + s * C::kV + kb * C::kVblk, &args.tv, j * kAttnTile + kb * 64, kvh * HD,
+                        &full[s]);
+        }
         issued = j + 1;
       }
       // every copy this thread started must land before the CTA exits
-      mbar_wait_drain(q_full, 0);
-      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) mbar_wait_drain(&kv_full[j & 1], (j >> 1) & 1);
+      if (kside) mbar_wait_drain(q_full, 0);
+      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) mbar_wait_drain(&full[j & 1], (j >> 1) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc_s = idesc_f16_f32(kAttnTile, kAttnTile);
       const uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD);
-      const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
+      const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait_bounded(&k_full[s], (j >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
 #pragma unroll
@@ -345,6 +401,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
                      sw128_desc(ak + s * C::kK + kb * 16384 + kk * 32), idesc_s, k > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[s]);
+        tc_commit(&k_empty[s]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -353,21 +410,24 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
           ok = false;
           break;
         }
-        if (!mbar_wait_bounded(&p_full[j & 1], (j >> 1) & 1, abort_flag)) {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&p_full[j & 1], (j >> 1) & 1, abort_flag) ||
+            !mbar_wait_bounded(&v_full[s], (j >> 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int s = j & 1;
+        // O += P V with P (128 queries x 128 keys, f16) read from TMEM
+        const uint32_t pa = tmem_base + C::kPCol + (j & 1) * C::kPCols;
 #pragma unroll
         for (int k = 0; k < kAttnTile / 16; ++k) {
           const int kb = k >> 2, kk = k & 3;
-          tc_mma_f16(tmem_base + 2 * kAttnTile, sw128_desc(ap + (j & 1) * C::kP + kb * 16384 + kk * 32),
-                     sw128_desc(av + s * C::kV + kb * C::kVblk + kk * 32), idesc_o,
-                     (j > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem_base + C::kOCol, pa + k * 8,
+                        sw128_desc(av + s * C::kV + kb * C::kVblk + kk * 32), idesc_o,
+                        (j > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&o_done[j & 1]);
-        tc_commit(&kv_empty[s]);
+        tc_commit(&v_empty[s]);
       }
       if (!ok) {
         *abort_flag = 1;
@@ -377,11 +437,29 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       mbar_wait_drain(mma_done, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 2-5)
-    const int qrow = (warp & 3) * 32 + lane;  // TMEM lane = query row of the tile
+    // ------------------------------------------------------------ softmax (warps 2-9)
+    // warps 2-5 take key columns 0-63 and O columns [0, HD/2); warps 6-9 the other
+    // halves; a warp reaches TMEM lanes 32 * (warp % 4) .. + 31, one query row each
+    constexpr int kH = kAttnTile / 2;  // keys per half
+    const int half = (warp - 2) >> 2;
+    const int qrow = (warp & 3) * 32 + lane;
     const int qi = q0 + qrow;
     const uint32_t lbase = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t ocol = 2 * kAttnTile;
+    const uint32_t scol = half * kH;
+    const uint32_t ocol = C::kOCol + half * (HD / 2);
+    float* my_x = xch + half * kAttnTile + qrow;              // + parity * 2 * kAttnTile
+    const float* peer_x = xch + (half ^ 1) * kAttnTile + qrow;
+    // partner exchange of one float per row through shared memory, parity
+    // buffered: tile j's values are overwritten only by tile j + 2's, which no
+    // thread writes before both halves have read tile j + 1's
+    auto exchange = [&](int j, float v, float* out) -> bool {
+      my_x[(j & 1) * 2 * kAttnTile] = v;
+      mbar_arrive(&xch_full[j & 1]);
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&xch_full[j & 1], (j >> 1) & 1, abort_flag)))
+        return false;
+      *out = peer_x[(j & 1) * 2 * kAttnTile];
+      return true;
+    };
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkt; ++j) {
@@ -391,28 +469,37 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         break;
       }
       tc_fence_after();
-      float sc[kAttnTile];
+      float sc[kH];
 #pragma unroll
-      for (int c = 0; c < kAttnTile / 32; ++c) {
+      for (int c = 0; c < kH / 32; ++c) {
         float part[32];
-        tmem_ld32(lbase + s * kAttnTile + c * 32, part);
+        tmem_ld32(lbase + s * kAttnTile + scol + c * 32, part);
 #pragma unroll
         for (int i = 0; i < 32; ++i) sc[c * 32 + i] = part[i];
       }
       // S is in registers: the MMA may overwrite this buffer with tile j + 2
       tc_fence_before();
       mbar_arrive(&s_free[s]);
-      const bool diag = j == qt;  // keys after the query are masked (causal)
-      float mx = -INFINITY;
+      if (j == qt) {  // diagonal tile: keys after the query are masked (causal)
 #pragma unroll
-      for (int c = 0; c < kAttnTile; ++c) {
-        if (diag && c > qrow) sc[c] = -INFINITY;
-        mx = fmaxf(mx, sc[c]);
+        for (int c = 0; c < kH; ++c)
+          if (half * kH + c > qrow) sc[c] = -INFINITY;
       }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kH; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      float mx_peer;
+      if (!exchange(j, mx, &mx_peer)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, mx_peer);
       // m is the max the exponentials in O and l refer to; it moves (and O and l are
       // rescaled) only when the row max grows by more than 2^8 in exp2 units, so
       // most tiles need neither the rescale nor to wait for the previous P V; P then
-      // holds values up to 256, well inside f16
+      // holds values up to 256, well inside f16.  Both halves of a row see the
+      // same m, mx and so the same decision.
       const float m_cand = fmaxf(m, mx);  // finite: key 0 is never masked
       const bool grow = (m_cand - m) * args.scale_log2 > 8.f;  // always on the first tile
       float alpha = 1.f;
@@ -420,13 +507,14 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         alpha = exp2f((m - m_cand) * args.scale_log2);
         m = m_cand;
       }
-      float rs = 0.f;
+      const float ms = m * args.scale_log2;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < kAttnTile; ++c) {
-        sc[c] = exp2f((sc[c] - m) * args.scale_log2);
-        rs += sc[c];
+      for (int c = 0; c < kH; ++c) {
+        sc[c] = ex2_ftz(fmaf(sc[c], args.scale_log2, -ms));
+        rs4[c & 3] += sc[c];
       }
-      l = l * alpha + rs;
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O must be complete up to tile j - 1 before it is rescaled
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1,
@@ -436,7 +524,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < HD / 16; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           float o[16];
           tmem_ld16(lbase + ocol + c * 16, o);
 #pragma unroll
@@ -450,38 +538,39 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
           ok = false;
           break;
         }
+        tc_fence_after();
       }
-      uint8_t* sPj = sP + (j & 1) * C::kP;
-      // P row -> the 128-byte-swizzled K-major A operand (chunk c of row r at c ^ (r & 7))
+      // this half's 64 keys -> 32 TMEM columns of f16 pairs (even key in the low half)
+      uint32_t pk[kH / 2];
 #pragma unroll
-      for (int cb = 0; cb < kAttnTile / 8; ++cb) {
-        __half2 hp[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) hp[i] = __floats2half2_rn(sc[cb * 8 + 2 * i], sc[cb * 8 + 2 * i + 1]);
-        const int blk = cb >> 3, ch = cb & 7;
-        *reinterpret_cast<uint4*>(sPj + blk * 16384 + qrow * 128 + ((ch ^ (qrow & 7)) << 4)) =
-            *reinterpret_cast<uint4*>(hp);
+      for (int i = 0; i < kH / 2; ++i) {
+        const __half2 hp = __floats2half2_rn(sc[2 * i], sc[2 * i + 1]);
+        pk[i] = *reinterpret_cast<const uint32_t*>(&hp);
       }
-      fence_proxy_async_smem();
+      tmem_st32_nowait(lbase + C::kPCol + (j & 1) * C::kPCols + half * (kH / 2), pk);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
     }
+    float l_peer = 0.f;
+    if (ok && !exchange(nkt, l, &l_peer)) ok = false;
     if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1,
                                                           abort_flag)))
       ok = false;
     if (ok) {
       tc_fence_after();
-      const float inv = 1.0f / l;
+      const float inv = 1.0f / (half == 0 ? l + l_peer : l_peer + l);
       const int ld = args.nh * HD;
 #pragma unroll
-      for (int c = 0; c < HD / 16; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         float o[16];
         tmem_ld16(lbase + ocol + c * 16, o);
         __half2 hv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) hv[i] = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
         if (qi < args.T) {
-          uint4* dst = reinterpret_cast<uint4*>(args.out16 + static_cast<size_t>(qi) * ld + h * HD + c * 16);
+          uint4* dst = reinterpret_cast<uint4*>(args.out16 + static_cast<size_t>(qi) * ld + h * HD +
+                                                half * (HD / 2) + c * 16);
           dst[0] = *reinterpret_cast<uint4*>(&hv[0]);
           dst[1] = *reinterpret_cast<uint4*>(&hv[4]);
         }
@@ -577,7 +666,7 @@ static cudaError_t attn_launch(const AttnPlan& a, const AttnWs& w, char* ws, con
     if (st != cudaSuccess) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  MOE_PDL(attn_fwd_kernel<HD>, dim3(fa.nqt, a.nh), dim3(192), smem, s, fa);
+  MOE_PDL(attn_fwd_kernel<HD>, dim3(fa.nqt, a.nh), dim3(kFaThreads), smem, s, fa);
   MOE_CUDA_RET(launch_dense_gemm(a.tm_o, a.H, a.nout, reinterpret_cast<const __half*>(ws + w.o16), T,
                                  reinterpret_cast<float*>(ws + w.oplanes), w.s2, a.d_err, a.num_sms, s));
   const size_t n = static_cast<size_t>(T) * a.H;

@@ -938,17 +938,24 @@ cudaError_t launch_router_gemm(const Plan& p, const WsLayout& L, char* ws, int T
 // K-split s partial of sum_k A[r][k] * B[t][k], A = `a_map` (m_rows x K, f16,
 // 64 x 128 boxes), B = b (T x K f16, row-major).  The caller adds the planes in
 // split order (the attention projections fold that sum into their next kernel).
+// The split count minimises a simple time model: the larger of the tensor work
+// (~1.25 PFLOP/s) and the weight stream (~6.5 TB/s), divided by the fraction of
+// SM-rounds the tiles fill, plus each extra plane written and read back once.
 int dense_gemm_splits(int m_rows, int T, int K, int num_sms) {
   const int units = ((m_rows + kBM - 1) / kBM) * ((T + 255) / 256);
   const int nk = (K + kBK - 1) / kBK;
+  const double flops_s = 2.0 * m_rows * T * K / 1.25e15;
+  const double weights_s = 2.0 * m_rows * K / 6.5e12;
+  const double plane_s = 8.0 * m_rows * T / 6.5e12;
   int best = 1;
-  double best_eff = 0.0;
+  double best_s = 0.0;
   for (int sp = 1; sp <= kRouterMaxSplit && nk / sp >= 8; ++sp) {
     const int u = units * sp;
     const int rounds = (u + num_sms - 1) / num_sms;
     const double eff = static_cast<double>(u) / (static_cast<double>(rounds) * num_sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
+    const double t_s = std::max(flops_s, weights_s) / eff + (sp - 1) * plane_s;
+    if (sp == 1 || t_s < 0.98 * best_s) {
+      best_s = t_s;
       best = sp;
     }
   }
