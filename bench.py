@@ -756,6 +756,9 @@ def run_ours(args) -> None:  # noqa: ANN001
     if world > 1:
         run_ep(args, world, rank, local)
         return
+    if args.only_attention:  # profiling aid: the attention block only
+        print(json.dumps({"attention": run_attention(args, local, _peaks()[0], _tc_peak())}))
+        return
     if args.only_other:  # profiling aid: BASELINE configs 2 and 3 only
         print(json.dumps({"other_configs": run_other_configs(args, local, world, _peaks()[0],
                                                               _tc_peak())}))
@@ -951,6 +954,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
     ap.add_argument("--only-other", action="store_true",
                     help="only BASELINE configs 2 and 3 (profiling aid)")
+    ap.add_argument("--only-attention", action="store_true",
+                    help="only the GLM-4.7-shape attention block (profiling aid)")
     ap.add_argument("--other-tokens", default="",
                     help="comma-separated batch sizes: run configs 2 and 3 only at these")
     ap.add_argument("--no-other", action="store_true",
