@@ -195,6 +195,11 @@ class MoeLayer:
         """A reusable end-to-end step over fixed pinned host buffers (see HostRunner)."""
         return HostRunner(self, x_pinned, out_pinned)
 
+    def host_pipeline(self, tokens: int, depth: int = 2) -> "HostPipeline":
+        """Steps from pinned host memory with their copies overlapping the neighbouring
+        steps' compute (see HostPipeline)."""
+        return HostPipeline(self, tokens, depth)
+
     def _staging(self, tokens: int) -> tuple[Any, Any, Any, Any]:
         torch = _torch()
         cap = self._pinned.get("cap", 0)
@@ -304,3 +309,86 @@ class HostRunner:
         self._graph.replay()
         torch.cuda.current_stream(self._din.device).synchronize()
         return self.out
+
+
+class HostPipeline:
+    """Layer steps from pinned host memory, copies overlapped with compute.
+
+    A serving loop that submits one batch per step: ``depth`` slots, each with its
+    own pinned input / output buffers (``x[s]``, ``out[s]``) and device copies.
+    ``submit(i)`` queues step i on slot ``i % depth``: the input copy on an H2D
+    stream, the layer (one CUDA graph per slot, captured at construction) on a
+    compute stream once that copy lands, and the output copy on a D2H stream once
+    the layer finishes.  ``wait(i)`` blocks until step i's output is in
+    ``out[i % depth]``.  So while step i computes, step i + 1's input and step
+    i - 1's output cross PCIe (in opposite directions).  A slot's device input is
+    refilled only after the layer that read it finished, and its device output
+    rewritten only after the copy that read it finished.  The caller fills ``x[s]`` for step i only after
+    ``wait(i - depth)`` returned (or before the first ``depth`` submits) and reads
+    ``out[s]`` after ``wait(i)``.  The slots share one workspace: steps compute
+    one after another on the compute stream.
+    """
+
+    def __init__(self, layer: MoeLayer, tokens: int, depth: int = 2) -> None:
+        torch = _torch()
+        if not 0 < tokens <= layer.cfg.max_tokens:
+            raise ValueError("tokens outside (0, max_tokens]")
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        dev = torch.device(f"cuda:{layer.cfg.device}")
+        h = layer.cfg.hidden
+        self.layer, self.tokens, self.depth = layer, tokens, depth
+        self.x = [torch.zeros((tokens, h), dtype=torch.float32, pin_memory=True) for _ in range(depth)]
+        self.out = [torch.empty((tokens, h), dtype=torch.float32, pin_memory=True) for _ in range(depth)]
+        self._din = [torch.zeros((tokens, h), dtype=torch.float32, device=dev) for _ in range(depth)]
+        self._dout = [torch.empty((tokens, h), dtype=torch.float32, device=dev) for _ in range(depth)]
+        self._ws = torch.empty(max(layer.workspace_bytes(tokens), 256), dtype=torch.uint8, device=dev)
+        self._h2d = torch.cuda.Stream(device=dev)
+        self._d2h = torch.cuda.Stream(device=dev)
+        self._comp = torch.cuda.Stream(device=dev)
+        self._ev_in = [torch.cuda.Event() for _ in range(depth)]
+        self._ev_out = [torch.cuda.Event() for _ in range(depth)]
+        self._ev_done = [torch.cuda.Event() for _ in range(depth)]
+        self._graphs = []
+        for s in range(depth):  # one uncaptured step per slot, then its graph
+            with torch.cuda.stream(self._comp):
+                self._forward(s)
+            self._comp.synchronize()
+            layer.status(self._comp)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self._comp):
+                self._forward(s)
+            self._graphs.append(g)
+        torch.cuda.synchronize(dev)
+
+    def _forward(self, s: int) -> None:
+        self.layer.forward_ptr(self._din[s].data_ptr(), self._dout[s].data_ptr(), self.tokens,
+                               self._ws.data_ptr(), self._ws.numel())
+
+    def submit(self, step: int) -> None:
+        """Queue step ``step`` (input from ``x[step % depth]``); returns at once."""
+        torch = _torch()
+        s = step % self.depth
+        self._h2d.wait_event(self._ev_out[s])  # the slot's previous layer read its input
+        with torch.cuda.stream(self._h2d):
+            self._din[s].copy_(self.x[s], non_blocking=True)
+            self._ev_in[s].record(self._h2d)
+        self._comp.wait_event(self._ev_in[s])
+        self._comp.wait_event(self._ev_done[s])  # the slot's previous output was copied out
+        with torch.cuda.stream(self._comp):
+            self._graphs[s].replay()
+        self._ev_out[s].record(self._comp)
+        self._d2h.wait_event(self._ev_out[s])
+        with torch.cuda.stream(self._d2h):
+            self.out[s].copy_(self._dout[s], non_blocking=True)
+            self._ev_done[s].record(self._d2h)
+
+    def wait(self, step: int) -> Any:
+        """Block until step ``step``'s output is in ``out[step % depth]``; returns it."""
+        s = step % self.depth
+        self._ev_done[s].synchronize()
+        return self.out[s]
+
+    def status(self) -> None:
+        """Synchronise and raise if a kernel reported a device-side error or timeout."""
+        self.layer.status(self._comp)

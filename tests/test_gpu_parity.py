@@ -155,6 +155,22 @@ def test_host_buffers_end_to_end() -> None:
     np.testing.assert_array_equal(runner().numpy(), ml.forward_host(x_pin.numpy()))
     ml.status()
     del runner
+    # the pipelined serving loop: distinct batches through two slots, each output
+    # read after its wait and equal to the one-step forward of that batch
+    pipe = ml.host_pipeline(x.shape[0], depth=2)
+    batches = [x * (1.0 + 0.25 * i) for i in range(5)]
+    pipe.x[0].copy_(torch.from_numpy(batches[0]))
+    pipe.x[1].copy_(torch.from_numpy(batches[1]))
+    for i in range(len(batches)):
+        pipe.submit(i)
+        if i >= 1:
+            got = pipe.wait(i - 1).numpy().copy()
+            np.testing.assert_array_equal(got, ml.forward_host(batches[i - 1]))
+            if i + 1 < len(batches):  # slot (i - 1) % 2 is free again: next batch
+                pipe.x[(i + 1) % 2].copy_(torch.from_numpy(batches[i + 1]))
+    np.testing.assert_array_equal(pipe.wait(len(batches) - 1).numpy(), ml.forward_host(batches[-1]))
+    pipe.status()
+    del pipe
     ml.close()
 
 
