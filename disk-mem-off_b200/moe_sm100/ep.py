@@ -106,6 +106,17 @@ class ExpertParallelMoe:
             if small_exchange == "p2p":
                 ops.p2p_setup(self.cap, group)
 
+    def host_pipeline(self, tokens: int, depth: int = 2) -> Any:
+        """Steps from pinned host memory with their copies overlapping the neighbouring
+        steps' compute (``layer.HostPipeline``).  The step is this rank's forward,
+        issued each step (not captured); every rank submits the same steps in order."""
+        from .layer import HostPipeline
+
+        def step(din: Any, dout: Any) -> None:
+            dout.copy_(self.forward(din))
+        return HostPipeline(step, tokens, self.ops.cfg.hidden, self.ops.cfg.device, depth,
+                            graph=False, check=self.ops.status)
+
     def forward(self, x: Any, timed: bool = False) -> Any:
         torch = _torch()
         ev = {}

@@ -197,8 +197,17 @@ class MoeLayer:
 
     def host_pipeline(self, tokens: int, depth: int = 2) -> "HostPipeline":
         """Steps from pinned host memory with their copies overlapping the neighbouring
-        steps' compute (see HostPipeline)."""
-        return HostPipeline(self, tokens, depth)
+        steps' compute (see HostPipeline); each slot's layer step is one CUDA graph."""
+        torch = _torch()
+        if not 0 < tokens <= self.cfg.max_tokens:
+            raise ValueError("tokens outside (0, max_tokens]")
+        dev = torch.device(f"cuda:{self.cfg.device}")
+        ws = torch.empty(max(self.workspace_bytes(tokens), 256), dtype=torch.uint8, device=dev)
+
+        def step(din: Any, dout: Any) -> None:  # the slots share ws: steps run in order
+            self.forward_ptr(din.data_ptr(), dout.data_ptr(), tokens, ws.data_ptr(), ws.numel())
+        return HostPipeline(step, tokens, self.cfg.hidden, self.cfg.device, depth, graph=True,
+                            check=self.status, keep=(ws,))
 
     def _staging(self, tokens: int) -> tuple[Any, Any, Any, Any]:
         torch = _torch()
@@ -317,32 +326,35 @@ class HostPipeline:
     A serving loop that submits one batch per step: ``depth`` slots, each with its
     own pinned input / output buffers (``x[s]``, ``out[s]``) and device copies.
     ``submit(i)`` queues step i on slot ``i % depth``: the input copy on an H2D
-    stream, the layer (one CUDA graph per slot, captured at construction) on a
-    compute stream once that copy lands, and the output copy on a D2H stream once
+    stream, the layer step (``step(din, dout)`` on a compute stream; with
+    ``graph=True`` one CUDA graph per slot, captured at construction after one
+    uncaptured run) once that copy lands, and the output copy on a D2H stream once
     the layer finishes.  ``wait(i)`` blocks until step i's output is in
     ``out[i % depth]``.  So while step i computes, step i + 1's input and step
     i - 1's output cross PCIe (in opposite directions).  A slot's device input is
     refilled only after the layer that read it finished, and its device output
-    rewritten only after the copy that read it finished.  The caller fills ``x[s]`` for step i only after
-    ``wait(i - depth)`` returned (or before the first ``depth`` submits) and reads
-    ``out[s]`` after ``wait(i)``.  The slots share one workspace: steps compute
-    one after another on the compute stream.
+    rewritten only after the copy that read it finished.  The caller fills
+    ``x[s]`` for step i only after ``wait(i - depth)`` returned (or before the
+    first ``depth`` submits) and reads ``out[s]`` after ``wait(i)``.  Steps compute
+    one after another on the compute stream, so they may share a workspace.
     """
 
-    def __init__(self, layer: MoeLayer, tokens: int, depth: int = 2) -> None:
+    def __init__(self, step: Any, tokens: int, hidden: int, device: int, depth: int = 2,
+                 graph: bool = True, check: Any = None, keep: tuple = ()) -> None:
         torch = _torch()
-        if not 0 < tokens <= layer.cfg.max_tokens:
-            raise ValueError("tokens outside (0, max_tokens]")
-        if depth < 1:
-            raise ValueError("depth must be >= 1")
-        dev = torch.device(f"cuda:{layer.cfg.device}")
-        h = layer.cfg.hidden
-        self.layer, self.tokens, self.depth = layer, tokens, depth
-        self.x = [torch.zeros((tokens, h), dtype=torch.float32, pin_memory=True) for _ in range(depth)]
-        self.out = [torch.empty((tokens, h), dtype=torch.float32, pin_memory=True) for _ in range(depth)]
-        self._din = [torch.zeros((tokens, h), dtype=torch.float32, device=dev) for _ in range(depth)]
-        self._dout = [torch.empty((tokens, h), dtype=torch.float32, device=dev) for _ in range(depth)]
-        self._ws = torch.empty(max(layer.workspace_bytes(tokens), 256), dtype=torch.uint8, device=dev)
+        if tokens <= 0 or depth < 1:
+            raise ValueError("tokens and depth must be positive")
+        dev = torch.device(f"cuda:{device}")
+        self.tokens, self.depth = tokens, depth
+        self._step, self._check, self._keep = step, check, keep
+        self.x = [torch.zeros((tokens, hidden), dtype=torch.float32, pin_memory=True)
+                  for _ in range(depth)]
+        self.out = [torch.empty((tokens, hidden), dtype=torch.float32, pin_memory=True)
+                    for _ in range(depth)]
+        self._din = [torch.zeros((tokens, hidden), dtype=torch.float32, device=dev)
+                     for _ in range(depth)]
+        self._dout = [torch.empty((tokens, hidden), dtype=torch.float32, device=dev)
+                      for _ in range(depth)]
         self._h2d = torch.cuda.Stream(device=dev)
         self._d2h = torch.cuda.Stream(device=dev)
         self._comp = torch.cuda.Stream(device=dev)
@@ -350,20 +362,17 @@ class HostPipeline:
         self._ev_out = [torch.cuda.Event() for _ in range(depth)]
         self._ev_done = [torch.cuda.Event() for _ in range(depth)]
         self._graphs = []
-        for s in range(depth):  # one uncaptured step per slot, then its graph
-            with torch.cuda.stream(self._comp):
-                self._forward(s)
-            self._comp.synchronize()
-            layer.status(self._comp)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=self._comp):
-                self._forward(s)
-            self._graphs.append(g)
+        if graph:
+            for s in range(depth):  # one uncaptured step per slot, then its graph
+                with torch.cuda.stream(self._comp):
+                    step(self._din[s], self._dout[s])
+                self._comp.synchronize()
+                self.status()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self._comp):
+                    step(self._din[s], self._dout[s])
+                self._graphs.append(g)
         torch.cuda.synchronize(dev)
-
-    def _forward(self, s: int) -> None:
-        self.layer.forward_ptr(self._din[s].data_ptr(), self._dout[s].data_ptr(), self.tokens,
-                               self._ws.data_ptr(), self._ws.numel())
 
     def submit(self, step: int) -> None:
         """Queue step ``step`` (input from ``x[step % depth]``); returns at once."""
@@ -376,7 +385,10 @@ class HostPipeline:
         self._comp.wait_event(self._ev_in[s])
         self._comp.wait_event(self._ev_done[s])  # the slot's previous output was copied out
         with torch.cuda.stream(self._comp):
-            self._graphs[s].replay()
+            if self._graphs:
+                self._graphs[s].replay()
+            else:
+                self._step(self._din[s], self._dout[s])
         self._ev_out[s].record(self._comp)
         self._d2h.wait_event(self._ev_out[s])
         with torch.cuda.stream(self._d2h):
@@ -391,4 +403,6 @@ class HostPipeline:
 
     def status(self) -> None:
         """Synchronise and raise if a kernel reported a device-side error or timeout."""
-        self.layer.status(self._comp)
+        self._comp.synchronize()
+        if self._check is not None:
+            self._check()

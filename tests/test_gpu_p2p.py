@@ -76,6 +76,26 @@ def test_peer_exchange_single_rank_matches_forward(one_rank_group, family: str, 
         ep.forward(torch.randn((7, 2048), generator=gen, device="cuda"), timed=True)
         assert ep.last_timing["exchanged_rows"] == 32
         assert 0 < ep.last_timing["recv_rows"] <= 7 * 8
+        # the pipelined serving loop through the same exchange: batches on two slots,
+        # each output as the single-GPU forward of its batch
+        pipe = ep.host_pipeline(24, depth=2)
+        xs = [torch.randn((24, 2048), generator=gen, device="cuda") for _ in range(4)]
+        pipe.x[0].copy_(xs[0])
+        pipe.x[1].copy_(xs[1])
+        for i in range(len(xs)):
+            pipe.submit(i)
+            if i >= 1:
+                got = pipe.wait(i - 1).clone()
+                if i + 1 < len(xs):
+                    pipe.x[(i + 1) % 2].copy_(xs[i + 1])
+                ref = full.forward(xs[i - 1]).cpu()
+                err = float((got.double() - ref.double()).norm() / ref.double().norm())
+                assert err <= TOL, (family, fmt, "pipeline", i - 1, err)
+        got = pipe.wait(len(xs) - 1).clone()
+        ref = full.forward(xs[-1]).cpu()
+        assert float((got.double() - ref.double()).norm() / ref.double().norm()) <= TOL
+        pipe.status()
+        full.status()
     finally:
         ops.close()
         full.close()
