@@ -85,6 +85,18 @@ static AttnWs attn_ws(const AttnPlan& a, int T) {
   return w;
 }
 
+// V consecutive floats (V = 2 or 4, 8- or 16-byte aligned) in one load
+template <int V>
+MOE_DEV void load_vec(const float* __restrict__ p, float (&out)[V]) {
+  if constexpr (V == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  } else {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    out[0] = a.x; out[1] = a.y;
+  }
+}
+
 // ------------------------------------------------------------------ q / k / v
 // One CTA per (padded) token, a warp per head vector.  Sums the GEMM's K-split
 // planes in split order, adds the bias, applies the per-head RMS norm
@@ -147,8 +159,10 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
           vv[u][0] += a2.x; vv[u][1] += a2.y;
         }
       }
+      float bb[V];
+      load_vec<V>(bias + hu * HD + lane * V, bb);
 #pragma unroll
-      for (int i = 0; i < V; ++i) vv[u][i] = t < T ? vv[u][i] + bias[hu * HD + lane * V + i] : 0.f;
+      for (int i = 0; i < V; ++i) vv[u][i] = t < T ? vv[u][i] + bb[i] : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -160,29 +174,44 @@ __global__ void __launch_bounds__(256) attn_qkv_kernel(
         const float* nw = kind == 0 ? qn : kn;
         if (nw) {
           float ss = 0.f;
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < V; ++i) ss = fmaf(v[i], v[i], ss);
-  #pragma unroll
+#pragma unroll
           for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-          const float r = sqrtf(ss / static_cast<float>(HD) + eps);
-  #pragma unroll
-          for (int i = 0; i < V; ++i) v[i] = (v[i] / r) * nw[lane * V + i];
+          const float rinv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
+          float w[V];
+          load_vec<V>(nw + lane * V, w);
+#pragma unroll
+          for (int i = 0; i < V; ++i) v[i] = (v[i] * rinv) * w[i];
         }
         if (half > 0) {
-  #pragma unroll
-          for (int i = 0; i < V; ++i) sh[warp][lane * V + i] = v[i];
-          __syncwarp();
-  #pragma unroll
+          // rotate-half partner of dim d (d +- half): with half a multiple of V and
+          // half / V a power of two it sits in lane lane ^ (half / V), same slot
+          const int pl = half / V;
+          float pv[V];
+          if (half % V == 0 && (pl & (pl - 1)) == 0 && 2 * pl <= 32) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[i], pl);
+          } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i) sh[warp][lane * V + i] = v[i];
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              const int d = lane * V + i;
+              pv[i] = d < rot ? sh[warp][d < half ? d + half : d - half] : 0.f;
+            }
+            __syncwarp();
+          }
+#pragma unroll
           for (int i = 0; i < V; ++i) {
             const int d = lane * V + i;
             if (d < rot) {
               const int j = d < half ? d : d - half;
               const float c = s_cos[j], sn = s_sin[j];
-              v[i] = d < half ? v[i] * c - sh[warp][d + half] * sn
-                              : v[i] * c + sh[warp][d - half] * sn;
+              v[i] = d < half ? v[i] * c - pv[i] * sn : v[i] * c + pv[i] * sn;
             }
           }
-          __syncwarp();
         }
       }
       // q, k and v rows [head][tpad][HD] (v is transposed by attn_vt_kernel)
