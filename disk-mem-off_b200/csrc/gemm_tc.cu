@@ -108,17 +108,23 @@ __host__ __device__ constexpr int gemm_threads() {
 // the converter warps) and the MMA reads its A operand from there: no f16 copy of
 // A in shared memory, so a stage is only the int8 tile and the token tile and
 // more k-blocks of weights fit in flight per SM; the hand-off to the MMA is a
-// TMEM store and a barrier.  Prefill tiles keep A in shared memory (a 256-column
-// accumulator pair fills TMEM).
+// TMEM store and a barrier.  128-token tiles keep A in shared memory.
 #ifndef MOE_INT8_TMEM_A
 #define MOE_INT8_TMEM_A 1
 #endif
-template <int BN, bool INT8>
+// 256-token INT8 tiles take the TMEM A path too for the gate/up GEMM
+// (MOE_INT8_TMEM_A_PREFILL 1; 2: the down GEMM as well, 0: neither).  The A slots
+// then take half of TMEM, so one accumulator buffer and five 40 KiB stages
+// instead of two buffers and four 56 KiB stages: gate/up 1.219 -> 1.171 ms at
+// 4096 tokens (GLM-4.7 dims), but the down GEMM (24 k-blocks a tile) loses its
+// epilogue overlap, 0.676 -> 0.819 ms.
 #ifndef MOE_INT8_TMEM_A_PREFILL
-#define MOE_INT8_TMEM_A_PREFILL 0
+#define MOE_INT8_TMEM_A_PREFILL 1
 #endif
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr bool gemm_ts() {
-  return MOE_INT8_TMEM_A && INT8 && (BN <= 64 || (MOE_INT8_TMEM_A_PREFILL && BN == 256));
+  return MOE_INT8_TMEM_A && INT8 &&
+         (BN <= 64 || (BN == 256 && MOE_INT8_TMEM_A_PREFILL >= (DOWN ? 2 : 1)));
 }
 
 // As many stages as fit under the 227 KiB opt-in shared memory per CTA (less the
@@ -156,37 +162,38 @@ constexpr int kGemmSmemBudget = 232448 - 1024 - kGemmBarBytes - 512;
 #define MOE_INT8_DECODE_KPS_TS 4
 #endif
 
-template <int BN, bool INT8>
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr int gemm_kps() {
-  return gemm_ts<BN, INT8>() ? (BN <= 64 ? MOE_INT8_DECODE_KPS_TS : 1)
-                             : (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1;
+  return gemm_ts<BN, INT8, DOWN>() ? (BN <= 64 ? MOE_INT8_DECODE_KPS_TS : 1)
+                                   : (INT8 && BN <= 64) ? MOE_INT8_DECODE_KPS : 1;
 }
 
-template <int BN, bool INT8>
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr int gemm_stage_bytes() {
-  using C = TileCfg<BN, gemm_ts<BN, INT8>()>;
-  return gemm_kps<BN, INT8>() * (C::kStageA + C::kStageB + (INT8 ? C::kStageA8 : 0));
+  using C = TileCfg<BN, gemm_ts<BN, INT8, DOWN>()>;
+  return gemm_kps<BN, INT8, DOWN>() * (C::kStageA + C::kStageB + (INT8 ? C::kStageA8 : 0));
 }
 
-template <int BN, bool INT8>
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr int gemm_stages() {
-  constexpr int s = kGemmSmemBudget / gemm_stage_bytes<BN, INT8>();
-  constexpr int cap = gemm_ts<BN, INT8>() ? MOE_GEMM_MAX_STAGES_TS : MOE_GEMM_MAX_STAGES;
+  constexpr int s = kGemmSmemBudget / gemm_stage_bytes<BN, INT8, DOWN>();
+  constexpr int cap = gemm_ts<BN, INT8, DOWN>() ? MOE_GEMM_MAX_STAGES_TS : MOE_GEMM_MAX_STAGES;
   return s > cap ? cap : s;
 }
 
-// TMEM A slots (KPS k-blocks of 32 columns each) in the columns the two
+// TMEM A slots (KPS k-blocks of 32 columns each) in the columns the
 // accumulator buffers leave free.
-template <int BN, bool INT8>
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr int gemm_a_slots() {
-  using C = TileCfg<BN, gemm_ts<BN, INT8>()>;
-  return gemm_ts<BN, INT8>() ? (C::kTmemCols - C::kAColBase) / (32 * gemm_kps<BN, INT8>()) : 0;
+  using C = TileCfg<BN, gemm_ts<BN, INT8, DOWN>()>;
+  return gemm_ts<BN, INT8, DOWN>() ? (C::kTmemCols - C::kAColBase) / (32 * gemm_kps<BN, INT8, DOWN>())
+                                   : 0;
 }
 
-template <int BN, bool INT8>
+template <int BN, bool INT8, bool DOWN = false>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
   return 1024 /*align slack*/ +
-         static_cast<size_t>(gemm_stages<BN, INT8>()) * gemm_stage_bytes<BN, INT8>() +
+         static_cast<size_t>(gemm_stages<BN, INT8, DOWN>()) * gemm_stage_bytes<BN, INT8, DOWN>() +
          kGemmBarBytes;
 }
 
@@ -310,11 +317,11 @@ template <int BN, int MODE, bool INT8>
 __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
     moe_gemm_kernel(const __grid_constant__ GemmArgs args) {
   constexpr bool DOWN = MODE == MODE_DOWN;
-  constexpr int STAGES = gemm_stages<BN, INT8>();
-  constexpr int KPS = gemm_kps<BN, INT8>();  // k-blocks per stage
-  constexpr bool TS = gemm_ts<BN, INT8>();   // widened A operand in TMEM
+  constexpr int STAGES = gemm_stages<BN, INT8, DOWN>();
+  constexpr int KPS = gemm_kps<BN, INT8, DOWN>();  // k-blocks per stage
+  constexpr bool TS = gemm_ts<BN, INT8, DOWN>();   // widened A operand in TMEM
   using Cfg = TileCfg<BN, TS>;
-  constexpr int NA = gemm_a_slots<BN, INT8>();  // TMEM A slots (TS)
+  constexpr int NA = gemm_a_slots<BN, INT8, DOWN>();  // TMEM A slots (TS)
   constexpr int NCONV = TS ? NA : STAGES;       // "widened" barriers: per A slot or per stage
   // per k-block operand bytes; stage s holds k-blocks [s * KPS, s * KPS + KPS) of each buffer
   constexpr int SA = Cfg::kStageA, SB = Cfg::kStageB, SA8 = Cfg::kStageA8;
@@ -753,7 +760,7 @@ __global__ void __launch_bounds__(gemm_threads<BN, INT8>(), 1)
 // ------------------------------------------------------------------ launcher
 template <int BN, int MODE, bool INT8>
 static cudaError_t run_gemm(const GemmArgs& a, int grid, cudaStream_t s) {
-  constexpr size_t smem = gemm_smem_bytes<BN, INT8>();
+  constexpr size_t smem = gemm_smem_bytes<BN, INT8, MODE == MODE_DOWN>();
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
