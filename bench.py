@@ -276,6 +276,19 @@ def _gemm_flops(T: int, k: int, H: int, I: int, SI: int) -> tuple[float, float]:
     return gateup, down
 
 
+def _gemm_bytes(T: int, k: int, H: int, I: int, SI: int, unique: int, wbytes: int
+                ) -> tuple[float, float]:
+    """Algorithmic HBM bytes of the two grouped GEMMs: the touched experts' weights
+    (and the shared expert's) once, the token rows in and the activations / expert
+    outputs out (f16), the shared expert's output in fp32."""
+    rows, srows = T * k, (T if SI else 0)
+    gateup = (unique * 2 * I * H + 2 * SI * H) * wbytes + (rows + srows) * H * 2 \
+        + (rows * I + srows * SI) * 2
+    down = (unique * H * I + H * SI) * wbytes + (rows * I + srows * SI) * 2 + rows * H * 2 \
+        + srows * H * 4
+    return float(gateup), float(down)
+
+
 def _measure(ml, T: int, H: int, steps: int, warmup: int, world: int, gen) -> dict:  # noqa: ANN001
     import torch
     x = torch.randn((T, H), generator=gen, device="cuda")
@@ -339,11 +352,21 @@ def run_other_configs(args, local: int, world: int, hbm: float, tflops: float) -
             entry = {"tokens_per_s": world * T / (m["ms"] * 1e-3), "ms_per_step": m["ms"],
                      "stage_ms": m["stage"], "unique_experts": m["unique"],
                      "max_expert_load": m["max_load"]}
-            if T >= 1024:  # prefill: tensor-core bound
+            if T >= 1024:  # prefill
                 entry["tc_frac_gateup"] = fg / (m["stage"][1] * 1e-3) / 1e12 / tflops
                 entry["tc_frac_down"] = fd / (m["stage"][2] * 1e-3) / 1e12 / tflops
                 entry["tc_frac_layer"] = (fg + fd) / (m["ms"] * 1e-3) / 1e12 / tflops
                 entry["tflops_layer"] = (fg + fd) / (m["ms"] * 1e-3) / 1e12
+                # each GEMM against the larger of its tensor and HBM floors: with few
+                # tokens per expert (Qwen3 shape: ~160) the weights, not the FLOPs, bound it
+                bg, bd = _gemm_bytes(T, K, H, I, SI, m["unique"], wbytes)
+                for name_, fl, by, st in (("gateup", fg, bg, m["stage"][1]),
+                                          ("down", fd, bd, m["stage"][2])):
+                    t_tc, t_hbm = fl / (tflops * 1e12), by / (hbm * 1e9)
+                    entry[f"roofline_{name_}"] = {
+                        "bound": "tensor" if t_tc >= t_hbm else "hbm",
+                        "frac": max(t_tc, t_hbm) / (st * 1e-3),
+                        "flops": fl, "bytes": by, "launch_ms": st}
             else:  # decode: weight streaming
                 wb = (m["unique"] + 1) * 3 * H * I * wbytes
                 entry["layer_hbm_frac"] = wb / (m["ms"] * 1e-3) / 1e9 / hbm
