@@ -274,10 +274,11 @@ struct FaCfg {
   static constexpr int kK = kAttnTile * HD * 2;        // one K stage
   static constexpr int kVblk = HD * 128;               // one 64-key block of V^T (HD rows x 128 B)
   static constexpr int kV = 2 * kVblk;                 // one V^T stage (128 keys)
+  static constexpr int kKStages = 3;                   // K tiles for S two tiles ahead
   static constexpr int kXch = 2 * 2 * kAttnTile * 4;   // row-max / row-sum exchange [2][2][128]
   // at least 120 KiB, so that one CTA holds an SM (and all 512 TMEM columns) for
   // either head size: a second CTA would only wait in tcgen05.alloc
-  static constexpr size_t kUsed = 1024 + kQ + 2 * kK + 2 * kV + 256 + kXch;
+  static constexpr size_t kUsed = 1024 + kQ + kKStages * kK + 2 * kV + 256 + kXch;
   static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
   static constexpr uint32_t kTmemCols = 512;
   // TMEM columns: S[2] at 0 / 128 (f32), O at 256 (HD f32), P[2] at 384 / 448
@@ -315,20 +316,20 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + C::kQ;
-  uint8_t* sV = sK + 2 * C::kK;
+  uint8_t* sV = sK + C::kKStages * C::kK;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * C::kV);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;    // [2] K ring (freed when S = Q K^T completes)
-  uint64_t* k_empty = bars + 3;   // [2]
-  uint64_t* v_full = bars + 5;    // [2] V^T ring (freed when P V completes)
-  uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_free = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;   // [2] P buffer b written (tiles j with j % 2 == b)
-  uint64_t* o_done = bars + 15;   // [2] P V of a tile on buffer b finished
-  uint64_t* mma_done = bars + 17;
-  uint64_t* xch_full = bars + 18; // [2] both halves' partial row max (row sum at the end) written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* k_full = bars + 1;    // [kKStages] K ring (freed when S = Q K^T completes)
+  uint64_t* k_empty = bars + 4;   // [kKStages]
+  uint64_t* v_full = bars + 7;    // [2] V^T ring (freed when P V completes)
+  uint64_t* v_empty = bars + 9;   // [2]
+  uint64_t* s_full = bars + 11;   // [2]
+  uint64_t* s_free = bars + 13;   // [2]
+  uint64_t* p_full = bars + 15;   // [2] P buffer b written (tiles j with j % 2 == b)
+  uint64_t* o_done = bars + 17;   // [2] P V of a tile on buffer b finished
+  uint64_t* mma_done = bars + 19;
+  uint64_t* xch_full = bars + 20; // [2] both halves' partial row max (row sum at the end) written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(bars + 32);  // [parity][half][query row]
 
@@ -341,9 +342,12 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    static_assert(C::kKStages == 3, "barrier slots");
+    for (int b = 0; b < C::kKStages; ++b) {
       mbar_init(&k_full[b], 1);
       mbar_init(&k_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&v_full[b], 1);
       mbar_init(&v_empty[b], 1);
       mbar_init(&s_full[b], 1);
@@ -384,10 +388,11 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_co
       }
       uint64_t* full = kside ? k_full : v_full;
       uint64_t* empty = kside ? k_empty : v_empty;
+      const int nst = kside ? C::kKStages : 2;
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
+        const int s = j % nst;
+        if (!mbar_wait_bounded(&empty[s], ((j / nst) & 1) ^ 1, abort_flag)) {
           *abort_flag = 1;
           record_error(args.err, DEV_TIMEOUT_EMPTY);
           break;
@@ -409,7 +414,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_co
       }
       // every copy this thread started must land before the CTA exits
       if (kside) mbar_wait_drain(q_full, 0);
-      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) mbar_wait_drain(&full[j & 1], (j >> 1) & 1);
+      for (int j = issued - 1; j >= 0 && j >= issued - nst; --j) mbar_wait_drain(&full[j % nst], (j / nst) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -419,23 +424,26 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_fwd_kernel(const __grid_co
       const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&k_full[s], (j >> 1) & 1, abort_flag)) return false;
+        const int s = j & 1, sk = j % C::kKStages;
+        if (!mbar_wait_bounded(&k_full[sk], (j / C::kKStages) & 1, abort_flag)) return false;
         if (!mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const int kb = k >> 2, kk = k & 3;
           tc_mma_f16(tmem_base + s * kAttnTile, sw128_desc(aq + kb * 16384 + kk * 32),
-                     sw128_desc(ak + s * C::kK + kb * 16384 + kk * 32), idesc_s, k > 0 ? 1u : 0u);
+                     sw128_desc(ak + sk * C::kK + kb * 16384 + kk * 32), idesc_s, k > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[s]);
-        tc_commit(&k_empty[s]);
+        tc_commit(&k_empty[sk]);
         return true;
       };
+      // S runs two tiles ahead: S of tile j + 2 goes into tile j's buffer as soon as
+      // the softmax has read it, ahead of P V of tile j
       if (ok) ok = issue_s(0);
+      if (ok && nkt > 1) ok = issue_s(1);
       for (int j = 0; ok && j < nkt; ++j) {
-        if (j + 1 < nkt && !issue_s(j + 1)) {
+        if (j + 2 < nkt && !issue_s(j + 2)) {
           ok = false;
           break;
         }
