@@ -17,9 +17,9 @@
 // and swap their partial row max through shared memory; they keep the max the
 // exponentials refer to and the running sum in registers, and rescale O in TMEM
 // only when the row max grows by more than 2^8 (in exp2 units), so most tiles
-// neither rescale nor wait for the previous P V.  Keys arrive in 128-key tiles
-// through a two-stage ring, and the S of the next tile is computed while the
-// softmax works on the current one.  All waits are bounded.
+// neither rescale nor wait for the previous P V.  Keys arrive in 128-key tiles,
+// K through a three-stage ring and V^T through a two-stage one, and S is
+// computed two tiles ahead of the softmax.  All waits are bounded.
 #include <math.h>
 
 #include <algorithm>
