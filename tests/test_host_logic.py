@@ -212,6 +212,36 @@ def test_stack_bench_memory_plan() -> None:
     assert abs((gib[0] - gib[1]) - 2 * (gib[1] - gib[2])) < 0.01
 
 
+def test_prefill_gemm_roofline_bytes() -> None:
+    """bench.py's prefill GEMM floors: the touched experts' weights once, the token rows
+    in and the activations / outputs out.  With ~160 tokens per expert and 16-bit
+    weights (the Qwen3-Next prefill) the weight stream, not the tensor work, bounds the
+    GEMMs; the GLM-4.7 INT8 prefill (~205 tokens per expert, 1-byte weights) is
+    tensor-bound."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(os.path.dirname(__file__)), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    T, k, H, I, SI = 8192, 10, 2048, 512, 512
+    bg, bd = bench._gemm_bytes(T, k, H, I, SI, 512, 2)
+    w_gu, w_d = (512 * 2 * I * H + 2 * SI * H) * 2, (512 * H * I + H * SI) * 2
+    rows = T * k
+    assert bg == w_gu + (rows + T) * H * 2 + (rows * I + T * SI) * 2
+    assert bd == w_d + (rows * I + T * SI) * 2 + rows * H * 2 + T * H * 4
+    fg, fd = bench._gemm_flops(T, k, H, I, SI)
+    tc, hbm = 1666.7e12, 6536e9  # the measured peaks of this pool's B200s
+    assert bg / hbm > fg / tc and bd / hbm > fd / tc      # Qwen3 prefill: weight-bound
+    fg8, _ = bench._gemm_flops(4096, 8, 5120, 1536, 1536)
+    bg8, _ = bench._gemm_bytes(4096, 8, 5120, 1536, 1536, 160, 1)
+    assert fg8 / tc > bg8 / hbm                           # GLM INT8 prefill: tensor-bound
+    # no shared expert: no shared rows or shared weights
+    bg0, bd0 = bench._gemm_bytes(64, 8, 1024, 256, 0, 16, 2)
+    assert bg0 == 16 * 2 * 256 * 1024 * 2 + 64 * 8 * 1024 * 2 + 64 * 8 * 256 * 2
+    assert bd0 == 16 * 1024 * 256 * 2 + 64 * 8 * 256 * 2 + 64 * 8 * 1024 * 2
+
+
 def test_fixed_capacity_needs_a_capacity() -> None:
     from moe_sm100.ep import ExpertParallelMoe
 
