@@ -155,13 +155,28 @@ static WsLayout ws_layout_general(const Plan& p, int rows, int k, int groups, in
   return L;
 }
 
+// 16-bit prefill batches whose experts average at most ~176 tokens take 192-token
+// tiles instead of 256: such a GEMM is bound by streaming the expert weights, and
+// the narrower token tile leaves room for a fifth stage of weights in flight while
+// most experts still fit in one tile (each extra tile re-reads the weights).
+#ifndef MOE_PREFILL_BN_NARROW
+#define MOE_PREFILL_BN_NARROW 1
+#endif
+static int prefill_bn(const Plan& p, int T) {
+  const int bn = pick_bn(T);
+  if (MOE_PREFILL_BN_NARROW && bn == 256 && !p.int8 && p.E > 0 &&
+      static_cast<int64_t>(T) * p.K <= 176LL * p.E)
+    return 192;
+  return bn;
+}
+
 WsLayout ws_layout(const Plan& p, int T) {
   if (p.E == 0)  // dense MLP: normalised rows and the shared-expert GEMMs only
     return ws_layout_general(p, T, 0, 0, T, pick_bn(T), false);
   // INT8 decode batches keep token tiles of at most 64 columns, so that their
   // GEMMs take the TMEM-A path (gemm_ts): an expert sees ~T*K/E tokens, far fewer
   // than T, and the wider tiles' shared-memory A path ran ~25 % slower at T = 128.
-  const int bn = (p.int8 && route_uses_tail(p, T)) ? std::min(pick_bn(T), 64) : pick_bn(T);
+  const int bn = (p.int8 && route_uses_tail(p, T)) ? std::min(pick_bn(T), 64) : prefill_bn(p, T);
   return ws_layout_general(p, T, p.K, p.E, p.SI > 0 ? T : 0, bn, true);
 }
 

@@ -783,6 +783,9 @@ static cudaError_t dispatch_bn(const GemmArgs& a, int bn, int grid, cudaStream_t
     case 32: return run_gemm<32, M, INT8>(a, grid, s);
     case 64: return run_gemm<64, M, INT8>(a, grid, s);
     case 128: return run_gemm<128, M, INT8>(a, grid, s);
+    case 192:  // 16-bit prefill tiles of experts with few tokens (prefill_bn)
+      if constexpr (!INT8) return run_gemm<192, M, INT8>(a, grid, s);
+      return cudaErrorInvalidValue;
     case 256: return run_gemm<256, M, INT8>(a, grid, s);
     default: return cudaErrorInvalidValue;
   }
