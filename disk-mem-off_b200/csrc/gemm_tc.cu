@@ -15,13 +15,16 @@
 // 128-byte swizzle; accumulators live in TMEM (two buffers so the epilogue of
 // one tile overlaps the MMAs of the next).
 //
-// INT8 per-channel weights: TMA brings the int8 tile into a staging buffer,
-// four converter warps widen it to f16 (exact for |q| <= 127) straight into the
-// swizzled MMA operand layout, and the per-row scale is applied to the fp32
-// accumulator in the epilogue (scale is per M row = per TMEM lane).
+// INT8 per-channel weights: a bulk copy brings the int8 tile into a staging
+// buffer and four converter warps widen it to f16 (exact for |q| <= 127), either
+// into the swizzled shared-memory operand layout or -- decode tiles and the
+// 256-token gate/up GEMM (gemm_ts) -- into TMEM, where the MMA reads its A
+// operand; the per-row scale is applied to the fp32 accumulator in the epilogue
+// (scale is per M row = per TMEM lane).
 //
-// Warp roles (192 or 320 threads): warp 0 TMA producer, warp 1 TMEM owner and
-// MMA issuer, warps 2-5 epilogue, warps 6-9 int8 converters.
+// Warp roles: warp 0 TMA producer, warp 1 TMEM owner and MMA issuer, then the
+// epilogue warps (4, or 8 for tiles of 128 columns and more), then the 4 int8
+// converter warps (INT8 weights only).
 #include "common.cuh"
 #include "moe_internal.h"
 
