@@ -316,11 +316,12 @@ MOE_DEV void warp_topk(const float* __restrict__ lrow, const float* __restrict__
 //                       max(1, |best key|) of the K-th key (usually none or
 //                       one); every expert when even the C-th key is that
 //                       close (ties across the whole window).
-//   route_exact_kernel  CTA per token, warp per row: fp32 dot products, with
-//                       loads unrolled across two rows so that many small CTAs
-//                       per SM keep L2 busy; writes the exact logits (plane 0's
-//                       row when every expert is recomputed) and the
-//                       shared-expert gate logit.
+//   route_exact_kernel  CTA per token, warp per row: fp32 dot products against
+//                       the token's normalised row, staged once in shared
+//                       memory, with sixteen loads of the router row in flight
+//                       per lane; writes the exact logits (plane 0's row when
+//                       every expert is recomputed) and the shared-expert gate
+//                       logit.
 //   route_final_kernel  warp per token: softmax over all experts with the
 //                       exact logits substituted, top-k among the recomputed
 //                       rows by exact keys and the lower-id tie rule, weights.
@@ -433,6 +434,7 @@ __global__ void __launch_bounds__(256) route_exact_kernel(
     const float* __restrict__ rms, float* __restrict__ exact, int T, int E, int R, int H,
     int has_gate) {
   pdl_enter();
+  extern __shared__ float4 s_u[];  // [H / 4]: wn * x of this token
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = nrows[t];
@@ -446,62 +448,43 @@ __global__ void __launch_bounds__(256) route_exact_kernel(
     if (all_rows) return r;
     return r < n ? cand[static_cast<size_t>(t) * kCandMax + r] : E;
   };
-  // two rows per pass, four float4 of each in flight per lane
-  for (int r0 = warp * 2; r0 < rows; r0 += 16) {
-    const int r1 = r0 + 1;
-    const bool has1 = r1 < rows;
-    const float4* w0 = reinterpret_cast<const float4*>(wr + static_cast<size_t>(row_of(r0)) * H);
-    const float4* w1 = reinterpret_cast<const float4*>(wr + static_cast<size_t>(row_of(has1 ? r1 : r0)) * H);
-    float a0 = 0.f, a1 = 0.f;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const float4 xv = xr[v], g = __ldg(gr + v);
+    s_u[v] = make_float4(g.x * xv.x, g.y * xv.y, g.z * xv.z, g.w * xv.w);
+  }
+  __syncthreads();
+  // a row per warp, sixteen float4 of it in flight per lane; each lane adds its
+  // columns k = lane (mod 32) in ascending order, then the warp's shuffle tree
+  for (int r = warp; r < rows; r += 8) {
+    const float4* w = reinterpret_cast<const float4*>(wr + static_cast<size_t>(row_of(r)) * H);
+    float a = 0.f;
     int k = lane;
-    for (; k + 96 < nv; k += 128) {
-      float4 xv[4], g[4], p[4], q[4];
+    for (; k + 32 * 15 < nv; k += 32 * 16) {
+      float4 p[16];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        xv[i] = xr[k + 32 * i];
-        g[i] = __ldg(gr + k + 32 * i);
-        p[i] = __ldg(w0 + k + 32 * i);
-        q[i] = __ldg(w1 + k + 32 * i);
-      }
+      for (int i = 0; i < 16; ++i) p[i] = __ldg(w + k + 32 * i);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 u = make_float4(g[i].x * xv[i].x, g[i].y * xv[i].y, g[i].z * xv[i].z, g[i].w * xv[i].w);
-        a0 = fmaf(u.x, p[i].x, a0);
-        a0 = fmaf(u.y, p[i].y, a0);
-        a0 = fmaf(u.z, p[i].z, a0);
-        a0 = fmaf(u.w, p[i].w, a0);
-        a1 = fmaf(u.x, q[i].x, a1);
-        a1 = fmaf(u.y, q[i].y, a1);
-        a1 = fmaf(u.z, q[i].z, a1);
-        a1 = fmaf(u.w, q[i].w, a1);
+      for (int i = 0; i < 16; ++i) {
+        const float4 u = s_u[k + 32 * i];
+        a = fmaf(u.x, p[i].x, a);
+        a = fmaf(u.y, p[i].y, a);
+        a = fmaf(u.z, p[i].z, a);
+        a = fmaf(u.w, p[i].w, a);
       }
     }
     for (; k < nv; k += 32) {
-      const float4 xv = xr[k], g = __ldg(gr + k), p = __ldg(w0 + k), q = __ldg(w1 + k);
-      const float4 u = make_float4(g.x * xv.x, g.y * xv.y, g.z * xv.z, g.w * xv.w);
-      a0 = fmaf(u.x, p.x, a0);
-      a0 = fmaf(u.y, p.y, a0);
-      a0 = fmaf(u.z, p.z, a0);
-      a0 = fmaf(u.w, p.w, a0);
-      a1 = fmaf(u.x, q.x, a1);
-      a1 = fmaf(u.y, q.y, a1);
-      a1 = fmaf(u.z, q.z, a1);
-      a1 = fmaf(u.w, q.w, a1);
+      const float4 u = s_u[k], p = __ldg(w + k);
+      a = fmaf(u.x, p.x, a);
+      a = fmaf(u.y, p.y, a);
+      a = fmaf(u.z, p.z, a);
+      a = fmaf(u.w, p.w, a);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-    }
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
     if (lane == 0) {
-      const float v0 = a0 / rt, v1 = a1 / rt;
-      if (all_rows) {
-        logits[static_cast<size_t>(t) * R + r0] = v0;  // plane 0's row becomes exact
-        if (has1) logits[static_cast<size_t>(t) * R + r1] = v1;
-      } else {
-        exact[static_cast<size_t>(t) * (kCandMax + 1) + r0] = v0;
-        if (has1) exact[static_cast<size_t>(t) * (kCandMax + 1) + r1] = v1;
-      }
+      const float v = a / rt;
+      if (all_rows) logits[static_cast<size_t>(t) * R + r] = v;  // plane 0's row becomes exact
+      else exact[static_cast<size_t>(t) * (kCandMax + 1) + r] = v;
     }
   }
 }
@@ -1598,7 +1581,8 @@ cudaError_t launch_route(const Plan& p, const WsLayout& L, char* ws, const float
       int32_t* nrows = reinterpret_cast<int32_t*>(ws + L.ncand);                                \
       MOE_PDL(route_cand_kernel<V>, dim3(grid), dim3(256), 0, s, logits, router_tc_splits(p, T), bias, cand,     \
                                                 nrows, T, E, R, K, p.cfg.score_func, p.d_err);  \
-      MOE_PDL(route_exact_kernel, dim3(T), dim3(256), 0, s, logits, cand, nrows, x, p.w.norm_w, p.w.router_w,    \
+      MOE_PDL(route_exact_kernel, dim3(T), dim3(256), static_cast<size_t>(p.H) * 4, s, logits, cand, nrows, x, \
+              p.w.norm_w, p.w.router_w,                                                                \
                                            reinterpret_cast<const float*>(ws + L.rms),          \
                                            reinterpret_cast<float*>(ws + L.exact), T, E, R, p.H, \
                                            p.cfg.has_shared_gate);                              \
