@@ -979,6 +979,13 @@ def run_reference(args) -> None:  # noqa: ANN001
     x = _decode_batches(T, 1000, not args.no_sub)[T].cpu().numpy()
     cfg = OracleConfig(hidden=5120, n_experts=160, top_k=8, inter=1536, shared_inter=1536,
                        routed_scaling_factor=2.5, eps=1e-5)
+    # every host thread this process may use: torchrun sets OMP_NUM_THREADS=1 for its
+    # ranks, and rank 0 runs the reference alone (the others have returned)
+    try:
+        from threadpoolctl import threadpool_limits
+        _blas = threadpool_limits(limits=len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
+    except Exception:
+        _blas = None
     lazy = LazyHostTensors(blob, meta)
     moe_block(x, lazy, cfg)  # fetch touched experts to host once (not timed)
     for _ in range(max(0, args.warmup - 1)):
